@@ -1,0 +1,208 @@
+/*
+ * secure_infer.h -- host ABI of libsecure_infer.so, CUDA (sm_100a) edition.
+ *
+ * The reference library is LD_PRELOADed and reached from Python through
+ * ctypes.CDLL(None) (secure_infer/kv_offload/npu_predict.py:158-254,
+ * native_layerwise.py:90-93, transport_codec.py:50,150).  Every name the
+ * reference exports for the authenticated KV transfer path is kept here with
+ * its signature and return convention; the vendor-memcpy interposition of the
+ * reference (aclrtMemcpyAsync, secure_infer.cpp:7729) is replaced by explicit
+ * submission calls (secure_infer_h2d_submit / secure_infer_d2h_submit) that a
+ * connector makes instead of the per-block vendor copy, plus per-layer calls
+ * that move a whole layer in one staged copy and one fused kernel.
+ *
+ * Streams are cudaStream_t passed as void*.  Host pointers are plain host
+ * memory (pinned for the pool); device pointers are CUDA device memory on the
+ * session's device.  Functions returning int use 0 = success, -1 = failure
+ * unless stated otherwise.
+ */
+#ifndef SECURE_INFER_H
+#define SECURE_INFER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SECURE_INFER_GCM_AAD_BYTES 64u        /* secure_infer.h:59 */
+#define SECURE_INFER_DIRECTION_H2D 1u         /* secure_infer.h:61 */
+#define SECURE_INFER_DIRECTION_D2H 2u         /* secure_infer.h:62 */
+
+/* ---------------------------------------------------------------- session */
+
+/* Install the session key (16 bytes, AES-128) and the 4-byte IV salt on
+ * `device`, derive H = E_K(0^128) and the key schedule on the device.  Stands
+ * in for the device key agreement (secure_infer.cpp:449-521), whose outputs
+ * are exactly this key and salt.  Resets tickets and the replay set. */
+int secure_infer_session_init(int device, const uint8_t* key16, const uint8_t* iv_salt4);
+
+/* Tear down the session (waits for in-flight work, frees staging). */
+int secure_infer_session_shutdown(void);
+
+/* ------------------------------------------------------- host KV ranges */
+
+/* secure_infer.cpp:1093. Registers a host range without KV metadata. */
+void secure_infer_register_host_range(const void* base, size_t bytes);
+
+/* secure_infer.cpp:1066-1091. Registers a host KV tensor: records inside it
+ * carry (layer, kind, block = offset / block_bytes) in their AAD. */
+void secure_infer_register_host_range_ex(const void* base, size_t bytes, uint32_t layer_id, uint32_t tensor_kind,
+                                         size_t block_bytes);
+
+/* ------------------------------------------------------ record helpers */
+
+/* Next transfer ticket (secure_infer.cpp:262-272); never 0. */
+uint64_t secure_infer_new_transfer_ticket(void);
+
+/* IV = base[0..3] || BE64(session_nonce + ticket) || BE32(block_offset + 2)
+ * (secure_infer.cpp:274-300, GCM mode: session nonce 0).  -1 on ticket 0. */
+int secure_infer_derive_transfer_iv(const uint8_t* base_iv16, uint64_t ticket, uint64_t block_offset,
+                                    uint8_t* out_iv16);
+
+/* 64-byte AAD "SFAD" v1 (secure_infer.cpp:730-775) for `bytes` at host_ptr,
+ * using the registered range that contains it.  -1 on bad arguments. */
+int secure_infer_build_gcm_aad(const void* host_ptr, size_t bytes, uint8_t direction, uint64_t ticket,
+                               uint64_t transfer_offset, uint8_t* out64);
+
+/* Bytes of one record: C padded to 32 || tag16 || zero16 || AAD64
+ * (secure_infer.cpp:6379-6388). */
+uint64_t secure_infer_record_bytes(uint64_t count);
+
+/* Host AES-128-GCM encrypt of n slices into records (OpenSSL EVP, worker
+ * threads), each with a fresh ticket; tickets_out[i] receives the ticket.
+ * records: n * record_stride bytes of host memory.  (secure_infer.cpp:6508-6537) */
+int secure_infer_h2d_encrypt_records(const void* const* srcs, uint64_t count, uint32_t n, void* records,
+                                     uint64_t record_stride, uint64_t* tickets_out);
+
+/* --------------------------------------------------- KV codec geometry */
+
+typedef struct {
+    uint32_t bits;    /* 0 = KV_CODEC none (raw bf16 bytes), 8 = int8, 4 = int4 */
+    uint32_t kind;    /* 0 = K, 1 = V (grouping axis) */
+    uint32_t heads;   /* KV heads per 128-token block; head_dim is 128 */
+    uint32_t layer;   /* written into the packet header on encode */
+} secure_infer_codec;
+
+/* Packet row bytes for (heads, bits): q || scale || low || int32[4], padded
+ * to 16 (transport_codec.py:35-41).  0 for bits not in {8, 4}. */
+uint64_t secure_infer_codec_packet_bytes(uint32_t heads, uint32_t bits);
+
+/* -------------------------------------------- reload (H2D) of one layer */
+
+/* Device part of a layer reload over records already in device memory.
+ * records: n records at `records + i * record_stride`; tickets[i] gives the
+ * IV; dsts[i] is the destination (raw bytes, or a bf16 paged-cache block when
+ * codec->bits != 0, where the payload is a codec packet).  The AES-CTR
+ * keystream is generated on `producer_stream` into `keystream` (device,
+ * n * record_stride bytes; may overlap nothing else) while the caller's
+ * stream waits only where it needs it; then one fused kernel verifies every
+ * tag, XORs, dequantises and scatters, zeroing the destination of any record
+ * that fails.  status[i] (device) receives 1/0.  Host arrays are captured at
+ * call time. */
+int secure_infer_reload_records(uint32_t layer, const void* records, uint64_t record_stride, uint64_t count,
+                                uint32_t n, const uint64_t* tickets, void* const* dsts, void* keystream,
+                                uint32_t* status, const secure_infer_codec* codec, void* stream,
+                                void* producer_stream);
+
+/* Full reload of one layer/kind: host encrypt (or pre-encrypted records when
+ * `records_are_encrypted` = 1 and srcs[0] points at n records with
+ * record_stride = secure_infer_record_bytes(count) and tickets given), staged
+ * H2D copy, keystream + fused verify/dequant/scatter, status D2H, and a
+ * pending authentication entry for `layer`. */
+int secure_infer_h2d_reload_layer(uint32_t layer, const void* const* srcs, void* const* dsts, uint32_t n,
+                                  uint64_t count, const secure_infer_codec* codec, int records_are_encrypted,
+                                  const uint64_t* tickets, void* stream);
+
+/* Record the completion event of the last reload of `layer` on `stream`
+ * (device-side release of attention; no host wait).  -1 if none. */
+int secure_infer_layer_ready_wait(uint32_t layer, void* stream);
+
+/* ------------------------------------- reference bracket + submission */
+
+/* secure_infer.cpp:5883-5903: submissions between begin/end of the outermost
+ * group are batched and flushed at end as per-layer reloads. */
+int secure_infer_h2d_layer_group_begin(size_t expected_tasks);
+int secure_infer_h2d_layer_group_end(void);
+
+/* Replaces one interposed H2D vendor copy of a registered host range
+ * (secure_infer.cpp:7729-7855): authenticated copy of `count` bytes from
+ * host `src` to device `dst`.  Inside a group it is queued; outside it is
+ * flushed immediately. */
+int secure_infer_h2d_submit(void* dst, size_t dst_capacity, const void* src, size_t count, void* stream);
+
+/* --------------------------------------------------- authentication */
+
+/* secure_infer.cpp:7303-7333: waits for every record of `layer`; a record
+ * that failed is retried once from the trusted host copy with a fresh ticket;
+ * 0 = all authentic, -1 = failure.  0 when nothing is pending. */
+int secure_infer_recovery_wait_layer_authentication(uint32_t layer);
+
+/* secure_infer.cpp:5311: job id attached to subsequent reloads. */
+void secure_infer_recovery_set_job_id(uint64_t job_id);
+
+/* secure_infer.cpp:7338: 1 = all records of the job authentic, 0 = some
+ * failed, -1 = no records for the job. */
+int secure_infer_recovery_wait_job_authentication(uint64_t job_id);
+
+/* ---------------------------------------------- writeback (D2H) path */
+
+/* secure_infer.cpp:2707-2970. Batch / group brackets; submissions inside a
+ * group are encrypted and tagged on the device, copied to the host, verified
+ * by host worker threads and decrypted into their destinations. */
+int secure_infer_d2h_batch_begin(size_t expected_groups);
+int secure_infer_d2h_group_begin(size_t expected_tasks);
+int secure_infer_d2h_submit(void* dst_host, const void* src_device, size_t count, void* stream);
+int secure_infer_d2h_group_end(void);
+int secure_infer_d2h_batch_device_barrier(void);   /* device copies landed */
+int secure_infer_d2h_batch_end(void);              /* host verification done */
+
+/* Writeback of one layer/kind in one call: gather n bf16 blocks (src_blocks,
+ * device), quantise with `codec` (bits 0 = raw), encrypt + tag on device,
+ * copy to the host, verify on the host and store the packet (or raw bytes) to
+ * dsts[i] (host, inside a registered range).  Returns after the device work is
+ * enqueued; completion is joined by secure_infer_d2h_wait(). */
+int secure_infer_d2h_writeback_layer(const void* const* src_blocks, void* const* dsts, uint32_t n,
+                                     const secure_infer_codec* codec, void* stream);
+int secure_infer_d2h_wait(void);
+
+/* ------------------------------------------------- prediction scope */
+
+/* secure_infer.cpp:1102-1146.  Keystreams here are derived from tickets at
+ * submission time, so there are no speculative reservations to drop; these
+ * bump the generation counter reported by the stats. */
+void secure_infer_invalidate_transfer_prefetches(void);
+void secure_infer_retire_transfer_prefetches(void);
+
+/* ------------------------------------------------------------ stats */
+
+/* secure_infer.cpp:821-835 */
+void secure_infer_get_transfer_prefetch_stats(uint64_t* ready, uint64_t* busy_fallback, uint64_t* missing_fallback);
+/* secure_infer.cpp:5038-5053: scheduled, ready, hit, miss, retired, stale, failed */
+void secure_infer_get_gcm_keystream_stats(uint64_t* scheduled, uint64_t* ready, uint64_t* hit, uint64_t* miss,
+                                          uint64_t* retired, uint64_t* stale, uint64_t* failed);
+/* worker.cpp:34-65 */
+void secure_infer_get_npu_keystream_stats(uint64_t* launched, uint64_t* completed, uint64_t* failed);
+void secure_infer_get_npu_keystream_pool_stats(uint64_t* slots, uint64_t* in_use);
+/* secure_infer.cpp:5055 */
+uint64_t secure_infer_count_ready_unconsumed_gcm_tickets(void);
+/* secure_infer.cpp:6089, :6113 (profiling rows are not collected: return 0) */
+int secure_infer_flush_completed_h2d_profile(void);
+int secure_infer_drain_h2d_profile_after_job(void);
+
+/* Records authenticated / rejected / retried since session init. */
+void secure_infer_get_auth_stats(uint64_t* verified, uint64_t* rejected, uint64_t* retried);
+
+/* Host-side fault injection (PIPE_GCM_TAMPER_H2D / _D2H in the reference,
+ * secure_infer.cpp:6187-6251, :2454-2468): flip one byte of the nth record
+ * (1-based, counted from this call) after host encryption (direction 1,
+ * target 0 = ciphertext, 1 = tag) or after the device copy to the host
+ * (direction 2).  nth = 0 disarms. */
+void secure_infer_arm_tamper(uint32_t direction, uint64_t nth, uint32_t target);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SECURE_INFER_H */

@@ -1,0 +1,72 @@
+"""Build the native library in-tree: secure_infer_b200/_build/libsecure_infer.so.
+
+Every CUDA source is compiled for sm_100a only
+(``-gencode arch=compute_100a,code=sm_100a``); host sources go through nvcc's
+host compiler.  The CUDA runtime is linked statically (nvcc's default), so the
+library works next to any torch build; OpenSSL libcrypto is linked for the
+host-side AES-GCM record path.
+
+    python -m secure_infer_b200.build [--force]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = PKG / "_build"
+LIB = BUILD / "libsecure_infer.so"
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden,-O3",
+          f"-I{CSRC}", f"-I{ROOT / 'include'}"]
+SOURCES = ["gcm_kernels.cu", "plugin_abi.cpp", "host_runtime.cpp"]
+HEADERS = ["gcm_device.cuh", "gcm_kernels.cuh", "host_runtime.h"]
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.exists() and d.stat().st_mtime > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    BUILD.mkdir(parents=True, exist_ok=True)
+    headers = [CSRC / h for h in HEADERS] + list((ROOT / "include").glob("*.h"))
+    objects = []
+    for src in SOURCES:
+        path = CSRC / src
+        if not path.exists():
+            continue
+        obj = BUILD / (src + ".o")
+        objects.append(obj)
+        if force or _stale(obj, [path, *headers]):
+            cmd = [NVCC, *ARCH, *COMMON, "-c", str(path), "-o", str(obj)]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+            print(" ".join(cmd), file=sys.stderr)
+            subprocess.run(cmd, check=True)
+    if force or _stale(LIB, objects):
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objects), "-lcrypto", "-lpthread"]
+        print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+    return LIB
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--force", action="store_true")
+    parser.add_argument("--verbose", action="store_true", help="ptxas register/spill report")
+    args = parser.parse_args()
+    print(build(args.force, args.verbose))
+
+
+if __name__ == "__main__":
+    main()

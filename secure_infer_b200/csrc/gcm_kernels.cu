@@ -1,0 +1,749 @@
+// gcm_kernels.cu -- sm_100a kernels of the authenticated KV transfer path.
+//
+//   gcm_schedule_kernel  per-key AES round keys + the 40 GHASH nibble tables
+//   gcm_ctr_kernel       AES-CTR keystream (optionally XORed with a payload)
+//   gcm_segment_kernel   segmented GHASH over AAD || payload || len, fused with
+//                        CTR XOR, the fail-closed gate, and (codec records) the
+//                        int8/int4 -> bf16 dequantisation + block-table scatter
+//   kv_encode_kernel     writeback quantisation of bf16 KV blocks into packets
+//   auth_gate_kernel     zero a buffer whose status is not 1
+//
+// Semantics follow the reference AICPU kernels
+// (secure_infer/native/kernels/aicpu/ghash.aicpu): counter blocks :133-147,
+// decrypt_verify :594-651, encrypt_tag :656-699, verify_xor :705-773,
+// verify_only :780-827, verify_xor_batch :834-940, xor_only :948-976,
+// ghash :978-1046, auth_gate :1051-1068; and the reference codec
+// (secure_infer/kv_offload/transport_codec.py:22-42, optimized_decode.py:5-27).
+#include "gcm_device.cuh"
+#include "gcm_kernels.cuh"
+
+#include <cuda_bf16.h>
+
+#include <mutex>
+
+namespace sib {
+
+// ----------------------------------------------------------------------------
+// Warp helpers
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint4 shfl_xor4(uint4 v, int m)
+{
+    return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m),
+                      __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
+}
+
+__device__ __forceinline__ uint4 warp_xor_reduce(uint4 v)
+{
+#pragma unroll
+    for (int m = 16; m; m >>= 1) v = xor4(v, shfl_xor4(v, m));
+    return v;
+}
+
+// z * M with the 32 lanes of a warp each doing one nibble lookup; z must be
+// warp-uniform.  tab is an unreplicated table (shared or global).
+template <bool kGlobal>
+__device__ __forceinline__ uint4 gf_mul_warp(uint4 z, const uint4* tab, int lane)
+{
+    const uint4* p = tab + lane * 16 + nibble_le(z, lane);
+    return warp_xor_reduce(kGlobal ? __ldg(p) : *p);
+}
+
+__device__ __forceinline__ uint4 len_block_le(uint32_t aad_bytes, uint64_t count)
+{
+    const uint64_t a = static_cast<uint64_t>(aad_bytes) * 8u, c = count * 8u;
+    return make_uint4(bswap32(static_cast<uint32_t>(a >> 32)), bswap32(static_cast<uint32_t>(a)),
+                      bswap32(static_cast<uint32_t>(c >> 32)), bswap32(static_cast<uint32_t>(c)));
+}
+
+__device__ __forceinline__ uint4 j0_block_le(const uint32_t iv[4])
+{
+    return make_uint4(bswap32(iv[0]), bswap32(iv[1]), bswap32(iv[2]), bswap32(1u));
+}
+
+__device__ __forceinline__ uint4 mask_bytes(uint4 v, uint64_t avail)
+{
+    if (avail >= 16) return v;
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int i = 0; i < 4; ++i) {
+        const int64_t keep = static_cast<int64_t>(avail) - 4 * i;
+        const uint32_t m = keep >= 4 ? 0xffffffffu : keep <= 0 ? 0u : ((1u << (8 * keep)) - 1u);
+        w[i] &= m;
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ void store_block(uint8_t* p, uint4 v, uint64_t avail, bool aligned)
+{
+    if (aligned && avail >= 16) *reinterpret_cast<uint4*>(p) = v;
+    else store_partial16(p, v, avail);
+}
+
+__device__ __forceinline__ bool equal4(uint4 a, uint4 b) { return is_zero4(xor4(a, b)); }
+
+// ----------------------------------------------------------------------------
+// Key schedule: one CTA of 8 warps.  Reuses the previous build when the key
+// (and H) bytes are unchanged, so per-call plugin launches stay cheap.
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) gcm_schedule_kernel(const uint8_t* key, const uint8_t* h,
+                                                           GcmSchedule* S, int need_tables)
+{
+    __shared__ uint4 tab_s[32 * 16];
+    __shared__ uint4 pow_le[kGhashTables];
+    __shared__ int s_skip;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    if (tid == 0) {
+        bool same = S->valid == 1u;
+        if (key) {
+            same = same && S->reserved[1] == 1u;
+            for (int i = 0; i < 16; ++i) same = same && S->key_copy[i] == key[i];
+        }
+        if (need_tables) {
+            same = same && S->reserved[0] == 1u && S->h_from_key == (h == nullptr ? 1u : 0u);
+            if (h) for (int i = 0; i < 16; ++i) same = same && S->h_copy[i] == h[i];
+        }
+        s_skip = same ? 1 : 0;
+    }
+    __syncthreads();
+    if (s_skip) return;
+
+    if (tid == 0) {
+        uint32_t rk[44] = {};
+        if (key) {
+            aes128_expand_le(key, rk);
+            for (int i = 0; i < 16; ++i) S->key_copy[i] = key[i];
+        }
+        S->reserved[1] = key ? 1u : 0u;   // round keys valid
+        for (int i = 0; i < 44; ++i) S->rk[i] = rk[i];
+        uint4 hv = zero4();
+        if (h) {
+            hv = load_partial16(h, 16);
+            for (int i = 0; i < 16; ++i) S->h_copy[i] = h[i];
+        } else {
+            hv = aes128_encrypt_global(zero4(), rk);   // H = E_K(0^128)
+        }
+        S->h_le = hv;
+        S->h_from_key = h == nullptr ? 1u : 0u;
+        S->reserved[0] = 0u;
+        pow_le[0] = hv;
+    }
+    __syncthreads();
+    if (!need_tables) {
+        if (tid == 0) { __threadfence(); S->valid = 1u; }
+        return;
+    }
+    if (warp == 0) {
+        // H^2..H^32 by repeated multiplication with H's table.
+        build_nibble_table_warp(bswap4(pow_le[0]), tab_s, lane);
+        __syncwarp();
+        uint4 cur = pow_le[0];
+        for (int e = 2; e <= 32; ++e) {
+            cur = gf_mul_warp<false>(cur, tab_s, lane);
+            if (lane == 0) pow_le[tab_pow_small(e)] = cur;
+        }
+        __syncwarp();
+        // H^64..H^256 with H^32's table.
+        build_nibble_table_warp(bswap4(cur), tab_s, lane);
+        __syncwarp();
+        for (int k = 2; k <= 8; ++k) {
+            cur = gf_mul_warp<false>(cur, tab_s, lane);
+            if (lane == 0) pow_le[tab_pow_32k(k)] = cur;
+        }
+        // H^4096 = (H^256)^16 by four squarings.
+        for (int i = 0; i < 4; ++i) {
+            __syncwarp();
+            build_nibble_table_warp(bswap4(cur), tab_s, lane);
+            __syncwarp();
+            cur = gf_mul_warp<false>(cur, tab_s, lane);
+        }
+        if (lane == 0) pow_le[kTabSeg] = cur;
+    }
+    __syncthreads();
+    for (int t = warp; t < kGhashTables; t += 8) build_nibble_table_warp(bswap4(pow_le[t]), S->tab[t], lane);
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        S->reserved[0] = 1u;
+        S->valid = 1u;
+    }
+}
+
+// ----------------------------------------------------------------------------
+// AES-CTR keystream / payload XOR.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void fill_aes_smem(uint32_t* te, uint32_t* rk, const GcmSchedule* S)
+{
+    uint4* te4 = reinterpret_cast<uint4*>(te);
+    for (uint32_t i = threadIdx.x; i < 2048; i += blockDim.x) {
+        const uint32_t t = kAesDev.te0[i >> 3];
+        te4[i] = make_uint4(t, t, t, t);
+    }
+    if (threadIdx.x < 44) rk[threadIdx.x] = S->rk[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(256) gcm_ctr_kernel(const __grid_constant__ CtrLaunch L, uint64_t uniform_blocks)
+{
+    __shared__ __align__(16) uint32_t te[256 * 32];
+    __shared__ uint32_t rk[44];
+    fill_aes_smem(te, rk, L.sched);
+    __syncthreads();
+    const CtrJob* jobs = L.jobs ? L.jobs : L.inl;
+    const SmemAes aes{te, rk, threadIdx.x & 31u};
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t gb = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; gb < L.total_blocks;
+         gb += stride) {
+        uint32_t j;
+        if (uniform_blocks) {
+            j = static_cast<uint32_t>(gb / uniform_blocks);
+        } else {
+            uint32_t lo = 0, hi = L.njobs - 1;
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi + 1) >> 1;
+                if (jobs[mid].block_first <= gb) lo = mid; else hi = mid - 1;
+            }
+            j = lo;
+        }
+        const CtrJob& J = jobs[j];
+        const uint64_t c = gb - J.block_first;
+        const uint64_t off = c * 16u;
+        const uint64_t avail = J.bytes - off;
+        uint4 ks = aes.encrypt(ctr_block_le(J.iv, c));
+        const bool aligned = !L.unaligned;
+        if (J.in) ks = xor4(ks, (aligned && avail >= 16) ? ldg16(J.in + off) : load_partial16(J.in + off, avail));
+        store_block(J.out + off, ks, avail, aligned);
+    }
+}
+
+// ----------------------------------------------------------------------------
+// Segmented GCM kernel.
+// ----------------------------------------------------------------------------
+// Work item = (record, segment).  The block sequence X = AAD || payload || len
+// (m blocks) is cut into segments aligned to its END: the last nseg-1 segments
+// hold kSegBlocks blocks, the first holds the remaining len0 blocks.  Thread t
+// of the CTA takes blocks base + t + 256 j (coalesced) and runs Horner with
+// H^256; the 256 partials are scaled to S_seg = sum_t Y_t H^(256-t) (see the
+// schedule comment).  Leading zero blocks (base < segment start) leave a
+// zero-started GHASH unchanged.  The last CTA of a record to finish joins the
+// segment partials with H^kSegBlocks, derives E_K(J0), checks/emits the tag
+// and, on authentication failure, zeroes everything the record wrote
+// ("write then gate": nothing is released before the stream reaches the
+// layer event recorded after this kernel).
+constexpr int kBatch = 8;
+constexpr size_t kGhashSmem = 4096 * sizeof(uint4);          // H^256 table, 8 replicas
+constexpr size_t kAesSmem = 256 * 32 * sizeof(uint32_t) + 256; // T-table replicas + round keys
+constexpr uint32_t kMaxCodecParamBytes = 32768;               // staged scale+low
+
+template <int N>
+__device__ __forceinline__ void dequant_store(const float (&q)[N], uint32_t e0, const CodecParams& cp,
+                                              const float* scale, const float* low, uint8_t* out)
+{
+    float v[N];
+    if (cp.kind == 0) {
+        const uint32_t hd = cp.heads * 128u;
+        const uint32_t sidx0 = (e0 / (64u * hd)) * hd + (e0 % hd);
+#pragma unroll
+        for (int k = 0; k < N; k += 4) {
+            const float4 s4 = *reinterpret_cast<const float4*>(scale + sidx0 + k);
+            const float4 l4 = *reinterpret_cast<const float4*>(low + sidx0 + k);
+            v[k + 0] = __fadd_rn(__fmul_rn(q[k + 0], s4.x), l4.x);
+            v[k + 1] = __fadd_rn(__fmul_rn(q[k + 1], s4.y), l4.y);
+            v[k + 2] = __fadd_rn(__fmul_rn(q[k + 2], s4.z), l4.z);
+            v[k + 3] = __fadd_rn(__fmul_rn(q[k + 3], s4.w), l4.w);
+        }
+    } else {
+        const uint32_t sidx = e0 / 64u;
+        const float s = scale[sidx], l = low[sidx];
+#pragma unroll
+        for (int k = 0; k < N; ++k) v[k] = __fadd_rn(__fmul_rn(q[k], s), l);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + 2u * static_cast<size_t>(e0));
+#pragma unroll
+    for (int k = 0; k < N; k += 8) {
+        uint4 o;
+        __nv_bfloat162 b;
+        b = __floats2bfloat162_rn(v[k + 0], v[k + 1]); o.x = *reinterpret_cast<uint32_t*>(&b);
+        b = __floats2bfloat162_rn(v[k + 2], v[k + 3]); o.y = *reinterpret_cast<uint32_t*>(&b);
+        b = __floats2bfloat162_rn(v[k + 4], v[k + 5]); o.z = *reinterpret_cast<uint32_t*>(&b);
+        b = __floats2bfloat162_rn(v[k + 6], v[k + 7]); o.w = *reinterpret_cast<uint32_t*>(&b);
+        dst[k / 8] = o;
+    }
+}
+
+__device__ __forceinline__ void dequant_block(uint4 p, uint64_t c, const CodecParams& cp, const float* scale,
+                                              const float* low, uint8_t* out)
+{
+    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+    if (cp.bits == 8) {
+        float q[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) q[k] = static_cast<float>((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
+        dequant_store<16>(q, static_cast<uint32_t>(c * 16u), cp, scale, low, out);
+    } else {
+        float q[32];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const uint32_t byte = (w[k >> 2] >> (8 * (k & 3))) & 0xffu;
+            q[2 * k] = static_cast<float>(byte & 0xfu);
+            q[2 * k + 1] = static_cast<float>(byte >> 4);
+        }
+        dequant_store<32>(q, static_cast<uint32_t>(c * 32u), cp, scale, low, out);
+    }
+}
+
+template <bool kInlineAes, bool kCodec>
+__global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_constant__ SegmentLaunch L)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* gtab = reinterpret_cast<uint4*>(smem);
+    uint32_t* aes_te = reinterpret_cast<uint32_t*>(smem + kGhashSmem);
+    uint32_t* aes_rk = aes_te + 256 * 32;
+    float* codec_sl = reinterpret_cast<float*>(smem + kGhashSmem + (kInlineAes ? kAesSmem : 0));
+    __shared__ uint4 red[kThreads];
+    __shared__ uint32_t s_last, s_ok;
+
+    const GcmSchedule* __restrict__ S = L.sched;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, rep = lane & 7u;
+    for (uint32_t i = tid; i < 4096; i += kThreads) gtab[i] = __ldg(&S->tab[kTabStride][i >> 3]);
+    if constexpr (kInlineAes) fill_aes_smem(aes_te, aes_rk, S);
+    __syncthreads();
+    const GcmRecord* recs = L.recs ? L.recs : L.inl;
+    const SmemAes aes{aes_te, aes_rk, lane};
+    const CodecParams cp = L.codec;
+
+    for (uint32_t w = blockIdx.x; w < L.total_segs; w += gridDim.x) {
+        uint32_t lo = 0, hi = L.nrec - 1;
+        while (lo < hi) {
+            const uint32_t mid = (lo + hi + 1) >> 1;
+            if (recs[mid].seg_first <= w) lo = mid; else hi = mid - 1;
+        }
+        const uint32_t r = lo;
+        const GcmRecord& R = recs[r];
+        const uint32_t op = R.op, flags = R.flags, nseg = R.nseg;
+        const uint64_t count = R.count;
+        const uint32_t aad_bytes = R.aad_bytes;
+        const uint8_t* in = R.in;
+        const uint8_t* ksp = R.ks;
+        uint8_t* out = R.out;
+        const bool aligned = (flags & kRecUnaligned) == 0;
+
+        const int64_t a_blk = (aad_bytes + 15) >> 4;
+        const int64_t n_blk = static_cast<int64_t>((count + 15) >> 4);
+        const int64_t m = a_blk + n_blk + 1;
+        const uint32_t k = w - R.seg_first;
+        const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * kSegBlocks;
+        const int64_t seg_end = len0 + static_cast<int64_t>(k) * kSegBlocks;
+        const int64_t seg_len = k == 0 ? len0 : kSegBlocks;
+        const int J = static_cast<int>((seg_len + kThreads - 1) / kThreads);
+        const int64_t base = seg_end - static_cast<int64_t>(J) * kThreads;
+
+        if constexpr (kCodec) {
+            // Stage the decrypted scale/low arrays when this segment holds
+            // quantised bytes (they sit after q in the packet).
+            const int64_t c_lo = (base > a_blk ? base : a_blk) - a_blk;
+            const bool needs = op == kOpDecrypt && c_lo < static_cast<int64_t>(cp.qb >> 4) && seg_end > a_blk;
+            __syncthreads();
+            if (needs) {
+                const uint32_t n16 = (2u * cp.sb) >> 4;
+                for (uint32_t i = tid; i < n16; i += kThreads) {
+                    const uint64_t off = cp.qb + 16ull * i;
+                    reinterpret_cast<uint4*>(codec_sl)[i] = xor4(ldg16(in + off), ldg16(ksp + off));
+                }
+            }
+            __syncthreads();
+        }
+
+        uint4 Y = zero4();
+        for (int jb = 0; jb < J; jb += kBatch) {
+            uint4 xin[kBatch], kin[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                xin[u] = zero4();
+                kin[u] = zero4();
+                const int j = jb + u;
+                const int64_t i = base + tid + static_cast<int64_t>(j) * kThreads;
+                if (j >= J || i < 0) continue;
+                if (i < a_blk) {
+                    xin[u] = load_partial16(R.aad + 16 * i, aad_bytes - 16 * i);
+                } else if (i < a_blk + n_blk) {
+                    const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
+                    const uint64_t avail = count - off;
+                    if (aligned && avail >= 16) {
+                        xin[u] = ldg16(in + off);
+                        if (ksp) kin[u] = ldg16(ksp + off);
+                    } else {
+                        xin[u] = load_partial16(in + off, avail);
+                        if (ksp) kin[u] = load_partial16(ksp + off, avail);
+                    }
+                } else {
+                    xin[u] = len_block_le(aad_bytes, count);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                const int j = jb + u;
+                if (j >= J) break;
+                const int64_t i = base + tid + static_cast<int64_t>(j) * kThreads;
+                uint4 X = xin[u];
+                if (i >= a_blk && i < a_blk + n_blk) {
+                    const uint64_t c = static_cast<uint64_t>(i - a_blk);
+                    const uint64_t off = c * 16u;
+                    const uint64_t avail = count - off;
+                    uint4 ks = kin[u];
+                    if constexpr (kInlineAes) {
+                        if (!ksp) ks = aes.encrypt(ctr_block_le(R.iv, c));
+                    }
+                    if (op == kOpDecrypt) {
+                        const uint4 P = xor4(X, ks);
+                        if constexpr (kCodec) {
+                            if (off < cp.qb) dequant_block(P, c, cp, codec_sl, codec_sl + (cp.sb >> 2), out);
+                        } else {
+                            store_block(out + off, P, avail, aligned);
+                        }
+                    } else if (op == kOpEncrypt) {
+                        const uint4 C = mask_bytes(xor4(X, ks), avail);
+                        store_block(out + off, C, avail, aligned);
+                        X = C;
+                    } else if (op == kOpXorOnly || (op == kOpGhash && (flags & kGhashXorOnSuccess))) {
+                        store_block(out + off, xor4(X, ks), avail, aligned);
+                    }
+                }
+                if (op != kOpXorOnly) Y = j == 0 ? X : xor4(gf_mul_table<8, false>(Y, gtab, rep), X);
+            }
+        }
+
+        if (op != kOpXorOnly) {
+            if (warp != 7) Y = gf_mul_table<1, true>(Y, S->tab[tab_pow_32k(7 - warp)], 0);
+            red[tid] = Y;
+            __syncthreads();
+            if (warp == 0) {
+                uint4 U = red[lane];
+#pragma unroll
+                for (int ww = 1; ww < 8; ++ww) U = xor4(U, red[ww * 32 + lane]);
+                U = gf_mul_table<1, true>(U, S->tab[tab_pow_small(32 - lane)], 0);
+                U = warp_xor_reduce(U);
+                if (lane == 0) L.partials[w] = U;
+            }
+        }
+        // Publish this segment: every thread's output stores, then the partial.
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const uint32_t prev = atomicAdd(&L.counters[r], 1u);
+            s_last = prev == nseg - 1 ? 1u : 0u;
+        }
+        __syncthreads();
+        if (!s_last) continue;
+
+        __threadfence();
+        if (warp == 0) {
+            uint4 acc = zero4();
+            if (op != kOpXorOnly) {
+                for (uint32_t kk = 0; kk < nseg; ++kk) {
+                    const uint4 p = __ldcg(&L.partials[R.seg_first + kk]);
+                    acc = kk == 0 ? p : xor4(gf_mul_warp<true>(acc, S->tab[kTabSeg], lane), p);
+                }
+            }
+            if (lane == 0) {
+                uint32_t ok = 1u;
+                if (op == kOpDecrypt || op == kOpVerify || op == kOpEncrypt) {
+                    const uint4 mask = aes128_encrypt_global(j0_block_le(R.iv), S->rk);
+                    const uint4 tag = xor4(acc, mask);
+                    if (op == kOpEncrypt) {
+                        store_partial16(R.tag_out, tag, 16);
+                    } else {
+                        ok = equal4(tag, load_partial16(R.tag_in, 16)) ? 1u : 0u;
+                        *R.status = ok;
+                    }
+                } else if (op == kOpGhash) {
+                    uint4 tag = acc;
+                    if (flags & kGhashFinalize) tag = xor4(tag, load_partial16(R.tag_mask, 16));
+                    store_partial16(R.tag_out, tag, 16);
+                    if (flags & kGhashVerify) ok = equal4(tag, load_partial16(R.tag_in, 16)) ? 1u : 0u;
+                    if (R.status) *R.status = ok;
+                } else if (R.status) {
+                    *R.status = 1u;   // kOpXorOnly: profiling control, no authentication
+                }
+                s_ok = ok;
+                L.counters[r] = 0u;
+            }
+        }
+        __syncthreads();
+        const bool gated = op == kOpDecrypt || (op == kOpGhash && (flags & kGhashXorOnSuccess));
+        if (!s_ok && gated && out) {
+            const uint64_t bytes = kCodec ? 2ull * 128u * cp.heads * 128u : count;
+            for (uint64_t off = static_cast<uint64_t>(tid) * 16u; off < bytes; off += 16u * kThreads)
+                store_block(out + off, zero4(), bytes - off, aligned);
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------
+// Writeback quantisation (transport_codec.py:22-42), one thread per group.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+__device__ __forceinline__ float quantise(float x, float low, float scale, float levels)
+{
+    return fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(x, low), scale)), 0.0f), levels);
+}
+
+__global__ void __launch_bounds__(256) kv_encode_kernel(const __grid_constant__ EncodeLaunch L)
+{
+    const CodecParams cp = L.codec;
+    const uint32_t hd = cp.heads * 128u, elements = 128u * hd, groups = elements / 64u;
+    const uint32_t rec = blockIdx.y;
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(L.cache + static_cast<size_t>(L.block_ids[rec]) *
+                                                                           elements * 2u);
+    uint8_t* pkt = L.packets + static_cast<size_t>(rec) * L.width;
+    float* scale = reinterpret_cast<float*>(pkt + cp.qb);
+    float* lowp = reinterpret_cast<float*>(pkt + cp.qb + cp.sb);
+    const float levels = static_cast<float>((1u << cp.bits) - 1u);
+    const uint32_t lane = threadIdx.x & 31u;
+
+    for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += gridDim.x * blockDim.x) {
+        if (cp.kind == 0) {
+            // 64 tokens of channel ch in token group tg; element e = (64 tg + t) hd + ch.
+            const uint32_t tg = g / hd, ch = g % hd;
+            const uint16_t* col = src + static_cast<size_t>(tg) * 64u * hd + ch;
+            float lo = __int_as_float(0x7f800000), hi = -lo;
+            for (int t = 0; t < 64; ++t) {
+                const float x = bf16_bits_to_f32(__ldg(col + static_cast<size_t>(t) * hd));
+                lo = fminf(lo, x);
+                hi = fmaxf(hi, x);
+            }
+            const float sc = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), levels), 1e-12f);
+            scale[g] = sc;
+            lowp[g] = lo;
+            uint8_t* qcol = pkt;
+            for (int t = 0; t < 64; ++t) {
+                const size_t e = (static_cast<size_t>(tg) * 64u + t) * hd + ch;
+                const uint32_t q = static_cast<uint32_t>(
+                    quantise(bf16_bits_to_f32(__ldg(col + static_cast<size_t>(t) * hd)), lo, sc, levels));
+                if (cp.bits == 8) {
+                    qcol[e] = static_cast<uint8_t>(q);
+                } else {
+                    // Elements e (even ch) and e + 1 share a byte: low nibble = even.
+                    const uint32_t partner = __shfl_down_sync(0xffffffffu, q, 1);
+                    if ((lane & 1u) == 0) qcol[e >> 1] = static_cast<uint8_t>(q | (partner << 4));
+                }
+            }
+        } else {
+            // 64 consecutive dims of one (token, head): element e = 64 g + i.
+            const uint4* p4 = reinterpret_cast<const uint4*>(src + static_cast<size_t>(g) * 64u);
+            float x[64];
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+                const uint4 d = __ldg(p4 + v);
+                const uint32_t ws[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+                for (int h2 = 0; h2 < 4; ++h2) {
+                    x[v * 8 + 2 * h2] = bf16_bits_to_f32(ws[h2] & 0xffffu);
+                    x[v * 8 + 2 * h2 + 1] = bf16_bits_to_f32(ws[h2] >> 16);
+                }
+            }
+            float lo = x[0], hi = x[0];
+#pragma unroll
+            for (int i = 1; i < 64; ++i) { lo = fminf(lo, x[i]); hi = fmaxf(hi, x[i]); }
+            const float sc = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), levels), 1e-12f);
+            scale[g] = sc;
+            lowp[g] = lo;
+            if (cp.bits == 8) {
+                uint4* dst = reinterpret_cast<uint4*>(pkt + static_cast<size_t>(g) * 64u);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    uint32_t wv[4];
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        uint32_t word = 0;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            word |= static_cast<uint32_t>(quantise(x[v * 16 + b * 4 + i], lo, sc, levels)) << (8 * i);
+                        wv[b] = word;
+                    }
+                    dst[v] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                }
+            } else {
+                uint4* dst = reinterpret_cast<uint4*>(pkt + static_cast<size_t>(g) * 32u);
+#pragma unroll
+                for (int v = 0; v < 2; ++v) {
+                    uint32_t wv[4];
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        uint32_t word = 0;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int e = v * 32 + b * 8 + 2 * i;
+                            const uint32_t byte = static_cast<uint32_t>(quantise(x[e], lo, sc, levels)) |
+                                                  (static_cast<uint32_t>(quantise(x[e + 1], lo, sc, levels)) << 4);
+                            word |= byte << (8 * i);
+                        }
+                        wv[b] = word;
+                    }
+                    dst[v] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                }
+            }
+        }
+    }
+    if (blockIdx.x == 0) {
+        // int32 header {1, layer, kind, bits} then zero padding to width.
+        const uint32_t hdr = cp.qb + 2u * cp.sb;
+        for (uint32_t i = threadIdx.x; i < L.width - hdr; i += blockDim.x) {
+            uint8_t v = 0;
+            if (i < 16) {
+                const uint32_t word = i < 4 ? 1u : i < 8 ? L.layer : i < 12 ? cp.kind : cp.bits;
+                v = static_cast<uint8_t>(word >> (8 * (i & 3)));
+            }
+            pkt[hdr + i] = v;
+        }
+    }
+}
+
+__global__ void auth_gate_kernel(uint8_t* data, const uint32_t* status, uint64_t bytes)
+{
+    if (__ldg(status) == 1u) return;
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < bytes;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        data[i] = 0;
+}
+
+// ----------------------------------------------------------------------------
+// Host launchers
+// ----------------------------------------------------------------------------
+namespace {
+
+struct DeviceInfo {
+    int sms = 0;
+    int seg_blocks_per_sm[4] = {0, 0, 0, 0};
+    bool attr_set[4] = {false, false, false, false};
+};
+
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+DeviceInfo& device_info(int dev)
+{
+    DeviceInfo& d = g_dev[dev & 63];
+    if (d.sms == 0) cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    return d;
+}
+
+template <bool A, bool C>
+int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cudaStream_t stream)
+{
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int per_sm = 0, sms = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        DeviceInfo& d = device_info(dev);
+        if (!d.attr_set[variant]) {
+            const size_t max_smem = kGhashSmem + kAesSmem + kMaxCodecParamBytes;
+            cudaError_t e = cudaFuncSetAttribute(gcm_segment_kernel<A, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(max_smem));
+            if (e != cudaSuccess) return e;
+            d.attr_set[variant] = true;
+        }
+        sms = d.sms;
+        per_sm = d.seg_blocks_per_sm[variant];
+    }
+    if (per_sm == 0) {
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gcm_segment_kernel<A, C>, kThreads, smem);
+        if (per_sm < 1) per_sm = 1;
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        device_info(dev).seg_blocks_per_sm[variant] = per_sm;
+    }
+    const uint32_t grid = static_cast<uint32_t>(
+        args.total_segs < static_cast<uint32_t>(sms * per_sm) ? args.total_segs : sms * per_sm);
+    gcm_segment_kernel<A, C><<<grid, kThreads, smem, stream>>>(args);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t schedule_bytes() { return sizeof(GcmSchedule); }
+
+uint32_t segments_for(uint64_t count, uint32_t aad_bytes)
+{
+    const uint64_t m = (aad_bytes + 15u) / 16u + (count + 15u) / 16u + 1u;
+    const uint64_t n = m / kSegBlocks;
+    return static_cast<uint32_t>(n ? n : 1u);
+}
+
+int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream)
+{
+    gcm_schedule_kernel<<<1, 256, 0, stream>>>(static_cast<const uint8_t*>(key), static_cast<const uint8_t*>(h),
+                                               sched, need_tables ? 1 : 0);
+    return cudaGetLastError();
+}
+
+int launch_ctr(const CtrLaunch& args, cudaStream_t stream)
+{
+    if (args.total_blocks == 0) return cudaSuccess;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms;
+    {
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        sms = device_info(dev).sms;
+    }
+    const CtrJob* jobs = args.jobs ? nullptr : args.inl;
+    uint64_t uniform = 0;
+    if (jobs) {
+        const uint64_t b0 = (jobs[0].bytes + 15) / 16;
+        bool same = true;
+        for (uint32_t i = 0; i < args.njobs; ++i) same = same && (jobs[i].bytes + 15) / 16 == b0 && jobs[i].block_first == i * b0;
+        uniform = same ? b0 : 0;
+    }
+    const uint64_t want = (args.total_blocks + 255) / 256;
+    const uint64_t cap = static_cast<uint64_t>(sms) * 6u;
+    const uint32_t grid = static_cast<uint32_t>(want < cap ? want : cap);
+    gcm_ctr_kernel<<<grid, 256, 0, stream>>>(args, uniform);
+    return cudaGetLastError();
+}
+
+int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStream_t stream)
+{
+    if (args.total_blocks == 0) return cudaSuccess;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms;
+    {
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        sms = device_info(dev).sms;
+    }
+    const uint64_t want = (args.total_blocks + 255) / 256;
+    const uint64_t cap = static_cast<uint64_t>(sms) * 6u;
+    const uint32_t grid = static_cast<uint32_t>(want < cap ? want : cap);
+    gcm_ctr_kernel<<<grid, 256, 0, stream>>>(args, uniform_blocks);
+    return cudaGetLastError();
+}
+
+int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream)
+{
+    if (args.total_segs == 0) return cudaSuccess;
+    const bool codec = args.codec.bits != 0;
+    if (codec && (inline_aes || 2u * args.codec.sb > kMaxCodecParamBytes)) return cudaErrorInvalidValue;
+    const size_t smem = kGhashSmem + (inline_aes ? kAesSmem : 0) + (codec ? 2u * args.codec.sb : 0);
+    if (inline_aes) return segment_launch_impl<true, false>(args, smem, 1, stream);
+    if (codec) return segment_launch_impl<false, true>(args, smem, 2, stream);
+    return segment_launch_impl<false, false>(args, smem, 0, stream);
+}
+
+int launch_encode(const EncodeLaunch& args, cudaStream_t stream)
+{
+    if (args.n == 0) return cudaSuccess;
+    const uint32_t groups = 128u * args.codec.heads * 128u / 64u;
+    const dim3 grid((groups + 255) / 256, args.n);
+    kv_encode_kernel<<<grid, 256, 0, stream>>>(args);
+    return cudaGetLastError();
+}
+
+int launch_auth_gate(uint8_t* data, const uint32_t* status, uint64_t bytes, cudaStream_t stream)
+{
+    const uint64_t want = (bytes + 255) / 256;
+    const uint32_t grid = static_cast<uint32_t>(want < 1024 ? (want ? want : 1) : 1024);
+    auth_gate_kernel<<<grid, 256, 0, stream>>>(data, status, bytes);
+    return cudaGetLastError();
+}
+
+}  // namespace sib

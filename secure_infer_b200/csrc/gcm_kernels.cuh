@@ -1,0 +1,112 @@
+// gcm_kernels.cuh -- launch descriptors shared by the CUDA kernels
+// (gcm_kernels.cu) and the host runtime (host_runtime.cpp).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sib {
+
+struct GcmSchedule;  // gcm_device.cuh
+
+// One authenticated record.  Segment work items are assigned in record order;
+// seg_first is the record's first work item (exclusive prefix sum of nseg).
+enum : uint32_t {
+    kOpDecrypt = 1,   // in = C -> out = P (zeroed on failure), status
+    kOpVerify = 2,    // in = C -> status only
+    kOpEncrypt = 3,   // in = P -> out = C, tag_out = GHASH(C) ^ E_K(J0)
+    kOpGhash = 4,     // generic GHASH (flags below), ghash_do semantics
+    kOpXorOnly = 5,   // out = in ^ ks, status = 1, no authentication
+};
+enum : uint32_t {
+    kGhashFinalize = 1u << 0,
+    kGhashVerify = 1u << 1,
+    kGhashXorOnSuccess = 1u << 2,
+    kRecUnaligned = 1u << 8,   // some pointer is not 16-byte aligned
+    kRecCodec = 1u << 9,       // out is a bf16 KV block; payload is a codec packet
+};
+
+struct GcmRecord {
+    const uint8_t* in;
+    const uint8_t* ks;         // keystream for in[0..count), or null (AES inline)
+    const uint8_t* aad;
+    const uint8_t* tag_in;     // expected tag (verify paths)
+    const uint8_t* tag_mask;   // explicit tag mask (kOpGhash + kGhashFinalize)
+    uint8_t* out;
+    uint8_t* tag_out;
+    uint32_t* status;
+    uint64_t count;
+    uint32_t iv[4];            // big-endian packs of the IV bytes; iv[3] = first counter
+    uint32_t aad_bytes;
+    uint32_t op;
+    uint32_t flags;
+    uint32_t seg_first;
+    uint32_t nseg;
+    uint32_t reserved;
+};
+
+// KV codec geometry for kRecCodec records (one layer/kind per launch).
+struct CodecParams {
+    uint32_t bits;    // 8 or 4
+    uint32_t kind;    // 0 = K (64-token groups per channel), 1 = V (64-dim groups)
+    uint32_t heads;   // KV heads in one block; head_dim is 128, tokens 128
+    uint32_t qb;      // quantised bytes
+    uint32_t sb;      // bytes of one fp32 parameter array (scale or low)
+};
+
+constexpr int kInlineRecords = 4;
+
+struct SegmentLaunch {
+    const GcmSchedule* sched;
+    const GcmRecord* recs;              // device array, or null -> inl
+    GcmRecord inl[kInlineRecords];
+    uint32_t nrec;
+    uint32_t total_segs;
+    uint4* partials;                    // [total_segs]
+    uint32_t* counters;                 // [nrec], zero on entry, zero on exit
+    CodecParams codec;
+};
+
+// AES-CTR keystream / CTR XOR jobs.
+struct CtrJob {
+    const uint8_t* in;   // null -> keystream only
+    uint8_t* out;
+    uint64_t bytes;
+    uint32_t iv[4];
+    uint64_t block_first;  // exclusive prefix sum of ceil(bytes/16)
+};
+
+constexpr int kInlineCtrJobs = 32;
+
+struct CtrLaunch {
+    const GcmSchedule* sched;
+    const CtrJob* jobs;                 // device array, or null -> inl
+    CtrJob inl[kInlineCtrJobs];
+    uint32_t njobs;
+    uint32_t unaligned;
+    uint64_t total_blocks;
+};
+
+// KV codec encode (writeback quantisation) of n blocks of one layer/kind.
+struct EncodeLaunch {
+    const uint8_t* cache;          // bf16 paged cache base, blocks of 128 x heads x 128
+    const int64_t* block_ids;      // device [n]: source block of record i
+    uint8_t* packets;              // [n][width]
+    uint32_t n;
+    uint32_t width;
+    uint32_t layer;
+    CodecParams codec;
+};
+
+// Host-side launchers (gcm_kernels.cu).  Return a cudaError_t value.
+// key may be null (GHASH-only requests); h null -> H = E_K(0^128) on device.
+int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream);
+int launch_ctr(const CtrLaunch& args, cudaStream_t stream);
+int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStream_t stream);
+int launch_auth_gate(uint8_t* data, const uint32_t* status, uint64_t bytes, cudaStream_t stream);
+int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream);
+int launch_encode(const EncodeLaunch& args, cudaStream_t stream);
+size_t schedule_bytes();
+uint32_t segments_for(uint64_t count, uint32_t aad_bytes);
+
+}  // namespace sib
