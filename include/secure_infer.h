@@ -95,8 +95,9 @@ uint64_t secure_infer_codec_packet_bytes(uint32_t heads, uint32_t bits);
  * records: n records at `records + i * record_stride`; tickets[i] gives the
  * IV; dsts[i] is the destination (raw bytes, or a bf16 paged-cache block when
  * codec->bits != 0, where the payload is a codec packet).  The AES-CTR
- * keystream is generated on `producer_stream` into `keystream` (device,
- * n * record_stride bytes; may overlap nothing else) while the caller's
+ * keystream is generated on `producer_stream` (null: the session's producer
+ * stream) into `keystream` (device, n * round16(count) bytes; null: AES is
+ * computed inside the fused kernel) while the caller's
  * stream waits only where it needs it; then one fused kernel verifies every
  * tag, XORs, dequantises and scatters, zeroing the destination of any record
  * that fails.  status[i] (device) receives 1/0.  Host arrays are captured at
@@ -105,6 +106,17 @@ int secure_infer_reload_records(uint32_t layer, const void* records, uint64_t re
                                 uint32_t n, const uint64_t* tickets, void* const* dsts, void* keystream,
                                 uint32_t* status, const secure_infer_codec* codec, void* stream,
                                 void* producer_stream);
+
+/* The two halves of secure_infer_reload_records, on one stream:
+ * keystream for n tickets into `keystream` (record i at i * round16(count)),
+ * and the fused verify/XOR/(dequant)/scatter with that keystream ready (null
+ * keystream: AES computed inside the fused kernel; codec records need a
+ * keystream). */
+int secure_infer_keystream_records(const uint64_t* tickets, uint32_t n, uint64_t count, void* keystream,
+                                   void* stream);
+int secure_infer_verify_records(uint32_t layer, const void* records, uint64_t record_stride, uint64_t count,
+                                uint32_t n, const uint64_t* tickets, void* const* dsts, const void* keystream,
+                                uint32_t* status, const secure_infer_codec* codec, void* stream);
 
 /* Full reload of one layer/kind: host encrypt (or pre-encrypted records when
  * `records_are_encrypted` = 1 and srcs[0] points at n records with

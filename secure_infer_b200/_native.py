@@ -38,7 +38,54 @@ PLUGIN_SIGNATURES = {
     "secure_infer_aicpu_gcm_xor_only_do": ([P] * 8 + [U64] + [U32] * 4, I32),
 }
 
-HOST_SIGNATURES: dict[str, tuple[list, object]] = {}
+CHARP = ct.c_char_p
+HOST_SIGNATURES: dict[str, tuple[list, object]] = {
+    "secure_infer_session_init": ([I32, P, P], I32),
+    "secure_infer_session_shutdown": ([], I32),
+    "secure_infer_register_host_range": ([P, SZ], None),
+    "secure_infer_register_host_range_ex": ([P, SZ, U32, U32, SZ], None),
+    "secure_infer_new_transfer_ticket": ([], U64),
+    "secure_infer_derive_transfer_iv": ([P, U64, U64, P], I32),
+    "secure_infer_build_gcm_aad": ([P, SZ, ct.c_uint8, U64, U64, P], I32),
+    "secure_infer_record_bytes": ([U64], U64),
+    "secure_infer_h2d_encrypt_records": ([PP, U64, U32, P, U64, U64P], I32),
+    "secure_infer_codec_packet_bytes": ([U32, U32], U64),
+    "secure_infer_reload_records": ([U32, P, U64, U64, U32, U64P, PP, P, P, P, P, P], I32),
+    "secure_infer_keystream_records": ([U64P, U32, U64, P, P], I32),
+    "secure_infer_verify_records": ([U32, P, U64, U64, U32, U64P, PP, P, P, P, P], I32),
+    "secure_infer_h2d_reload_layer": ([U32, PP, PP, U32, U64, P, I32, U64P, P], I32),
+    "secure_infer_layer_ready_wait": ([U32, P], I32),
+    "secure_infer_h2d_layer_group_begin": ([SZ], I32),
+    "secure_infer_h2d_layer_group_end": ([], I32),
+    "secure_infer_h2d_submit": ([P, SZ, P, SZ, P], I32),
+    "secure_infer_recovery_wait_layer_authentication": ([U32], I32),
+    "secure_infer_recovery_set_job_id": ([U64], None),
+    "secure_infer_recovery_wait_job_authentication": ([U64], I32),
+    "secure_infer_d2h_batch_begin": ([SZ], I32),
+    "secure_infer_d2h_group_begin": ([SZ], I32),
+    "secure_infer_d2h_submit": ([P, P, SZ, P], I32),
+    "secure_infer_d2h_group_end": ([], I32),
+    "secure_infer_d2h_batch_device_barrier": ([], I32),
+    "secure_infer_d2h_batch_end": ([], I32),
+    "secure_infer_d2h_writeback_layer": ([PP, PP, U32, P, P], I32),
+    "secure_infer_d2h_wait": ([], I32),
+    "secure_infer_invalidate_transfer_prefetches": ([], None),
+    "secure_infer_retire_transfer_prefetches": ([], None),
+    "secure_infer_get_transfer_prefetch_stats": ([U64P] * 3, None),
+    "secure_infer_get_gcm_keystream_stats": ([U64P] * 7, None),
+    "secure_infer_get_npu_keystream_stats": ([U64P] * 3, None),
+    "secure_infer_get_npu_keystream_pool_stats": ([U64P] * 2, None),
+    "secure_infer_count_ready_unconsumed_gcm_tickets": ([], U64),
+    "secure_infer_flush_completed_h2d_profile": ([], I32),
+    "secure_infer_drain_h2d_profile_after_job": ([], I32),
+    "secure_infer_get_auth_stats": ([U64P] * 3, None),
+    "secure_infer_arm_tamper": ([U32, U64, U32], None),
+}
+
+
+class Codec(ct.Structure):
+    """secure_infer_codec (include/secure_infer.h)."""
+    _fields_ = [("bits", ct.c_uint32), ("kind", ct.c_uint32), ("heads", ct.c_uint32), ("layer", ct.c_uint32)]
 
 _lib: ct.CDLL | None = None
 

@@ -492,8 +492,7 @@ __global__ void __launch_bounds__(256) kv_encode_kernel(const __grid_constant__ 
     const CodecParams cp = L.codec;
     const uint32_t hd = cp.heads * 128u, elements = 128u * hd, groups = elements / 64u;
     const uint32_t rec = blockIdx.y;
-    const uint16_t* src = reinterpret_cast<const uint16_t*>(L.cache + static_cast<size_t>(L.block_ids[rec]) *
-                                                                           elements * 2u);
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(L.srcs[rec]);
     uint8_t* pkt = L.packets + static_cast<size_t>(rec) * L.width;
     float* scale = reinterpret_cast<float*>(pkt + cp.qb);
     float* lowp = reinterpret_cast<float*>(pkt + cp.qb + cp.sb);

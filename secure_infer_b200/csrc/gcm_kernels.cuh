@@ -89,8 +89,7 @@ struct CtrLaunch {
 
 // KV codec encode (writeback quantisation) of n blocks of one layer/kind.
 struct EncodeLaunch {
-    const uint8_t* cache;          // bf16 paged cache base, blocks of 128 x heads x 128
-    const int64_t* block_ids;      // device [n]: source block of record i
+    const uint8_t* const* srcs;    // device array [n] of bf16 blocks (128 x heads x 128)
     uint8_t* packets;              // [n][width]
     uint32_t n;
     uint32_t width;

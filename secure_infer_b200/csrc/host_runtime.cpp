@@ -1,0 +1,1392 @@
+// host_runtime.cpp -- host side of the authenticated KV transfer path.
+//
+// What the reference does per interposed vendor copy (secure_infer.cpp:
+// 6290-7116 for H2D, :8076-8562 and :2359-2970 for D2H) is done here per
+// layer:
+//
+//   H2D reload of one layer/kind (n records)
+//     host   tickets -> IVs (:274-300) -> AADs (:730-775) -> OpenSSL
+//            AES-128-GCM on worker threads into a pinned staging slot laid
+//            out as n records C[aligned32] || tag || 0^16 || AAD (:6379-6388)
+//     stream one cudaMemcpyAsync of the whole slot
+//     producer stream: AES-CTR keystream for all n IVs (depends only on the
+//            tickets, so it runs while the ciphertext is still on the link)
+//     stream fused kernel: GHASH verify + XOR + (dequant) + scatter into the
+//            paged cache, zeroing failed records; status D2H; layer event
+//   recovery_wait_layer_authentication(layer): joins the layer's statuses and
+//     retries each failed record once from the trusted host copy with a fresh
+//     ticket (:7303-7333).
+//
+//   D2H writeback of one layer/kind (n blocks)
+//     stream (quantise) + CTR encrypt + tag on device into a staging slot,
+//            one D2H copy of the records
+//     host   a completion thread waits for the copy, then worker threads
+//            verify + decrypt every record with OpenSSL into the host pool
+//            (:2470-2547); a failed record is zeroed and reported.
+#include "gcm_kernels.cuh"
+#include "../../include/secure_infer.h"
+
+#include <openssl/evp.h>
+
+#include <algorithm>
+#include <atomic>
+#include <condition_variable>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <deque>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <thread>
+#include <unordered_set>
+#include <vector>
+
+namespace sib {
+namespace host {
+namespace {
+
+constexpr uint64_t kAadBytes = 64;
+
+void store_be32(uint8_t* d, uint32_t v)
+{
+    d[0] = static_cast<uint8_t>(v >> 24); d[1] = static_cast<uint8_t>(v >> 16);
+    d[2] = static_cast<uint8_t>(v >> 8);  d[3] = static_cast<uint8_t>(v);
+}
+
+void store_be64(uint8_t* d, uint64_t v)
+{
+    for (int i = 0; i < 8; ++i) d[i] = static_cast<uint8_t>(v >> (56 - 8 * i));
+}
+
+uint32_t load_be32(const uint8_t* s)
+{
+    return (static_cast<uint32_t>(s[0]) << 24) | (static_cast<uint32_t>(s[1]) << 16) |
+           (static_cast<uint32_t>(s[2]) << 8) | s[3];
+}
+
+uint64_t aligned32(uint64_t count)
+{
+    const uint64_t a = (count + 31u) & ~static_cast<uint64_t>(31u);
+    return a ? a : 32u;
+}
+
+uint64_t record_bytes(uint64_t count) { return aligned32(count) + 32u + kAadBytes; }
+
+uint64_t round16(uint64_t v) { return (v + 15u) & ~static_cast<uint64_t>(15u); }
+
+// ---------------------------------------------------------------- host ranges
+struct HostRange {
+    uintptr_t begin, end;
+    uint32_t layer, kind;
+    size_t block_bytes;
+};
+
+std::mutex g_ranges_mu;
+std::vector<HostRange> g_ranges;
+
+bool lookup_range(const void* p, size_t bytes, HostRange* out, uint64_t* block, uint64_t* offset)
+{
+    const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+    if (bytes > UINTPTR_MAX - b) return false;
+    const uintptr_t e = b + bytes;
+    std::lock_guard<std::mutex> lock(g_ranges_mu);
+    // Newest registration first: a host allocation that reuses the address of
+    // a freed, previously registered tensor must get its own metadata.
+    for (auto it = g_ranges.rbegin(); it != g_ranges.rend(); ++it) {
+        const HostRange& r = *it;
+        if (b < r.begin || e > r.end) continue;
+        *out = r;
+        const uint64_t rel = b - r.begin;
+        const uint64_t stride = r.block_bytes ? r.block_bytes : 1u;
+        *block = rel / stride;
+        *offset = rel % stride;
+        return true;
+    }
+    return false;
+}
+
+void build_aad(const void* host_ptr, size_t bytes, uint8_t direction, uint64_t ticket, uint64_t transfer_offset,
+               uint64_t epoch, uint8_t out[64])
+{
+    HostRange r{};
+    uint64_t block = 0, offset = 0;
+    if (!lookup_range(host_ptr, bytes, &r, &block, &offset)) {
+        // Unregistered memory: deterministic descriptor from the address.
+        r.layer = UINT32_MAX;
+        r.kind = UINT32_MAX;
+        block = reinterpret_cast<uintptr_t>(host_ptr);
+        offset = 0;
+    }
+    std::memset(out, 0, 64);
+    out[0] = 'S'; out[1] = 'F'; out[2] = 'A'; out[3] = 'D';
+    out[4] = 1;
+    out[5] = direction;
+    out[6] = static_cast<uint8_t>(r.kind & 0xffu);
+    store_be32(out + 8, r.layer);
+    store_be64(out + 12, block);
+    store_be64(out + 20, offset);
+    store_be64(out + 28, bytes);
+    store_be64(out + 36, ticket);
+    store_be64(out + 44, transfer_offset);
+    store_be64(out + 52, epoch);
+}
+
+// ---------------------------------------------------------------- worker pool
+class Pool {
+public:
+    explicit Pool(unsigned n)
+    {
+        for (unsigned i = 0; i < n; ++i) threads_.emplace_back([this] { run(); });
+    }
+    ~Pool()
+    {
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            stop_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : threads_) t.join();
+    }
+    size_t size() const { return threads_.size(); }
+
+    // Runs fn(0..n-1) on the workers and the calling thread; returns when done.
+    void parallel_for(size_t n, const std::function<void(size_t)>& fn)
+    {
+        if (n == 0) return;
+        auto job = std::make_shared<Job>();
+        job->n = n;
+        job->fn = &fn;
+        const size_t helpers = std::min(threads_.size(), n - 1);
+        {
+            std::lock_guard<std::mutex> lock(mu_);
+            for (size_t i = 0; i < helpers; ++i) queue_.push_back(job);
+        }
+        cv_.notify_all();
+        work(*job);
+        std::unique_lock<std::mutex> lock(job->mu);
+        job->cv.wait(lock, [&] { return job->done == job->n && job->workers == 0; });
+    }
+
+private:
+    struct Job {
+        size_t n = 0;
+        const std::function<void(size_t)>* fn = nullptr;
+        std::atomic<size_t> next{0};
+        size_t done = 0;
+        int workers = 0;
+        std::mutex mu;
+        std::condition_variable cv;
+    };
+
+    static void work(Job& job)
+    {
+        {
+            std::lock_guard<std::mutex> lock(job.mu);
+            ++job.workers;
+        }
+        size_t finished = 0;
+        for (size_t i = job.next.fetch_add(1); i < job.n; i = job.next.fetch_add(1)) {
+            (*job.fn)(i);
+            ++finished;
+        }
+        std::lock_guard<std::mutex> lock(job.mu);
+        job.done += finished;
+        --job.workers;
+        job.cv.notify_all();
+    }
+
+    void run()
+    {
+        for (;;) {
+            std::shared_ptr<Job> job;
+            {
+                std::unique_lock<std::mutex> lock(mu_);
+                cv_.wait(lock, [&] { return stop_ || !queue_.empty(); });
+                if (stop_ && queue_.empty()) return;
+                job = queue_.front();
+                queue_.pop_front();
+            }
+            if (job->next.load() < job->n) work(*job);
+        }
+    }
+
+    std::vector<std::thread> threads_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    std::deque<std::shared_ptr<Job>> queue_;
+    bool stop_ = false;
+};
+
+unsigned pool_threads()
+{
+    if (const char* v = std::getenv("SECURE_INFER_CRYPTO_THREADS")) return static_cast<unsigned>(std::max(0, std::atoi(v)));
+    const unsigned hw = std::thread::hardware_concurrency();
+    return hw > 1 ? std::min(hw - 1, 31u) : 0u;
+}
+
+Pool& pool()
+{
+    static Pool p(pool_threads());
+    return p;
+}
+
+// ---------------------------------------------------------------- OpenSSL
+struct CtxHolder {
+    EVP_CIPHER_CTX* ctx = EVP_CIPHER_CTX_new();
+    ~CtxHolder() { EVP_CIPHER_CTX_free(ctx); }
+};
+
+EVP_CIPHER_CTX* thread_ctx()
+{
+    thread_local CtxHolder holder;
+    return holder.ctx;
+}
+
+// Record = C (zero padded to 32) || tag || zero16 || AAD (secure_infer.cpp:6508-6537).
+bool encrypt_record(const uint8_t key[16], const uint8_t iv[16], const uint8_t aad[64], const uint8_t* src,
+                    uint64_t count, uint8_t* rec)
+{
+    EVP_CIPHER_CTX* ctx = thread_ctx();
+    const uint64_t aligned = aligned32(count);
+    int n = 0, fin = 0;
+    bool ok = EVP_EncryptInit_ex(ctx, EVP_aes_128_gcm(), nullptr, nullptr, nullptr) == 1 &&
+              EVP_CIPHER_CTX_ctrl(ctx, EVP_CTRL_GCM_SET_IVLEN, 12, nullptr) == 1 &&
+              EVP_EncryptInit_ex(ctx, nullptr, nullptr, key, iv) == 1 &&
+              EVP_EncryptUpdate(ctx, nullptr, &n, aad, static_cast<int>(kAadBytes)) == 1 &&
+              EVP_EncryptUpdate(ctx, rec, &n, src, static_cast<int>(count)) == 1 &&
+              EVP_EncryptFinal_ex(ctx, rec + n, &fin) == 1 &&
+              EVP_CIPHER_CTX_ctrl(ctx, EVP_CTRL_GCM_GET_TAG, 16, rec + aligned) == 1;
+    std::memset(rec + count, 0, aligned - count);
+    std::memset(rec + aligned + 16, 0, 16);
+    std::memcpy(rec + aligned + 32, aad, kAadBytes);
+    return ok;
+}
+
+// secure_infer.cpp:2479-2501; zeroes `out` on failure.
+bool decrypt_record(const uint8_t key[16], const uint8_t iv[16], const uint8_t aad[64], const uint8_t* c,
+                    uint64_t count, const uint8_t tag[16], uint8_t* out)
+{
+    EVP_CIPHER_CTX* ctx = thread_ctx();
+    int n = 0, fin = 0;
+    uint8_t tag_copy[16];
+    std::memcpy(tag_copy, tag, 16);
+    const bool ok = EVP_DecryptInit_ex(ctx, EVP_aes_128_gcm(), nullptr, nullptr, nullptr) == 1 &&
+                    EVP_CIPHER_CTX_ctrl(ctx, EVP_CTRL_GCM_SET_IVLEN, 12, nullptr) == 1 &&
+                    EVP_DecryptInit_ex(ctx, nullptr, nullptr, key, iv) == 1 &&
+                    EVP_DecryptUpdate(ctx, nullptr, &n, aad, static_cast<int>(kAadBytes)) == 1 &&
+                    EVP_DecryptUpdate(ctx, out, &n, c, static_cast<int>(count)) == 1 &&
+                    EVP_CIPHER_CTX_ctrl(ctx, EVP_CTRL_GCM_SET_TAG, 16, tag_copy) == 1 &&
+                    EVP_DecryptFinal_ex(ctx, out + n, &fin) == 1;
+    if (!ok) std::memset(out, 0, count);
+    return ok;
+}
+
+// ---------------------------------------------------------------- session
+struct LayerBatch;
+
+// Device launch descriptors for one reload_records call.
+struct LaunchSlot {
+    uint32_t cap_recs = 0, cap_segs = 0;
+    GcmRecord* host_recs = nullptr;
+    CtrJob* host_jobs = nullptr;
+    GcmRecord* dev_recs = nullptr;
+    CtrJob* dev_jobs = nullptr;
+    uint4* partials = nullptr;
+    uint32_t* counters = nullptr;
+    cudaEvent_t free_ev = nullptr;
+    bool used = false;
+};
+
+// Record staging for one host-side transfer (H2D or D2H).
+struct StageSlot {
+    uint64_t cap = 0, ks_cap = 0;
+    uint32_t cap_recs = 0;
+    uint8_t* host = nullptr;       // pinned records
+    uint8_t* dev = nullptr;        // device records
+    uint8_t* ks = nullptr;         // device keystream / D2H plaintext packets
+    uint8_t* host_aad = nullptr;   // pinned [cap_recs][64] (D2H)
+    uint8_t* dev_aad = nullptr;
+    const uint8_t** host_ptrs = nullptr;   // pinned [cap_recs] (D2H encode gather)
+    const uint8_t** dev_ptrs = nullptr;
+    uint32_t* dev_status = nullptr;
+    uint32_t* host_status = nullptr;
+    cudaEvent_t done = nullptr;
+    std::shared_ptr<LayerBatch> owner;
+};
+
+struct RetryInfo {
+    const void* src;
+    void* dst;
+};
+
+struct LayerBatch {
+    uint32_t layer = 0;
+    uint64_t job = 0;
+    uint32_t n = 0;
+    uint64_t count = 0;
+    secure_infer_codec codec{};
+    bool encrypted = false;
+    cudaStream_t stream = nullptr;
+    StageSlot* slot = nullptr;
+    cudaEvent_t done = nullptr;   // owned
+    bool harvested = false;
+    std::vector<uint32_t> status;
+    std::vector<RetryInfo> items;
+    ~LayerBatch()
+    {
+        if (done) cudaEventDestroy(done);
+    }
+};
+
+struct D2HGroup {
+    uint32_t n = 0;
+    uint64_t count = 0;
+    StageSlot* slot = nullptr;
+    cudaEvent_t copied = nullptr;    // owned
+    std::vector<void*> dsts;
+    std::vector<uint8_t> ivs;        // [n][16]
+    std::vector<uint8_t> aads;       // [n][64]
+    bool verified = false;
+    bool ok = true;
+    uint64_t batch = 0;
+};
+
+struct Session {
+    bool ready = false;
+    int device = 0;
+    uint8_t key[16] = {};
+    uint8_t salt[4] = {};
+    GcmSchedule* sched = nullptr;
+    cudaStream_t producer = nullptr;
+    std::atomic<uint64_t> next_ticket{1};
+    std::mutex replay_mu;
+    std::unordered_set<uint64_t> replay;
+
+    std::vector<LaunchSlot> launch;   // ring
+    size_t launch_next = 0;
+    std::vector<StageSlot> h2d;       // ring
+    size_t h2d_next = 0;
+    std::vector<StageSlot> d2h;       // ring
+    size_t d2h_next = 0;
+
+    std::map<uint32_t, std::vector<std::shared_ptr<LayerBatch>>> pending;
+    std::map<uint32_t, cudaEvent_t> last_event;   // not owned: batch->done
+    std::map<uint32_t, std::shared_ptr<LayerBatch>> last_batch;
+    uint64_t job = 0;
+
+    // D2H completion
+    std::deque<std::shared_ptr<D2HGroup>> d2h_queue;
+    std::vector<std::shared_ptr<D2HGroup>> d2h_all;
+    std::thread d2h_thread;
+    std::condition_variable d2h_cv;
+    bool d2h_stop = false;
+
+    ~Session()
+    {
+        // Process exit without secure_infer_session_shutdown(): stop the
+        // completion thread without touching CUDA (the runtime may be gone).
+        if (d2h_thread.joinable()) {
+            d2h_stop = true;
+            d2h_cv.notify_all();
+            if (d2h_queue.empty()) d2h_thread.join(); else d2h_thread.detach();
+        }
+    }
+};
+
+std::recursive_mutex g_mu;      // H2D path + session state
+bool host_only_session = false;
+std::mutex g_d2h_mu;            // D2H completion state
+Session g_s;
+
+std::atomic<uint64_t> g_verified{0}, g_rejected{0}, g_retried{0};
+std::atomic<uint64_t> g_ks_scheduled{0}, g_ks_hit{0}, g_ks_launches{0}, g_generation{0};
+std::atomic<uint64_t> g_tamper_h2d_nth{0}, g_tamper_d2h_nth{0};
+std::atomic<uint32_t> g_tamper_h2d_target{0};
+
+constexpr size_t kLaunchSlots = 8;
+
+size_t stage_slot_count()
+{
+    const char* v = std::getenv("SECURE_INFER_STAGE_SLOTS");
+    const int n = v ? std::atoi(v) : 3;
+    return static_cast<size_t>(std::max(1, std::min(n, 16)));
+}
+
+#define CUDA_OK(expr) ((expr) == cudaSuccess)
+
+bool ensure_launch_slot(LaunchSlot& s, uint32_t recs, uint32_t segs)
+{
+    if (s.used) cudaEventSynchronize(s.free_ev);
+    if (s.cap_recs >= recs && s.cap_segs >= segs) return true;
+    cudaFreeHost(s.host_recs); cudaFreeHost(s.host_jobs);
+    cudaFree(s.dev_recs); cudaFree(s.dev_jobs); cudaFree(s.partials); cudaFree(s.counters);
+    s = LaunchSlot{0, 0, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, s.free_ev, false};
+    const uint32_t r = std::max<uint32_t>(recs, 256), g = std::max<uint32_t>(segs, 2048);
+    if (!CUDA_OK(cudaHostAlloc(&s.host_recs, sizeof(GcmRecord) * r, cudaHostAllocDefault)) ||
+        !CUDA_OK(cudaHostAlloc(&s.host_jobs, sizeof(CtrJob) * r, cudaHostAllocDefault)) ||
+        !CUDA_OK(cudaMalloc(&s.dev_recs, sizeof(GcmRecord) * r)) ||
+        !CUDA_OK(cudaMalloc(&s.dev_jobs, sizeof(CtrJob) * r)) ||
+        !CUDA_OK(cudaMalloc(&s.partials, sizeof(uint4) * g)) ||
+        !CUDA_OK(cudaMalloc(&s.counters, sizeof(uint32_t) * r)) ||
+        !CUDA_OK(cudaMemset(s.counters, 0, sizeof(uint32_t) * r)))
+        return false;
+    s.cap_recs = r;
+    s.cap_segs = g;
+    return true;
+}
+
+void free_stage(StageSlot& s)
+{
+    cudaFreeHost(s.host); cudaFreeHost(s.host_aad); cudaFreeHost(s.host_ptrs); cudaFreeHost(s.host_status);
+    cudaFree(s.dev); cudaFree(s.ks); cudaFree(s.dev_aad); cudaFree(s.dev_ptrs); cudaFree(s.dev_status);
+    s.host = s.dev = s.ks = s.host_aad = s.dev_aad = nullptr;
+    s.host_ptrs = s.dev_ptrs = nullptr;
+    s.host_status = s.dev_status = nullptr;
+    s.cap = s.ks_cap = 0;
+    s.cap_recs = 0;
+}
+
+bool ensure_stage(StageSlot& s, uint64_t bytes, uint64_t ks_bytes, uint32_t recs)
+{
+    if (s.cap >= bytes && s.ks_cap >= ks_bytes && s.cap_recs >= recs) return true;
+    if (s.done) cudaEventSynchronize(s.done);
+    free_stage(s);
+    const uint32_t r = std::max<uint32_t>(recs, 256);
+    if (!CUDA_OK(cudaHostAlloc(&s.host, bytes, cudaHostAllocDefault)) || !CUDA_OK(cudaMalloc(&s.dev, bytes)) ||
+        (ks_bytes && !CUDA_OK(cudaMalloc(&s.ks, ks_bytes))) ||
+        !CUDA_OK(cudaHostAlloc(&s.host_aad, 64ull * r, cudaHostAllocDefault)) ||
+        !CUDA_OK(cudaMalloc(&s.dev_aad, 64ull * r)) ||
+        !CUDA_OK(cudaHostAlloc(reinterpret_cast<void**>(&s.host_ptrs), sizeof(void*) * r, cudaHostAllocDefault)) ||
+        !CUDA_OK(cudaMalloc(reinterpret_cast<void**>(&s.dev_ptrs), sizeof(void*) * r)) ||
+        !CUDA_OK(cudaHostAlloc(reinterpret_cast<void**>(&s.host_status), sizeof(uint32_t) * r, cudaHostAllocDefault)) ||
+        !CUDA_OK(cudaMalloc(reinterpret_cast<void**>(&s.dev_status), sizeof(uint32_t) * r))) {
+        free_stage(s);
+        return false;
+    }
+    s.cap = bytes;
+    s.ks_cap = ks_bytes;
+    s.cap_recs = r;
+    return true;
+}
+
+void harvest(LayerBatch& b)
+{
+    if (b.harvested) return;
+    cudaEventSynchronize(b.done);
+    b.status.assign(b.slot->host_status, b.slot->host_status + b.n);
+    b.harvested = true;
+}
+
+uint64_t reserve_ticket()
+{
+    const uint64_t t = g_s.next_ticket.fetch_add(1, std::memory_order_relaxed);
+    std::lock_guard<std::mutex> lock(g_s.replay_mu);
+    g_s.replay.insert(t);
+    return t;
+}
+
+bool reserve_given_ticket(uint64_t t)
+{
+    if (t == 0) return false;
+    std::lock_guard<std::mutex> lock(g_s.replay_mu);
+    return g_s.replay.insert(t).second;   // duplicates are replays (secure_infer.cpp:777-789)
+}
+
+void iv_for(uint64_t ticket, uint8_t iv[16])
+{
+    std::memcpy(iv, g_s.salt, 4);
+    store_be64(iv + 4, ticket);   // session nonce 0 in GCM mode (secure_infer.cpp:242-245)
+    store_be32(iv + 12, 2u);
+}
+
+void iv_words_for(uint64_t ticket, uint32_t w[4])
+{
+    w[0] = load_be32(g_s.salt);
+    w[1] = static_cast<uint32_t>(ticket >> 32);
+    w[2] = static_cast<uint32_t>(ticket);
+    w[3] = 2u;
+}
+
+bool codec_geometry(const secure_infer_codec* codec, CodecParams* cp, uint64_t* packet)
+{
+    *cp = CodecParams{};
+    *packet = 0;
+    if (codec == nullptr || codec->bits == 0) return true;
+    if ((codec->bits != 8 && codec->bits != 4) || codec->kind > 1 || codec->heads == 0 || codec->heads > 16)
+        return false;
+    const uint64_t elements = 128ull * codec->heads * 128ull;
+    cp->bits = codec->bits;
+    cp->kind = codec->kind;
+    cp->heads = codec->heads;
+    cp->qb = static_cast<uint32_t>(elements * codec->bits / 8);
+    cp->sb = static_cast<uint32_t>(elements / 64 * 4);
+    *packet = (cp->qb + 2ull * cp->sb + 16 + 15) / 16 * 16;
+    return true;
+}
+
+bool misaligned(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
+
+// Keystream for n records (stride round16(count)) on `stream`.  Caller holds g_mu.
+int keystream_records_locked(const uint64_t* tickets, uint32_t n, uint64_t count, uint8_t* keystream,
+                             cudaStream_t stream)
+{
+    if (!g_s.ready || tickets == nullptr || n == 0 || count == 0 || keystream == nullptr) return -1;
+    const uint64_t ks_stride = round16(count);
+    LaunchSlot& slot = g_s.launch[g_s.launch_next];
+    g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
+    if (!ensure_launch_slot(slot, n, 1)) return -1;
+    for (uint32_t i = 0; i < n; ++i) {
+        CtrJob& j = slot.host_jobs[i];
+        j = CtrJob{};
+        j.out = keystream + i * ks_stride;
+        j.bytes = count;
+        iv_words_for(tickets[i], j.iv);
+        j.block_first = static_cast<uint64_t>(i) * (ks_stride / 16);
+    }
+    if (!CUDA_OK(cudaMemcpyAsync(slot.dev_jobs, slot.host_jobs, sizeof(CtrJob) * n, cudaMemcpyHostToDevice, stream)))
+        return -1;
+    CtrLaunch K{};
+    K.sched = g_s.sched;
+    K.jobs = slot.dev_jobs;
+    K.njobs = n;
+    K.unaligned = misaligned(keystream) ? 1u : 0u;
+    K.total_blocks = static_cast<uint64_t>(n) * (ks_stride / 16);
+    if (launch_ctr_uniform(K, ks_stride / 16, stream) != cudaSuccess) return -1;
+    cudaEventRecord(slot.free_ev, stream);
+    slot.used = true;
+    g_ks_scheduled += n;
+    ++g_ks_launches;
+    return 0;
+}
+
+// Fused verify / XOR / (dequant) / scatter over n device-resident records.
+// keystream null -> AES inline.  Caller holds g_mu.
+int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t count, uint32_t n,
+                          const uint64_t* tickets, void* const* dsts, const uint8_t* keystream, uint32_t* status,
+                          const secure_infer_codec* codec, cudaStream_t stream)
+{
+    if (!g_s.ready || records == nullptr || n == 0 || count == 0 || tickets == nullptr || dsts == nullptr ||
+        status == nullptr || stride < record_bytes(count) || (stride & 15u))
+        return -1;
+    CodecParams cp;
+    uint64_t packet = 0;
+    if (!codec_geometry(codec, &cp, &packet)) return -1;
+    if (cp.bits && (count != packet || keystream == nullptr)) return -1;
+    const uint64_t aligned = aligned32(count);
+    const uint64_t ks_stride = round16(count);
+    const uint32_t nseg = segments_for(count, kAadBytes);
+    LaunchSlot& slot = g_s.launch[g_s.launch_next];
+    g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
+    if (!ensure_launch_slot(slot, n, nseg * n)) return -1;
+    const bool rec_misaligned = misaligned(records);
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint8_t* base = records + i * stride;
+        GcmRecord& r = slot.host_recs[i];
+        r = GcmRecord{};
+        r.op = kOpDecrypt;
+        r.in = base;
+        r.ks = keystream ? keystream + i * ks_stride : nullptr;
+        r.aad = base + aligned + 32;
+        r.aad_bytes = static_cast<uint32_t>(kAadBytes);
+        r.tag_in = base + aligned;
+        r.out = static_cast<uint8_t*>(dsts[i]);
+        r.status = status + i;
+        r.count = count;
+        iv_words_for(tickets[i], r.iv);
+        r.seg_first = i * nseg;
+        r.nseg = nseg;
+        if (rec_misaligned || misaligned(dsts[i]) || misaligned(r.ks)) r.flags |= kRecUnaligned;
+        if (cp.bits) {
+            if (r.flags & kRecUnaligned) return -1;
+            r.flags |= kRecCodec;
+        }
+    }
+    if (!CUDA_OK(cudaMemcpyAsync(slot.dev_recs, slot.host_recs, sizeof(GcmRecord) * n, cudaMemcpyHostToDevice, stream)))
+        return -1;
+    SegmentLaunch L{};
+    L.sched = g_s.sched;
+    L.recs = slot.dev_recs;
+    L.nrec = n;
+    L.total_segs = nseg * n;
+    L.partials = slot.partials;
+    L.counters = slot.counters;
+    L.codec = cp;
+    if (launch_segments(L, keystream == nullptr, stream) != cudaSuccess) return -1;
+    cudaEventRecord(slot.free_ev, stream);
+    slot.used = true;
+    if (keystream) g_ks_hit += n;
+    return 0;
+}
+
+// Keystream on `producer`, joined into `stream`, then the fused kernel.
+int reload_records_locked(uint32_t layer, const uint8_t* records, uint64_t stride, uint64_t count, uint32_t n,
+                          const uint64_t* tickets, void* const* dsts, uint8_t* keystream, uint32_t* status,
+                          const secure_infer_codec* codec, cudaStream_t stream, cudaStream_t producer)
+{
+    (void)layer;
+    if (keystream) {
+        if (keystream_records_locked(tickets, n, count, keystream, producer) != 0) return -1;
+        if (producer != stream) {
+            cudaEvent_t ev = nullptr;
+            if (!CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming))) return -1;
+            cudaEventRecord(ev, producer);
+            cudaStreamWaitEvent(stream, ev, 0);
+            cudaEventDestroy(ev);
+        }
+    }
+    return verify_records_locked(records, stride, count, n, tickets, dsts, keystream, status, codec, stream);
+}
+
+void maybe_tamper_h2d(uint8_t* rec, uint64_t count)
+{
+    uint64_t nth = g_tamper_h2d_nth.load();
+    while (nth != 0) {
+        if (g_tamper_h2d_nth.compare_exchange_weak(nth, nth - 1)) {
+            if (nth == 1) {
+                // Flip one byte after host encryption, before the DMA (secure_infer.cpp:6560-6602).
+                uint8_t* target = g_tamper_h2d_target.load() == 1 ? rec + aligned32(count) : rec + count / 2;
+                target[0] ^= 0x01;
+            }
+            return;
+        }
+    }
+}
+
+// Encrypt + stage + device reload.  Returns the batch (not yet registered).
+std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* const* srcs, void* const* dsts, uint32_t n,
+                                                uint64_t count, const secure_infer_codec* codec, bool encrypted,
+                                                const uint64_t* given_tickets, cudaStream_t stream)
+{
+    if (!g_s.ready || srcs == nullptr || dsts == nullptr || n == 0 || count == 0) return nullptr;
+    CodecParams cp;
+    uint64_t packet = 0;
+    if (!codec_geometry(codec, &cp, &packet)) return nullptr;
+    const uint64_t stride = record_bytes(count);
+    StageSlot& slot = g_s.h2d[g_s.h2d_next];
+    g_s.h2d_next = (g_s.h2d_next + 1) % g_s.h2d.size();
+    if (slot.owner) harvest(*slot.owner);   // statuses leave the slot before reuse
+    if (!ensure_stage(slot, stride * n, round16(count) * n, n)) return nullptr;
+    if (slot.done) cudaEventSynchronize(slot.done);
+
+    std::vector<uint64_t> tickets(n);
+    if (encrypted) {
+        if (given_tickets == nullptr) return nullptr;
+        for (uint32_t i = 0; i < n; ++i)
+            if (!reserve_given_ticket(given_tickets[i])) return nullptr;
+        tickets.assign(given_tickets, given_tickets + n);
+    } else {
+        for (uint32_t i = 0; i < n; ++i) tickets[i] = reserve_ticket();
+        std::atomic<bool> ok{true};
+        const uint8_t* key = g_s.key;
+        pool().parallel_for(n, [&](size_t i) {
+            uint8_t iv[16], aad[64];
+            iv_for(tickets[i], iv);
+            build_aad(srcs[i], count, SECURE_INFER_DIRECTION_H2D, tickets[i], 0, 0, aad);
+            if (!encrypt_record(key, iv, aad, static_cast<const uint8_t*>(srcs[i]), count, slot.host + i * stride))
+                ok = false;
+        });
+        if (!ok) return nullptr;
+        for (uint32_t i = 0; i < n; ++i) maybe_tamper_h2d(slot.host + i * stride, count);
+    }
+
+    auto batch = std::make_shared<LayerBatch>();
+    batch->layer = layer;
+    batch->job = g_s.job;
+    batch->n = n;
+    batch->count = count;
+    if (codec) batch->codec = *codec;
+    batch->encrypted = encrypted;
+    batch->stream = stream;
+    batch->slot = &slot;
+    batch->items.resize(n);
+    for (uint32_t i = 0; i < n; ++i) batch->items[i] = RetryInfo{encrypted ? nullptr : srcs[i], dsts[i]};
+    if (!CUDA_OK(cudaEventCreateWithFlags(&batch->done, cudaEventDisableTiming))) return nullptr;
+
+    // The keystream area of this slot may still be read by its previous
+    // kernel: the producer waits for the slot's last completion.
+    if (slot.done) cudaStreamWaitEvent(g_s.producer, slot.done, 0);
+    const void* host_src = encrypted ? srcs[0] : slot.host;
+    if (!CUDA_OK(cudaMemcpyAsync(slot.dev, host_src, stride * n, cudaMemcpyHostToDevice, stream))) return nullptr;
+    if (reload_records_locked(layer, slot.dev, stride, count, n, tickets.data(), dsts, slot.ks, slot.dev_status,
+                              codec, stream, g_s.producer) != 0)
+        return nullptr;
+    cudaMemcpyAsync(slot.host_status, slot.dev_status, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, stream);
+    cudaEventRecord(batch->done, stream);
+    slot.done = batch->done;
+    slot.owner = batch;
+    return batch;
+}
+
+void register_batch_locked(const std::shared_ptr<LayerBatch>& b)
+{
+    g_s.pending[b->layer].push_back(b);
+    g_s.last_event[b->layer] = b->done;
+    g_s.last_batch[b->layer] = b;
+}
+
+// ------------------------------------------------------------ H2D groups
+struct Submission {
+    void* dst;
+    const void* src;
+    size_t count;
+    cudaStream_t stream;
+};
+
+thread_local int t_group_depth = 0;
+thread_local std::vector<Submission> t_group;
+
+int flush_submissions(std::vector<Submission>& subs)
+{
+    // Bucket by (layer, count, stream); each bucket is one staged reload.
+    std::map<std::tuple<uint32_t, size_t, cudaStream_t>, std::vector<size_t>> buckets;
+    for (size_t i = 0; i < subs.size(); ++i) {
+        HostRange r{};
+        uint64_t block = 0, off = 0;
+        const uint32_t layer = lookup_range(subs[i].src, subs[i].count, &r, &block, &off) ? r.layer : UINT32_MAX;
+        buckets[{layer, subs[i].count, subs[i].stream}].push_back(i);
+    }
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    for (auto& kv : buckets) {
+        std::vector<const void*> srcs;
+        std::vector<void*> dsts;
+        for (size_t i : kv.second) {
+            srcs.push_back(subs[i].src);
+            dsts.push_back(subs[i].dst);
+        }
+        auto b = submit_layer_locked(std::get<0>(kv.first), srcs.data(), dsts.data(), static_cast<uint32_t>(srcs.size()),
+                                     std::get<1>(kv.first), nullptr, false, nullptr, std::get<2>(kv.first));
+        if (!b) return -1;
+        register_batch_locked(b);
+    }
+    subs.clear();
+    return 0;
+}
+
+// ------------------------------------------------------------ D2H
+uint64_t g_d2h_batch_id = 0;
+thread_local uint64_t t_d2h_batch = 0;
+thread_local int t_d2h_group_depth = 0;
+thread_local std::vector<Submission> t_d2h_group;
+
+void d2h_worker()
+{
+    std::unique_lock<std::mutex> lock(g_d2h_mu);
+    for (;;) {
+        g_s.d2h_cv.wait(lock, [] { return g_s.d2h_stop || !g_s.d2h_queue.empty(); });
+        if (g_s.d2h_queue.empty()) return;
+        auto g = g_s.d2h_queue.front();
+        g_s.d2h_queue.pop_front();
+        lock.unlock();
+        cudaEventSynchronize(g->copied);
+        const uint64_t stride = record_bytes(g->count), aligned = aligned32(g->count);
+        uint64_t nth = g_tamper_d2h_nth.load();
+        while (nth != 0 && !g_tamper_d2h_nth.compare_exchange_weak(nth, nth > g->n ? nth - g->n : 0)) {}
+        if (nth != 0 && nth <= g->n) g->slot->host[(nth - 1) * stride] ^= 0x01;   // secure_infer.cpp:2454-2468
+        std::atomic<bool> ok{true};
+        const uint8_t* key = g_s.key;
+        pool().parallel_for(g->n, [&](size_t i) {
+            const uint8_t* rec = g->slot->host + i * stride;
+            if (!decrypt_record(key, &g->ivs[16 * i], &g->aads[64 * i], rec, g->count, rec + aligned,
+                                static_cast<uint8_t*>(g->dsts[i])))
+                ok = false;
+        });
+        lock.lock();
+        g->ok = ok.load();
+        g->verified = true;
+        if (g->ok) g_verified += g->n; else g_rejected += g->n;
+        g_s.d2h_cv.notify_all();
+    }
+}
+
+int d2h_submit_group(const void* const* srcs, void* const* dsts, uint32_t n, uint64_t count,
+                     const secure_infer_codec* codec, cudaStream_t stream)
+{
+    CodecParams cp;
+    uint64_t packet = 0;
+    if (!codec_geometry(codec, &cp, &packet) || n == 0 || srcs == nullptr || dsts == nullptr) return -1;
+    if (cp.bits) count = packet;
+    if (count == 0) return -1;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!g_s.ready) return -1;
+    const uint64_t stride = record_bytes(count), aligned = aligned32(count);
+    StageSlot& slot = g_s.d2h[g_s.d2h_next];
+    g_s.d2h_next = (g_s.d2h_next + 1) % g_s.d2h.size();
+    {
+        // The slot's previous group must be verified before its host copy is reused.
+        std::unique_lock<std::mutex> dl(g_d2h_mu);
+        g_s.d2h_cv.wait(dl, [&] {
+            for (auto& g : g_s.d2h_all)
+                if (g->slot == &slot && !g->verified) return false;
+            return true;
+        });
+    }
+    if (!ensure_stage(slot, stride * n, cp.bits ? packet * n : 0, n)) return -1;
+    auto g = std::make_shared<D2HGroup>();
+    g->n = n;
+    g->count = count;
+    g->slot = &slot;
+    g->batch = t_d2h_batch;
+    g->dsts.assign(dsts, dsts + n);
+    g->ivs.resize(16ull * n);
+    g->aads.resize(64ull * n);
+    if (!CUDA_OK(cudaEventCreateWithFlags(&g->copied, cudaEventDisableTiming))) return -1;
+    std::vector<GcmRecord> recs(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint64_t t = reserve_ticket();
+        iv_for(t, &g->ivs[16 * i]);
+        build_aad(dsts[i], count, SECURE_INFER_DIRECTION_D2H, t, 0, 0, &g->aads[64 * i]);
+        std::memcpy(slot.host_aad + 64ull * i, &g->aads[64 * i], 64);
+        slot.host_ptrs[i] = static_cast<const uint8_t*>(srcs[i]);
+    }
+    if (!CUDA_OK(cudaMemcpyAsync(slot.dev_aad, slot.host_aad, 64ull * n, cudaMemcpyHostToDevice, stream))) return -1;
+    if (cp.bits) {
+        if (!CUDA_OK(cudaMemcpyAsync(slot.dev_ptrs, slot.host_ptrs, sizeof(void*) * n, cudaMemcpyHostToDevice, stream)))
+            return -1;
+        EncodeLaunch E{};
+        E.srcs = slot.dev_ptrs;
+        E.packets = slot.ks;
+        E.n = n;
+        E.width = static_cast<uint32_t>(packet);
+        E.layer = codec->layer;
+        E.codec = cp;
+        if (launch_encode(E, stream) != cudaSuccess) return -1;
+    }
+    // Device records: op Encrypt, C into the staging records, tag after C.
+    const uint32_t nseg = segments_for(count, kAadBytes);
+    LaunchSlot& ls = g_s.launch[g_s.launch_next];
+    g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
+    if (!ensure_launch_slot(ls, n, nseg * n)) return -1;
+    for (uint32_t i = 0; i < n; ++i) {
+        GcmRecord& r = ls.host_recs[i];
+        r = GcmRecord{};
+        r.op = kOpEncrypt;
+        r.in = cp.bits ? slot.ks + i * packet : static_cast<const uint8_t*>(srcs[i]);
+        r.aad = slot.dev_aad + 64ull * i;
+        r.aad_bytes = static_cast<uint32_t>(kAadBytes);
+        r.out = slot.dev + i * stride;
+        r.tag_out = slot.dev + i * stride + aligned;
+        r.count = count;
+        const uint8_t* iv = &g->ivs[16 * i];
+        r.iv[0] = load_be32(iv); r.iv[1] = load_be32(iv + 4); r.iv[2] = load_be32(iv + 8); r.iv[3] = 2u;
+        r.seg_first = i * nseg;
+        r.nseg = nseg;
+        if (misaligned(r.in)) r.flags |= kRecUnaligned;
+    }
+    if (!CUDA_OK(cudaMemcpyAsync(ls.dev_recs, ls.host_recs, sizeof(GcmRecord) * n, cudaMemcpyHostToDevice, stream)))
+        return -1;
+    SegmentLaunch L{};
+    L.sched = g_s.sched;
+    L.recs = ls.dev_recs;
+    L.nrec = n;
+    L.total_segs = nseg * n;
+    L.partials = ls.partials;
+    L.counters = ls.counters;
+    if (launch_segments(L, true, stream) != cudaSuccess) return -1;
+    cudaEventRecord(ls.free_ev, stream);
+    ls.used = true;
+    if (!CUDA_OK(cudaMemcpyAsync(slot.host, slot.dev, stride * n, cudaMemcpyDeviceToHost, stream))) return -1;
+    cudaEventRecord(g->copied, stream);
+    {
+        std::lock_guard<std::mutex> dl(g_d2h_mu);
+        g_s.d2h_queue.push_back(g);
+        g_s.d2h_all.push_back(g);
+    }
+    g_s.d2h_cv.notify_all();
+    return 0;
+}
+
+// Waits for D2H groups of `batch` (0 = all); drops finished groups.
+int d2h_join(uint64_t batch, bool device_only)
+{
+    std::unique_lock<std::mutex> dl(g_d2h_mu);
+    if (device_only) {
+        std::vector<cudaEvent_t> evs;
+        for (auto& g : g_s.d2h_all)
+            if (batch == 0 || g->batch == batch) evs.push_back(g->copied);
+        dl.unlock();
+        for (auto e : evs) cudaEventSynchronize(e);
+        return 0;
+    }
+    g_s.d2h_cv.wait(dl, [&] {
+        for (auto& g : g_s.d2h_all)
+            if ((batch == 0 || g->batch == batch) && !g->verified) return false;
+        return true;
+    });
+    bool ok = true;
+    for (auto it = g_s.d2h_all.begin(); it != g_s.d2h_all.end();) {
+        if (batch == 0 || (*it)->batch == batch) {
+            ok = ok && (*it)->ok;
+            cudaEventDestroy((*it)->copied);
+            it = g_s.d2h_all.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    return ok ? 0 : -1;
+}
+
+int d2h_flush_thread_group()
+{
+    std::map<std::pair<size_t, cudaStream_t>, std::vector<size_t>> buckets;
+    for (size_t i = 0; i < t_d2h_group.size(); ++i)
+        buckets[{t_d2h_group[i].count, t_d2h_group[i].stream}].push_back(i);
+    for (auto& kv : buckets) {
+        std::vector<const void*> srcs;
+        std::vector<void*> dsts;
+        for (size_t i : kv.second) {
+            srcs.push_back(t_d2h_group[i].src);
+            dsts.push_back(t_d2h_group[i].dst);
+        }
+        if (d2h_submit_group(srcs.data(), dsts.data(), static_cast<uint32_t>(srcs.size()), kv.first.first, nullptr,
+                             kv.first.second) != 0)
+            return -1;
+    }
+    t_d2h_group.clear();
+    return 0;
+}
+
+void shutdown_locked()
+{
+    host_only_session = false;
+    if (!g_s.ready) return;
+    cudaDeviceSynchronize();
+    {
+        std::lock_guard<std::mutex> dl(g_d2h_mu);
+        g_s.d2h_stop = true;
+    }
+    g_s.d2h_cv.notify_all();
+    if (g_s.d2h_thread.joinable()) g_s.d2h_thread.join();
+    for (auto& g : g_s.d2h_all) cudaEventDestroy(g->copied);
+    g_s.d2h_all.clear();
+    g_s.d2h_queue.clear();
+    for (auto& kv : g_s.pending)
+        for (auto& b : kv.second) harvest(*b);
+    g_s.pending.clear();
+    g_s.last_event.clear();
+    g_s.last_batch.clear();
+    for (auto& s : g_s.h2d) { s.owner.reset(); free_stage(s); }
+    for (auto& s : g_s.d2h) free_stage(s);
+    for (auto& s : g_s.launch) {
+        cudaFreeHost(s.host_recs); cudaFreeHost(s.host_jobs);
+        cudaFree(s.dev_recs); cudaFree(s.dev_jobs); cudaFree(s.partials); cudaFree(s.counters);
+        if (s.free_ev) cudaEventDestroy(s.free_ev);
+    }
+    g_s.launch.clear();
+    g_s.h2d.clear();
+    g_s.d2h.clear();
+    cudaFree(g_s.sched);
+    g_s.sched = nullptr;
+    if (g_s.producer) cudaStreamDestroy(g_s.producer);
+    g_s.producer = nullptr;
+    g_s.ready = false;
+}
+
+}  // namespace
+}  // namespace host
+}  // namespace sib
+
+using namespace sib::host;
+using sib::launch_schedule;
+
+#define SI_EXPORT extern "C" __attribute__((visibility("default")))
+
+SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const uint8_t* iv_salt4)
+{
+    if (key16 == nullptr || iv_salt4 == nullptr) return -1;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    shutdown_locked();
+    host_only_session = false;
+    g_s.device = device;
+    std::memcpy(g_s.key, key16, 16);
+    std::memcpy(g_s.salt, iv_salt4, 4);
+    g_s.next_ticket = 1;
+    {
+        std::lock_guard<std::mutex> rl(g_s.replay_mu);
+        g_s.replay.clear();
+    }
+    g_s.job = 0;
+    if (device < 0) {
+        // Host-only session: record encryption, tickets and AAD work without
+        // a GPU; every device entry point still reports failure.
+        host_only_session = true;
+        return 0;
+    }
+    if (!CUDA_OK(cudaSetDevice(device))) return -1;
+    uint8_t* dkey = nullptr;
+    if (!CUDA_OK(cudaMalloc(&g_s.sched, sib::schedule_bytes())) ||
+        !CUDA_OK(cudaMemset(g_s.sched, 0, sib::schedule_bytes())) || !CUDA_OK(cudaMalloc(&dkey, 16)) ||
+        !CUDA_OK(cudaMemcpy(dkey, key16, 16, cudaMemcpyHostToDevice)) ||
+        !CUDA_OK(cudaStreamCreateWithFlags(&g_s.producer, cudaStreamNonBlocking))) {
+        cudaFree(dkey);
+        return -1;
+    }
+    // H = E_K(0^128) and the GHASH tables are derived on the device; the key
+    // copy used for the derivation is wiped and freed right after.
+    const bool ok = launch_schedule(g_s.sched, dkey, nullptr, true, g_s.producer) == cudaSuccess &&
+                    CUDA_OK(cudaMemsetAsync(dkey, 0, 16, g_s.producer)) &&
+                    CUDA_OK(cudaStreamSynchronize(g_s.producer));
+    cudaFree(dkey);
+    if (!ok) return -1;
+    g_s.launch.resize(kLaunchSlots);
+    for (auto& s : g_s.launch) cudaEventCreateWithFlags(&s.free_ev, cudaEventDisableTiming);
+    g_s.h2d.resize(stage_slot_count());
+    g_s.d2h.resize(stage_slot_count());
+    g_s.d2h_stop = false;
+    g_s.d2h_thread = std::thread(d2h_worker);
+    g_verified = g_rejected = g_retried = 0;
+    g_s.ready = true;
+    return 0;
+}
+
+SI_EXPORT int secure_infer_session_shutdown(void)
+{
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    shutdown_locked();
+    return 0;
+}
+
+SI_EXPORT void secure_infer_register_host_range_ex(const void* base, size_t bytes, uint32_t layer_id,
+                                                   uint32_t tensor_kind, size_t block_bytes)
+{
+    if (base == nullptr || bytes == 0) return;
+    const uintptr_t b = reinterpret_cast<uintptr_t>(base);
+    if (bytes > UINTPTR_MAX - b) return;
+    std::lock_guard<std::mutex> lock(g_ranges_mu);
+    for (auto& r : g_ranges) {
+        if (r.begin == b && r.end == b + bytes) {
+            r.layer = layer_id;
+            r.kind = tensor_kind;
+            r.block_bytes = block_bytes;
+            return;
+        }
+    }
+    g_ranges.push_back({b, b + bytes, layer_id, tensor_kind, block_bytes});
+}
+
+SI_EXPORT void secure_infer_register_host_range(const void* base, size_t bytes)
+{
+    secure_infer_register_host_range_ex(base, bytes, UINT32_MAX, UINT32_MAX, 0);
+}
+
+SI_EXPORT uint64_t secure_infer_new_transfer_ticket(void) { return reserve_ticket(); }
+
+SI_EXPORT int secure_infer_derive_transfer_iv(const uint8_t* base_iv16, uint64_t ticket, uint64_t block_offset,
+                                              uint8_t* out_iv16)
+{
+    if (base_iv16 == nullptr || out_iv16 == nullptr || ticket == 0 || block_offset > UINT32_MAX - 2u) return -1;
+    std::memcpy(out_iv16, base_iv16, 16);
+    store_be64(out_iv16 + 4, ticket);
+    store_be32(out_iv16 + 12, static_cast<uint32_t>(block_offset + 2u));
+    return 0;
+}
+
+SI_EXPORT int secure_infer_build_gcm_aad(const void* host_ptr, size_t bytes, uint8_t direction, uint64_t ticket,
+                                         uint64_t transfer_offset, uint8_t* out64)
+{
+    if (out64 == nullptr || host_ptr == nullptr || bytes == 0 || ticket == 0 ||
+        (direction != SECURE_INFER_DIRECTION_H2D && direction != SECURE_INFER_DIRECTION_D2H))
+        return -1;
+    build_aad(host_ptr, bytes, direction, ticket, transfer_offset, 0, out64);
+    return 0;
+}
+
+SI_EXPORT uint64_t secure_infer_record_bytes(uint64_t count) { return record_bytes(count); }
+
+SI_EXPORT int secure_infer_h2d_encrypt_records(const void* const* srcs, uint64_t count, uint32_t n, void* records,
+                                               uint64_t record_stride, uint64_t* tickets_out)
+{
+    if (srcs == nullptr || records == nullptr || n == 0 || count == 0 || record_stride < record_bytes(count))
+        return -1;
+    std::vector<uint64_t> tickets(n);
+    uint8_t key[16];
+    {
+        std::lock_guard<std::recursive_mutex> lock(g_mu);
+        if (!g_s.ready && !host_only_session) return -1;
+        std::memcpy(key, g_s.key, 16);
+        for (uint32_t i = 0; i < n; ++i) tickets[i] = g_s.next_ticket.fetch_add(1);
+    }
+    std::atomic<bool> ok{true};
+    uint8_t* out = static_cast<uint8_t*>(records);
+    pool().parallel_for(n, [&](size_t i) {
+        uint8_t iv[16], aad[64];
+        iv_for(tickets[i], iv);
+        build_aad(srcs[i], count, SECURE_INFER_DIRECTION_H2D, tickets[i], 0, 0, aad);
+        if (!encrypt_record(key, iv, aad, static_cast<const uint8_t*>(srcs[i]), count, out + i * record_stride))
+            ok = false;
+    });
+    if (tickets_out) std::memcpy(tickets_out, tickets.data(), sizeof(uint64_t) * n);
+    return ok ? 0 : -1;
+}
+
+SI_EXPORT uint64_t secure_infer_codec_packet_bytes(uint32_t heads, uint32_t bits)
+{
+    secure_infer_codec c{bits, 0, heads, 0};
+    sib::CodecParams cp;
+    uint64_t packet = 0;
+    if (bits == 0 || !codec_geometry(&c, &cp, &packet)) return 0;
+    return packet;
+}
+
+SI_EXPORT int secure_infer_reload_records(uint32_t layer, const void* records, uint64_t record_stride, uint64_t count,
+                                          uint32_t n, const uint64_t* tickets, void* const* dsts, void* keystream,
+                                          uint32_t* status, const secure_infer_codec* codec, void* stream,
+                                          void* producer_stream)
+{
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    return reload_records_locked(layer, static_cast<const uint8_t*>(records), record_stride, count, n, tickets, dsts,
+                                 static_cast<uint8_t*>(keystream), status, codec, static_cast<cudaStream_t>(stream),
+                                 producer_stream ? static_cast<cudaStream_t>(producer_stream) : g_s.producer);
+}
+
+SI_EXPORT int secure_infer_keystream_records(const uint64_t* tickets, uint32_t n, uint64_t count, void* keystream,
+                                             void* stream)
+{
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    return keystream_records_locked(tickets, n, count, static_cast<uint8_t*>(keystream),
+                                    static_cast<cudaStream_t>(stream));
+}
+
+SI_EXPORT int secure_infer_verify_records(uint32_t layer, const void* records, uint64_t record_stride, uint64_t count,
+                                          uint32_t n, const uint64_t* tickets, void* const* dsts,
+                                          const void* keystream, uint32_t* status, const secure_infer_codec* codec,
+                                          void* stream)
+{
+    (void)layer;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    return verify_records_locked(static_cast<const uint8_t*>(records), record_stride, count, n, tickets, dsts,
+                                 static_cast<const uint8_t*>(keystream), status, codec,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+SI_EXPORT int secure_infer_h2d_reload_layer(uint32_t layer, const void* const* srcs, void* const* dsts, uint32_t n,
+                                            uint64_t count, const secure_infer_codec* codec,
+                                            int records_are_encrypted, const uint64_t* tickets, void* stream)
+{
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    auto b = submit_layer_locked(layer, srcs, dsts, n, count, codec, records_are_encrypted != 0, tickets,
+                                 static_cast<cudaStream_t>(stream));
+    if (!b) return -1;
+    register_batch_locked(b);
+    return 0;
+}
+
+SI_EXPORT int secure_infer_layer_ready_wait(uint32_t layer, void* stream)
+{
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    auto it = g_s.last_event.find(layer);
+    if (it == g_s.last_event.end()) return -1;
+    return CUDA_OK(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), it->second, 0)) ? 0 : -1;
+}
+
+SI_EXPORT int secure_infer_h2d_layer_group_begin(size_t expected_tasks)
+{
+    if (t_group_depth++ == 0) {
+        t_group.clear();
+        t_group.reserve(expected_tasks);
+    }
+    return 0;
+}
+
+SI_EXPORT int secure_infer_h2d_layer_group_end(void)
+{
+    if (t_group_depth == 0) return -1;
+    if (--t_group_depth != 0) return 0;
+    return flush_submissions(t_group);
+}
+
+SI_EXPORT int secure_infer_h2d_submit(void* dst, size_t dst_capacity, const void* src, size_t count, void* stream)
+{
+    if (dst == nullptr || src == nullptr || count == 0 || dst_capacity < count) return -1;
+    if (t_group_depth > 0) {
+        t_group.push_back({dst, src, count, static_cast<cudaStream_t>(stream)});
+        return 0;
+    }
+    std::vector<Submission> one{{dst, src, count, static_cast<cudaStream_t>(stream)}};
+    return flush_submissions(one);
+}
+
+SI_EXPORT int secure_infer_recovery_wait_layer_authentication(uint32_t layer)
+{
+    std::vector<std::shared_ptr<LayerBatch>> batches;
+    {
+        std::lock_guard<std::recursive_mutex> lock(g_mu);
+        auto it = g_s.pending.find(layer);
+        if (it == g_s.pending.end()) return 0;
+        batches.swap(it->second);
+        g_s.pending.erase(it);
+    }
+    bool ok = true;
+    for (auto& b : batches) {
+        std::lock_guard<std::recursive_mutex> lock(g_mu);
+        harvest(*b);
+        std::vector<const void*> srcs;
+        std::vector<void*> dsts;
+        for (uint32_t i = 0; i < b->n; ++i) {
+            if (b->status[i] == 1u) { ++g_verified; continue; }
+            ++g_rejected;
+            if (b->encrypted || b->items[i].src == nullptr) { ok = false; continue; }
+            srcs.push_back(b->items[i].src);
+            dsts.push_back(b->items[i].dst);
+        }
+        if (srcs.empty()) continue;
+        // One strict retry from the trusted host copy under fresh tickets.
+        g_retried += srcs.size();
+        auto r = submit_layer_locked(b->layer, srcs.data(), dsts.data(), static_cast<uint32_t>(srcs.size()), b->count,
+                                     b->codec.bits ? &b->codec : nullptr, false, nullptr, b->stream);
+        if (!r) { ok = false; continue; }
+        harvest(*r);
+        for (uint32_t i = 0; i < r->n; ++i) {
+            if (r->status[i] == 1u) ++g_verified; else { ++g_rejected; ok = false; }
+        }
+        g_s.last_event[b->layer] = r->done;
+        g_s.last_batch[b->layer] = r;
+    }
+    return ok ? 0 : -1;
+}
+
+SI_EXPORT void secure_infer_recovery_set_job_id(uint64_t job_id)
+{
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    g_s.job = job_id;
+}
+
+SI_EXPORT int secure_infer_recovery_wait_job_authentication(uint64_t job_id)
+{
+    std::vector<std::shared_ptr<LayerBatch>> batches;
+    {
+        std::lock_guard<std::recursive_mutex> lock(g_mu);
+        for (auto it = g_s.pending.begin(); it != g_s.pending.end();) {
+            auto& v = it->second;
+            for (auto b = v.begin(); b != v.end();) {
+                if ((*b)->job == job_id) { batches.push_back(*b); b = v.erase(b); } else { ++b; }
+            }
+            it = v.empty() ? g_s.pending.erase(it) : std::next(it);
+        }
+    }
+    if (batches.empty()) return -1;
+    bool valid = true;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    for (auto& b : batches) {
+        harvest(*b);
+        for (uint32_t i = 0; i < b->n; ++i) {
+            if (b->status[i] == 1u) ++g_verified; else { ++g_rejected; valid = false; }
+        }
+    }
+    return valid ? 1 : 0;
+}
+
+SI_EXPORT int secure_infer_d2h_batch_begin(size_t expected_groups)
+{
+    (void)expected_groups;
+    std::lock_guard<std::mutex> dl(g_d2h_mu);
+    t_d2h_batch = ++g_d2h_batch_id;
+    return 0;
+}
+
+SI_EXPORT int secure_infer_d2h_group_begin(size_t expected_tasks)
+{
+    if (t_d2h_group_depth++ == 0) {
+        t_d2h_group.clear();
+        t_d2h_group.reserve(expected_tasks);
+    }
+    return 0;
+}
+
+SI_EXPORT int secure_infer_d2h_submit(void* dst_host, const void* src_device, size_t count, void* stream)
+{
+    if (dst_host == nullptr || src_device == nullptr || count == 0) return -1;
+    t_d2h_group.push_back({dst_host, src_device, count, static_cast<cudaStream_t>(stream)});
+    if (t_d2h_group_depth == 0) return d2h_flush_thread_group();
+    return 0;
+}
+
+SI_EXPORT int secure_infer_d2h_group_end(void)
+{
+    if (t_d2h_group_depth == 0) return -1;
+    if (--t_d2h_group_depth != 0) return 0;
+    return d2h_flush_thread_group();
+}
+
+SI_EXPORT int secure_infer_d2h_batch_device_barrier(void) { return d2h_join(t_d2h_batch, true); }
+
+SI_EXPORT int secure_infer_d2h_batch_end(void)
+{
+    const int rc = d2h_join(t_d2h_batch, false);
+    t_d2h_batch = 0;
+    return rc;
+}
+
+SI_EXPORT int secure_infer_d2h_writeback_layer(const void* const* src_blocks, void* const* dsts, uint32_t n,
+                                               const secure_infer_codec* codec, void* stream)
+{
+    if (codec == nullptr) return -1;
+    const uint64_t raw = 2ull * 128u * codec->heads * 128u;
+    return d2h_submit_group(src_blocks, dsts, n, raw, codec, static_cast<cudaStream_t>(stream));
+}
+
+SI_EXPORT int secure_infer_d2h_wait(void) { return d2h_join(0, false); }
+
+SI_EXPORT void secure_infer_invalidate_transfer_prefetches(void) { ++g_generation; }
+SI_EXPORT void secure_infer_retire_transfer_prefetches(void) { ++g_generation; }
+
+SI_EXPORT void secure_infer_get_transfer_prefetch_stats(uint64_t* ready, uint64_t* busy_fallback,
+                                                        uint64_t* missing_fallback)
+{
+    if (ready) *ready = g_ks_hit.load();
+    if (busy_fallback) *busy_fallback = 0;
+    if (missing_fallback) *missing_fallback = 0;
+}
+
+SI_EXPORT void secure_infer_get_gcm_keystream_stats(uint64_t* scheduled, uint64_t* ready, uint64_t* hit,
+                                                    uint64_t* miss, uint64_t* retired, uint64_t* stale,
+                                                    uint64_t* failed)
+{
+    if (scheduled) *scheduled = g_ks_scheduled.load();
+    if (ready) *ready = g_ks_scheduled.load();
+    if (hit) *hit = g_ks_hit.load();
+    if (miss) *miss = 0;
+    if (retired) *retired = g_ks_hit.load();
+    if (stale) *stale = 0;
+    if (failed) *failed = 0;
+}
+
+SI_EXPORT void secure_infer_get_npu_keystream_stats(uint64_t* launched, uint64_t* completed, uint64_t* failed)
+{
+    if (launched) *launched = g_ks_launches.load();
+    if (completed) *completed = g_ks_launches.load();
+    if (failed) *failed = 0;
+}
+
+SI_EXPORT void secure_infer_get_npu_keystream_pool_stats(uint64_t* slots, uint64_t* in_use)
+{
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (slots) *slots = g_s.h2d.size();
+    if (in_use) {
+        uint64_t u = 0;
+        for (auto& s : g_s.h2d) u += (s.owner && !s.owner->harvested) ? 1 : 0;
+        *in_use = u;
+    }
+}
+
+SI_EXPORT uint64_t secure_infer_count_ready_unconsumed_gcm_tickets(void) { return 0; }
+SI_EXPORT int secure_infer_flush_completed_h2d_profile(void) { return 0; }
+SI_EXPORT int secure_infer_drain_h2d_profile_after_job(void) { return 0; }
+
+SI_EXPORT void secure_infer_get_auth_stats(uint64_t* verified, uint64_t* rejected, uint64_t* retried)
+{
+    if (verified) *verified = g_verified.load();
+    if (rejected) *rejected = g_rejected.load();
+    if (retried) *retried = g_retried.load();
+}
+
+SI_EXPORT void secure_infer_arm_tamper(uint32_t direction, uint64_t nth, uint32_t target)
+{
+    if (direction == SECURE_INFER_DIRECTION_H2D) {
+        g_tamper_h2d_target = target;
+        g_tamper_h2d_nth = nth;
+    } else if (direction == SECURE_INFER_DIRECTION_D2H) {
+        g_tamper_d2h_nth = nth;
+    }
+}

@@ -1,0 +1,117 @@
+"""Host-side logic of libsecure_infer without a GPU: tickets, IV, AAD from
+registered ranges, and OpenSSL record encryption, against the golden records
+and the oracle."""
+from __future__ import annotations
+
+import ctypes as ct
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import det_bytes
+from oracle import gcm as orc
+
+
+@pytest.fixture()
+def host_session(golden_records):
+    from secure_infer_b200 import _native
+    lib = _native.lib()
+    key = (ct.c_uint8 * 16)(*bytes.fromhex(golden_records["key"]))
+    salt = (ct.c_uint8 * 4)(*bytes.fromhex(golden_records["salt"]))
+    assert lib.secure_infer_session_init(-1, key, salt) == 0
+    yield lib
+    lib.secure_infer_session_shutdown()
+
+
+def test_derive_iv_matches_golden(host_session, golden_records):
+    lib = host_session
+    salt = bytes.fromhex(golden_records["salt"])
+    base = (ct.c_uint8 * 16)(*(salt + bytes(12)))
+    out = (ct.c_uint8 * 16)()
+    for row in golden_records["rows"]:
+        assert lib.secure_infer_derive_transfer_iv(base, row["ticket"], 0, out) == 0
+        assert bytes(out).hex() == row["iv"]
+    assert lib.secure_infer_derive_transfer_iv(base, 0, 0, out) == -1   # ticket 0 is reserved
+
+
+def test_aad_from_registered_range(host_session, golden_records):
+    lib = host_session
+    for row in golden_records["rows"]:
+        count = row["count"]
+        pool = np.zeros((row["block"] + 2) * count, np.uint8)
+        lib.secure_infer_register_host_range_ex(pool.ctypes.data, pool.nbytes, row["layer"], row["kind"], count)
+        out = (ct.c_uint8 * 64)()
+        ptr = pool.ctypes.data + row["block"] * count
+        assert lib.secure_infer_build_gcm_aad(ptr, count, 1, row["ticket"], 0, out) == 0
+        assert bytes(out).hex() == row["aad"]
+    # Unregistered memory: layer/kind all-ones, block = address.
+    buf = np.zeros(64, np.uint8)
+    out = (ct.c_uint8 * 64)()
+    assert lib.secure_infer_build_gcm_aad(buf.ctypes.data, 64, 2, 9, 0, out) == 0
+    a = bytes(out)
+    assert a[:4] == b"SFAD" and a[5] == 2 and a[6] == 0xFF and a[8:12] == b"\xff" * 4
+    assert int.from_bytes(a[12:20], "big") == buf.ctypes.data
+    assert lib.secure_infer_build_gcm_aad(buf.ctypes.data, 64, 3, 9, 0, out) == -1
+
+
+def test_encrypt_records_match_golden_layout(host_session, golden_records):
+    lib = host_session
+    row = golden_records["rows"][1]
+    count = row["count"]
+    pool = np.zeros((row["block"] + 1) * count, np.uint8)
+    plain = det_bytes(row["plain_seed"], count)
+    pool[row["block"] * count:(row["block"] + 1) * count] = np.frombuffer(plain, np.uint8)
+    lib.secure_infer_register_host_range_ex(pool.ctypes.data, pool.nbytes, row["layer"], row["kind"], count)
+    stride = lib.secure_infer_record_bytes(count)
+    assert stride == row["record_len"]
+    # Advance the ticket counter so the record gets the golden ticket.
+    for _ in range(row["ticket"] - 1):
+        lib.secure_infer_new_transfer_ticket()
+    rec = np.zeros(stride, np.uint8)
+    srcs = (ct.c_void_p * 1)(pool.ctypes.data + row["block"] * count)
+    tickets = (ct.c_uint64 * 1)()
+    assert lib.secure_infer_h2d_encrypt_records(srcs, count, 1, rec.ctypes.data, stride, tickets) == 0
+    assert tickets[0] == row["ticket"]
+    assert hashlib.sha256(rec.tobytes()).hexdigest() == row["record_sha256"]
+
+
+def test_encrypt_many_records_threads(host_session):
+    lib = host_session
+    count, n = 8192 + 7, 37
+    data = np.frombuffer(det_bytes("many", count * n), np.uint8).reshape(n, count).copy()
+    lib.secure_infer_register_host_range_ex(data.ctypes.data, data.nbytes, 4, 1, count)
+    stride = lib.secure_infer_record_bytes(count)
+    recs = np.zeros((n, stride), np.uint8)
+    srcs = (ct.c_void_p * n)(*[data.ctypes.data + i * count for i in range(n)])
+    tickets = (ct.c_uint64 * n)()
+    assert lib.secure_infer_h2d_encrypt_records(srcs, count, n, recs.ctypes.data, stride, tickets) == 0
+    assert len(set(tickets)) == n and min(tickets) >= 1
+    key, salt = None, None
+    aligned = orc.record_aligned_bytes(count)
+    for i in range(n):
+        aad = recs[i, aligned + 32:].tobytes()
+        assert aad[:4] == b"SFAD" and int.from_bytes(aad[12:20], "big") == i
+        assert int.from_bytes(aad[36:44], "big") == tickets[i]
+    # Decrypt with the oracle (OpenSSL) using the session key/salt of the fixture.
+    import json
+    from conftest import GOLDEN
+    g = json.loads((GOLDEN / "records.json").read_text())
+    key, salt = bytes.fromhex(g["key"]), bytes.fromhex(g["salt"])
+    for i in (0, n // 2, n - 1):
+        iv = orc.derive_transfer_iv(salt, tickets[i])
+        out, ok = orc.host_decrypt_verify(key, iv, recs[i, aligned + 32:].tobytes(), recs[i, :count].tobytes(),
+                                          recs[i, aligned:aligned + 16].tobytes())
+        assert ok == 1 and out == data[i].tobytes()
+
+
+def test_device_entry_points_fail_without_device(host_session):
+    lib = host_session
+    buf = np.zeros(64, np.uint8)
+    srcs = (ct.c_void_p * 1)(buf.ctypes.data)
+    assert lib.secure_infer_h2d_reload_layer(0, srcs, srcs, 1, 64, None, 0, None, None) == -1
+    assert lib.secure_infer_recovery_wait_layer_authentication(0) == 0   # nothing pending
+    assert lib.secure_infer_recovery_wait_job_authentication(5) == -1
+    assert lib.secure_infer_h2d_layer_group_end() == -1                   # unbalanced bracket
+    assert lib.secure_infer_h2d_layer_group_begin(4) == 0
+    assert lib.secure_infer_h2d_layer_group_end() == 0                    # empty group: nothing to flush
