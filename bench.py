@@ -190,7 +190,7 @@ def run_gpu(args, cfg):
     count = [payload[layer][0][0].numel() * payload[layer][0].element_size() for layer in range(L)]
     strides = [nl.record_bytes(c) for c in count]
     drecs, tickets, dsts, codecs = [], [], [], []
-    max_ks = max(((c + 15) // 16 * 16) * n for c in count)
+    max_ks = max(((c + 15) // 16 * 16 + 16) * n for c in count)
     for layer in range(L):
         c, s = count[layer], strides[layer]
         srcs = [payload[layer][k].data_ptr() + i * c for k in range(2) for i in range(B)]
@@ -223,7 +223,7 @@ def run_gpu(args, cfg):
                                                        None, sp) == 0
                 launches += 1
             else:
-                ks_stride = (c + 15) // 16 * 16
+                ks_stride = (c + 15) // 16 * 16 + 16
                 for k in range(2):
                     off = k * B
                     assert lib.secure_infer_verify_records(

@@ -96,8 +96,9 @@ uint64_t secure_infer_codec_packet_bytes(uint32_t heads, uint32_t bits);
  * IV; dsts[i] is the destination (raw bytes, or a bf16 paged-cache block when
  * codec->bits != 0, where the payload is a codec packet).  The AES-CTR
  * keystream is generated on `producer_stream` (null: the session's producer
- * stream) into `keystream` (device, n * round16(count) bytes; null: AES is
- * computed inside the fused kernel) while the caller's
+ * stream) into `keystream` (device, n * (round16(count) + 16) bytes: record i
+ * at i * (round16(count) + 16), its last 16 bytes holding the tag mask
+ * E_K(J0); null: AES is computed inside the fused kernel) while the caller's
  * stream waits only where it needs it; then one fused kernel verifies every
  * tag, XORs, dequantises and scatters, zeroing the destination of any record
  * that fails.  status[i] (device) receives 1/0.  Host arrays are captured at
@@ -108,7 +109,8 @@ int secure_infer_reload_records(uint32_t layer, const void* records, uint64_t re
                                 void* producer_stream);
 
 /* The two halves of secure_infer_reload_records, on one stream:
- * keystream for n tickets into `keystream` (record i at i * round16(count)),
+ * keystream for n tickets into `keystream` (record i at i * (round16(count) + 16),
+ * tag mask E_K(J0) in its last 16 bytes),
  * and the fused verify/XOR/(dequant)/scatter with that keystream ready (null
  * keystream: AES computed inside the fused kernel; codec records need a
  * keystream). */

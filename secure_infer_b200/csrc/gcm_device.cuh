@@ -295,14 +295,20 @@ __device__ inline void build_nibble_table_warp(uint4 m_be, uint4* dst, int lane)
 // Each warp first scales its lanes by H^(32 (7 - w)), warps are XOR-combined,
 // then lane l scales by H^(32 - l): every lane multiplies once, no idle lanes.
 // Segments of one record are joined by Horner with H^kSegBlocks.
+// The layer kernel (raw records with a prefetched keystream) gives each warp
+// 512 blocks, Horner stride H^32, lane scaling H^(32 - l), and joins warp
+// segments with H^512.
 //   tab[e - 1]         H^e,      e = 1..32
-//   tab[30 + k]        H^(32 k), k = 2..8   (tab[38] = H^256, the stride)
-//   tab[39]            H^4096 (segment join)
-constexpr int kGhashTables = 40;
+//   tab[30 + k]        H^(32 k), k = 2..8   (tab[38] = H^256, the CTA stride)
+//   tab[39]            H^4096 (CTA segment join)
+//   tab[40]            H^512 (warp segment join)
+constexpr int kGhashTables = 41;
 constexpr int kThreads = 256;                       // threads per segment CTA
 constexpr int kSegBlocks = 4096;                    // 16-byte blocks per segment
 constexpr int kTabStride = 38;                      // H^256
 constexpr int kTabSeg = 39;                         // H^4096
+constexpr int kWarpSegBlocks = 512;                 // 16-byte blocks per warp segment
+constexpr int kTabWarpSeg = 40;                     // H^512
 
 __host__ __device__ constexpr int tab_pow_small(int e) { return e - 1; }            // H^e, 1 <= e <= 32
 __host__ __device__ constexpr int tab_pow_32k(int k) { return k == 1 ? 31 : 30 + k; }  // H^(32k), 1 <= k <= 8

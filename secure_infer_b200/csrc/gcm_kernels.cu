@@ -149,12 +149,13 @@ __global__ void __launch_bounds__(256) gcm_schedule_kernel(const uint8_t* key, c
             cur = gf_mul_warp<false>(cur, tab_s, lane);
             if (lane == 0) pow_le[tab_pow_32k(k)] = cur;
         }
-        // H^4096 = (H^256)^16 by four squarings.
+        // H^512 and H^4096 by squaring H^256 once and four times.
         for (int i = 0; i < 4; ++i) {
             __syncwarp();
             build_nibble_table_warp(bswap4(cur), tab_s, lane);
             __syncwarp();
             cur = gf_mul_warp<false>(cur, tab_s, lane);
+            if (i == 0 && lane == 0) pow_le[kTabWarpSeg] = cur;
         }
         if (lane == 0) pow_le[kTabSeg] = cur;
     }
@@ -181,14 +182,78 @@ __device__ __forceinline__ void fill_aes_smem(uint32_t* te, uint32_t* rk, const 
     if (threadIdx.x < 44) rk[threadIdx.x] = S->rk[threadIdx.x];
 }
 
-__global__ void __launch_bounds__(256) gcm_ctr_kernel(const __grid_constant__ CtrLaunch L, uint64_t uniform_blocks)
+// Four replicated T-tables (Te_t = rotl(te0, 8t)) laid out so that one PRMT
+// forms a lookup's shared-memory address: byte 0 = lane * 4 (+128 for odd t),
+// byte 1 = the state byte v, byte 2 = t >> 1.  Table pair (Te0, Te1) fills
+// [0, 64 KiB), pair (Te2, Te3) fills [64 KiB, 128 KiB); every lane reads its
+// own bank, so a warp's 32 lookups are one conflict-free wavefront.
+constexpr uint32_t kCtrThreads = 1024;
+constexpr size_t kCtrTableBytes = 131072;
+constexpr size_t kCtrSmem = kCtrTableBytes + 256;
+
+struct Aes4Tables {
+    const uint8_t* smem;
+    uint32_t base[4];
+    __device__ __forceinline__ uint32_t look(int t, uint32_t s, int k) const
+    {
+        const uint32_t addr = __byte_perm(s, base[t], 0x7604u | (static_cast<uint32_t>(k) << 4));
+        return *reinterpret_cast<const uint32_t*>(smem + addr);
+    }
+};
+
+__device__ __forceinline__ uint4 aes128_encrypt_t4(uint4 in, const Aes4Tables& T, const uint32_t* __restrict__ rk)
 {
-    __shared__ __align__(16) uint32_t te[256 * 32];
-    __shared__ uint32_t rk[44];
-    fill_aes_smem(te, rk, L.sched);
+    uint32_t s0 = in.x ^ rk[0], s1 = in.y ^ rk[1], s2 = in.z ^ rk[2], s3 = in.w ^ rk[3];
+#pragma unroll
+    for (int r = 1; r < 10; ++r) {
+        const uint4 k4 = *reinterpret_cast<const uint4*>(rk + 4 * r);
+        const uint32_t t0 = T.look(0, s0, 0) ^ T.look(1, s1, 1) ^ T.look(2, s2, 2) ^ T.look(3, s3, 3) ^ k4.x;
+        const uint32_t t1 = T.look(0, s1, 0) ^ T.look(1, s2, 1) ^ T.look(2, s3, 2) ^ T.look(3, s0, 3) ^ k4.y;
+        const uint32_t t2 = T.look(0, s2, 0) ^ T.look(1, s3, 1) ^ T.look(2, s0, 2) ^ T.look(3, s1, 3) ^ k4.z;
+        const uint32_t t3 = T.look(0, s3, 0) ^ T.look(1, s0, 1) ^ T.look(2, s1, 2) ^ T.look(3, s2, 3) ^ k4.w;
+        s0 = t0; s1 = t1; s2 = t2; s3 = t3;
+    }
+    // Final round: S(x) sits in byte 0 of Te2, byte 1 of Te3, byte 2 of Te0,
+    // byte 3 of Te1; PRMT gathers the four bytes of each output column.
+    const uint4 k4 = *reinterpret_cast<const uint4*>(rk + 40);
+    auto column = [&](uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+        const uint32_t lo = __byte_perm(T.look(2, a, 0), T.look(3, b, 1), 0x0050u);
+        const uint32_t hi = __byte_perm(T.look(0, c, 2), T.look(1, d, 3), 0x7200u);
+        return __byte_perm(lo, hi, 0x7610u);
+    };
+    return make_uint4(column(s0, s1, s2, s3) ^ k4.x, column(s1, s2, s3, s0) ^ k4.y,
+                      column(s2, s3, s0, s1) ^ k4.z, column(s3, s0, s1, s2) ^ k4.w);
+}
+
+__device__ __forceinline__ void fill_aes4_smem(uint8_t* smem, const GcmSchedule* S)
+{
+    uint4* s4 = reinterpret_cast<uint4*>(smem);
+    for (uint32_t i = threadIdx.x; i < kCtrTableBytes / 16; i += blockDim.x) {
+        const uint32_t off = i * 16u;
+        const uint32_t v = (off >> 8) & 0xffu;
+        const uint32_t t = ((off >> 16) << 1) | ((off >> 7) & 1u);
+        const uint32_t val = rotl32(kAesDev.te0[v], static_cast<int>(8 * t));
+        s4[i] = make_uint4(val, val, val, val);
+    }
+    uint32_t* rk = reinterpret_cast<uint32_t*>(smem + kCtrTableBytes);
+    if (threadIdx.x < 44) rk[threadIdx.x] = S->rk[threadIdx.x];
+}
+
+__device__ __forceinline__ Aes4Tables aes4_view(const uint8_t* smem)
+{
+    const uint32_t lane4 = (threadIdx.x & 31u) * 4u;
+    return Aes4Tables{smem, {lane4, lane4 | 128u, 0x10000u | lane4, 0x10000u | lane4 | 128u}};
+}
+
+__global__ void __launch_bounds__(kCtrThreads, 1) gcm_ctr_kernel(const __grid_constant__ CtrLaunch L,
+                                                                  uint64_t uniform_blocks)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    fill_aes4_smem(smem, L.sched);
     __syncthreads();
+    const uint32_t* rk = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
+    const Aes4Tables T = aes4_view(smem);
     const CtrJob* jobs = L.jobs ? L.jobs : L.inl;
-    const SmemAes aes{te, rk, threadIdx.x & 31u};
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
     for (uint64_t gb = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; gb < L.total_blocks;
          gb += stride) {
@@ -207,7 +272,7 @@ __global__ void __launch_bounds__(256) gcm_ctr_kernel(const __grid_constant__ Ct
         const uint64_t c = gb - J.block_first;
         const uint64_t off = c * 16u;
         const uint64_t avail = J.bytes - off;
-        uint4 ks = aes.encrypt(ctr_block_le(J.iv, c));
+        uint4 ks = aes128_encrypt_t4(ctr_block_le(J.iv, c), T, rk);
         const bool aligned = !L.unaligned;
         if (J.in) ks = xor4(ks, (aligned && avail >= 16) ? ldg16(J.in + off) : load_partial16(J.in + off, avail));
         store_block(J.out + off, ks, avail, aligned);
@@ -478,6 +543,153 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
 }
 
 // ----------------------------------------------------------------------------
+// Layer kernels: uniform records, descriptors in kernel parameters.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void layer_iv(uint32_t iv0, uint64_t ticket, uint32_t iv[4])
+{
+    iv[0] = iv0;
+    iv[1] = static_cast<uint32_t>(ticket >> 32);
+    iv[2] = static_cast<uint32_t>(ticket);
+    iv[3] = 2u;
+}
+
+// Keystream of every record plus E_K(J0) in the record's last 16 bytes.
+template <int kCap>
+__global__ void __launch_bounds__(kCtrThreads, 1) gcm_layer_ctr_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    fill_aes4_smem(smem, L.h.sched);
+    __syncthreads();
+    const uint32_t* rk = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
+    const Aes4Tables T = aes4_view(smem);
+    const uint32_t payload_blocks = static_cast<uint32_t>((L.h.count + 15) >> 4);
+    const uint32_t nb = payload_blocks + 1;
+    const uint32_t total = nb * L.h.n;
+    for (uint32_t gb = blockIdx.x * blockDim.x + threadIdx.x; gb < total; gb += gridDim.x * blockDim.x) {
+        const uint32_t r = gb / nb, c = gb - r * nb;
+        uint32_t iv[4];
+        layer_iv(L.h.iv0, L.rec[r].ticket, iv);
+        uint8_t* out = L.h.ks + static_cast<uint64_t>(r) * L.h.ks_stride + 16ull * c;
+        const uint4 in = c == payload_blocks ? j0_block_le(iv) : ctr_block_le(iv, c);
+        const uint4 ks = aes128_encrypt_t4(in, T, rk);
+        if (L.h.unaligned) store_partial16(out, ks, 16); else *reinterpret_cast<uint4*>(out) = ks;
+    }
+}
+
+// Fused verify + XOR + scatter, one warp per 512-block segment (aligned to the
+// END of X = AAD || payload || len; the first segment takes the remainder).
+// Lane l hashes blocks base + l + 32 j with Horner stride H^32 (8x-replicated
+// shared table), prefetching the next two steps; the warp partial is
+// sum_l Y_l H^(32 - l).  The last warp of a record joins the partials with
+// H^512 (unreplicated shared table), XORs the tag mask the keystream kernel
+// left behind, compares, writes the status and zeroes the record's output on
+// a mismatch ("write then gate").
+constexpr uint32_t kLayerThreads = 512;
+constexpr size_t kLayerSmem = kGhashSmem + 512 * sizeof(uint4);
+
+template <int kCap>
+__global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* gtab = reinterpret_cast<uint4*>(smem);
+    uint4* jtab = reinterpret_cast<uint4*>(smem + kGhashSmem);
+    const GcmSchedule* __restrict__ S = L.h.sched;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u;
+    for (uint32_t i = tid; i < 4096; i += kLayerThreads) gtab[i] = __ldg(&S->tab[tab_pow_small(32)][i >> 3]);
+    for (uint32_t i = tid; i < 512; i += kLayerThreads) jtab[i] = __ldg(&S->tab[kTabWarpSeg][i]);
+    __syncthreads();
+
+    const uint64_t count = L.h.count;
+    const bool aligned = L.h.unaligned == 0;
+    const int64_t a_blk = 4;   // 64-byte AAD
+    const int64_t n_blk = static_cast<int64_t>((count + 15) >> 4);
+    const int64_t m = a_blk + n_blk + 1;
+    const uint32_t nseg = L.h.nseg;
+    const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * kWarpSegBlocks;
+    const uint64_t tag_off = ((count + 31) & ~uint64_t(31)) ? ((count + 31) & ~uint64_t(31)) : 32;
+    const uint32_t total = nseg * L.h.n;
+    const uint32_t warps_per_cta = kLayerThreads / 32;
+    const uint4 len_blk = len_block_le(64, count);
+
+    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * warps_per_cta) {
+        const uint32_t r = w / nseg, k = w - r * nseg;
+        const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
+        const uint8_t* aad = in + tag_off + 32;
+        const uint8_t* ksp = L.h.ks + static_cast<uint64_t>(r) * L.h.ks_stride;
+        uint8_t* out = L.rec[r].dst;
+        const int64_t seg_end = len0 + static_cast<int64_t>(k) * kWarpSegBlocks;
+        const int64_t seg_len = k == 0 ? len0 : kWarpSegBlocks;
+        const int J = static_cast<int>((seg_len + 31) / 32);
+        const int64_t base = seg_end - static_cast<int64_t>(J) * 32;
+
+        auto load = [&](int j, uint4& x, uint4& ks) {
+            x = zero4();
+            ks = zero4();
+            const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
+            if (j >= J || i < 0) return;
+            if (i < a_blk) {
+                x = load_partial16(aad + 16 * i, 64 - 16 * i);
+            } else if (i < a_blk + n_blk) {
+                const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
+                const uint64_t avail = count - off;
+                if (aligned && avail >= 16) {
+                    x = ldg16(in + off);
+                    ks = ldg16(ksp + off);
+                } else {
+                    x = load_partial16(in + off, avail);
+                    ks = load_partial16(ksp + off, avail);
+                }
+            } else {
+                x = len_blk;
+            }
+        };
+        uint4 x0, k0, x1, k1;
+        load(0, x0, k0);
+        load(1, x1, k1);
+        uint4 Y = zero4();
+#pragma unroll 1
+        for (int j = 0; j < J; ++j) {
+            uint4 x2, k2;
+            load(j + 2, x2, k2);
+            const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
+            if (i >= a_blk && i < a_blk + n_blk) {
+                const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
+                store_block(out + off, xor4(x0, k0), count - off, aligned);
+            }
+            Y = j == 0 ? x0 : xor4(gf_mul_table<8, false>(Y, gtab, rep), x0);
+            x0 = x1; k0 = k1; x1 = x2; k1 = k2;
+        }
+        Y = gf_mul_table<1, true>(Y, S->tab[tab_pow_small(32 - static_cast<int>(lane))], 0);
+        const uint4 part = warp_xor_reduce(Y);
+
+        __threadfence();
+        __syncwarp();
+        uint32_t last = 0;
+        if (lane == 0) {
+            L.h.partials[w] = part;
+            __threadfence();
+            last = atomicAdd(&L.h.counters[r], 1u) == nseg - 1 ? 1u : 0u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        uint4 acc = __ldcg(&L.h.partials[r * nseg]);
+        for (uint32_t kk = 1; kk < nseg; ++kk)
+            acc = xor4(gf_mul_warp<false>(acc, jtab, lane), __ldcg(&L.h.partials[r * nseg + kk]));
+        const uint4 mask = *reinterpret_cast<const uint4*>(ksp + (L.h.ks_stride - 16));
+        const bool ok = equal4(xor4(acc, mask), load_partial16(in + tag_off, 16));
+        if (lane == 0) {
+            L.h.status[r] = ok ? 1u : 0u;
+            L.h.counters[r] = 0u;
+        }
+        if (!ok) {
+            for (uint64_t off = static_cast<uint64_t>(lane) * 16u; off < count; off += 512u)
+                store_block(out + off, zero4(), count - off, aligned);
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------
 // Writeback quantisation (transport_codec.py:22-42), one thread per group.
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
@@ -612,6 +824,7 @@ namespace {
 
 struct DeviceInfo {
     int sms = 0;
+    bool ctr_attr_set = false;
     int seg_blocks_per_sm[4] = {0, 0, 0, 0};
     bool attr_set[4] = {false, false, false, false};
 };
@@ -693,11 +906,7 @@ int launch_ctr(const CtrLaunch& args, cudaStream_t stream)
         for (uint32_t i = 0; i < args.njobs; ++i) same = same && (jobs[i].bytes + 15) / 16 == b0 && jobs[i].block_first == i * b0;
         uniform = same ? b0 : 0;
     }
-    const uint64_t want = (args.total_blocks + 255) / 256;
-    const uint64_t cap = static_cast<uint64_t>(sms) * 6u;
-    const uint32_t grid = static_cast<uint32_t>(want < cap ? want : cap);
-    gcm_ctr_kernel<<<grid, 256, 0, stream>>>(args, uniform);
-    return cudaGetLastError();
+    return launch_ctr_uniform(args, uniform, stream);
 }
 
 int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStream_t stream)
@@ -708,13 +917,83 @@ int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStrea
     int sms;
     {
         std::lock_guard<std::mutex> lock(g_dev_mu);
-        sms = device_info(dev).sms;
+        DeviceInfo& d = device_info(dev);
+        sms = d.sms;
+        if (!d.ctr_attr_set) {
+            const cudaError_t e = cudaFuncSetAttribute(gcm_ctr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(kCtrSmem));
+            if (e != cudaSuccess) return e;
+            d.ctr_attr_set = true;
+        }
     }
-    const uint64_t want = (args.total_blocks + 255) / 256;
-    const uint64_t cap = static_cast<uint64_t>(sms) * 6u;
+    const uint64_t want = (args.total_blocks + kCtrThreads - 1) / kCtrThreads;
+    const uint64_t cap = static_cast<uint64_t>(sms);
     const uint32_t grid = static_cast<uint32_t>(want < cap ? want : cap);
-    gcm_ctr_kernel<<<grid, 256, 0, stream>>>(args, uniform_blocks);
+    gcm_ctr_kernel<<<grid, kCtrThreads, kCtrSmem, stream>>>(args, uniform_blocks);
     return cudaGetLastError();
+}
+
+uint32_t layer_segments_for(uint64_t count)
+{
+    const uint64_t m = 4u + (count + 15u) / 16u + 1u;
+    const uint64_t n = m / kWarpSegBlocks;
+    return static_cast<uint32_t>(n ? n : 1u);
+}
+
+template <int kCap, class Kernel>
+int layer_launch(Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint32_t threads, size_t smem,
+                 uint32_t items, bool& attr_set, cudaStream_t stream)
+{
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms;
+    {
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        sms = device_info(dev).sms;
+        if (!attr_set) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            attr_set = true;
+        }
+    }
+    LayerLaunch<kCap> L;
+    L.h = h;
+    for (uint32_t i = 0; i < h.n; ++i) L.rec[i] = rec[i];
+    const uint32_t grid = items < static_cast<uint32_t>(sms) ? items : static_cast<uint32_t>(sms);
+    kernel<<<grid, threads, smem, stream>>>(L);
+    return cudaGetLastError();
+}
+
+int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
+{
+    if (h.n == 0) return cudaSuccess;
+    if (h.n > static_cast<uint32_t>(kLayerCapLarge)) return cudaErrorInvalidValue;
+    const uint32_t blocks = static_cast<uint32_t>(((h.count + 15) / 16 + 1) * h.n);
+    const uint32_t items = (blocks + kCtrThreads - 1) / kCtrThreads;
+    static bool set_small[64], set_large[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
+        return layer_launch<kLayerCapSmall>(gcm_layer_ctr_kernel<kLayerCapSmall>, h, rec, kCtrThreads, kCtrSmem, items,
+                                            set_small[dev & 63], stream);
+    return layer_launch<kLayerCapLarge>(gcm_layer_ctr_kernel<kLayerCapLarge>, h, rec, kCtrThreads, kCtrSmem, items,
+                                        set_large[dev & 63], stream);
+}
+
+int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
+{
+    if (h.n == 0) return cudaSuccess;
+    if (h.n > static_cast<uint32_t>(kLayerCapLarge)) return cudaErrorInvalidValue;
+    const uint32_t items = h.nseg * h.n;
+    static bool set_small[64], set_large[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
+        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall>, h, rec, kLayerThreads,
+                                            kLayerSmem, items, set_small[dev & 63], stream);
+    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge>, h, rec, kLayerThreads, kLayerSmem,
+                                        items, set_large[dev & 63], stream);
 }
 
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream)

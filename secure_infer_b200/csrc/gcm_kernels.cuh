@@ -97,6 +97,49 @@ struct EncodeLaunch {
     CodecParams codec;
 };
 
+// A layer of uniform records laid out as C[aligned32(count)] || tag || 0^16 ||
+// AAD64 at `records + i * stride`, IV = {iv0, ticket >> 32, ticket, 2}.  Passed
+// by value in kernel parameters (16 bytes per record), so a launch needs no
+// descriptor copy.  Keystream record i lives at ks + i * ks_stride,
+// ks_stride = round16(count) + 16, with E_K(J0) in its last 16 bytes.
+struct LayerRec {
+    uint8_t* dst;
+    uint64_t ticket;
+};
+
+struct LayerHeader {
+    const GcmSchedule* sched;
+    const uint8_t* records;
+    uint64_t stride;
+    uint64_t count;
+    uint8_t* ks;
+    uint64_t ks_stride;
+    uint32_t* status;
+    uint4* partials;        // [n * nseg]
+    uint32_t* counters;     // [n], zero on entry and exit
+    uint32_t iv0;
+    uint32_t n;
+    uint32_t nseg;
+    uint32_t unaligned;
+};
+
+template <int kCap>
+struct LayerLaunch {
+    LayerHeader h;
+    LayerRec rec[kCap];
+};
+
+constexpr int kLayerCapSmall = 128;
+constexpr int kLayerCapLarge = 1024;
+
+inline uint64_t layer_ks_stride(uint64_t count) { return ((count + 15) & ~uint64_t(15)) + 16; }
+uint32_t layer_segments_for(uint64_t count);
+
+// Keystream (+ tag masks) and fused verify/XOR/scatter for up to
+// kLayerCapLarge records; rec points at n LayerRec entries.
+int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
+int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
+
 // Host-side launchers (gcm_kernels.cu).  Return a cudaError_t value.
 // key may be null (GHASH-only requests); h null -> H = E_K(0^128) on device.
 int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream);
@@ -107,5 +150,6 @@ int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t str
 int launch_encode(const EncodeLaunch& args, cudaStream_t stream);
 size_t schedule_bytes();
 uint32_t segments_for(uint64_t count, uint32_t aad_bytes);
+
 
 }  // namespace sib

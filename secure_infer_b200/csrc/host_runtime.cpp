@@ -528,41 +528,36 @@ bool codec_geometry(const secure_infer_codec* codec, CodecParams* cp, uint64_t* 
 
 bool misaligned(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
 
-// Keystream for n records (stride round16(count)) on `stream`.  Caller holds g_mu.
+// Keystream for n records (stride layer_ks_stride(count), E_K(J0) in each
+// record's last 16 bytes) on `stream`.  Caller holds g_mu.
 int keystream_records_locked(const uint64_t* tickets, uint32_t n, uint64_t count, uint8_t* keystream,
                              cudaStream_t stream)
 {
     if (!g_s.ready || tickets == nullptr || n == 0 || count == 0 || keystream == nullptr) return -1;
-    const uint64_t ks_stride = round16(count);
-    LaunchSlot& slot = g_s.launch[g_s.launch_next];
-    g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
-    if (!ensure_launch_slot(slot, n, 1)) return -1;
-    for (uint32_t i = 0; i < n; ++i) {
-        CtrJob& j = slot.host_jobs[i];
-        j = CtrJob{};
-        j.out = keystream + i * ks_stride;
-        j.bytes = count;
-        iv_words_for(tickets[i], j.iv);
-        j.block_first = static_cast<uint64_t>(i) * (ks_stride / 16);
+    const uint64_t ks_stride = layer_ks_stride(count);
+    std::vector<LayerRec> recs(std::min<uint32_t>(n, kLayerCapLarge));
+    for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
+        const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
+        LayerHeader h{};
+        h.sched = g_s.sched;
+        h.count = count;
+        h.ks = keystream + first * ks_stride;
+        h.ks_stride = ks_stride;
+        h.iv0 = load_be32(g_s.salt);
+        h.n = m;
+        h.unaligned = misaligned(keystream) ? 1u : 0u;
+        for (uint32_t i = 0; i < m; ++i) recs[i] = LayerRec{nullptr, tickets[first + i]};
+        if (launch_layer_keystream(h, recs.data(), stream) != cudaSuccess) return -1;
     }
-    if (!CUDA_OK(cudaMemcpyAsync(slot.dev_jobs, slot.host_jobs, sizeof(CtrJob) * n, cudaMemcpyHostToDevice, stream)))
-        return -1;
-    CtrLaunch K{};
-    K.sched = g_s.sched;
-    K.jobs = slot.dev_jobs;
-    K.njobs = n;
-    K.unaligned = misaligned(keystream) ? 1u : 0u;
-    K.total_blocks = static_cast<uint64_t>(n) * (ks_stride / 16);
-    if (launch_ctr_uniform(K, ks_stride / 16, stream) != cudaSuccess) return -1;
-    cudaEventRecord(slot.free_ev, stream);
-    slot.used = true;
     g_ks_scheduled += n;
     ++g_ks_launches;
     return 0;
 }
 
 // Fused verify / XOR / (dequant) / scatter over n device-resident records.
-// keystream null -> AES inline.  Caller holds g_mu.
+// Raw records with a keystream run on the layer kernel (descriptors in kernel
+// parameters); codec records and keystream-less requests use the CTA-segment
+// kernel.  Caller holds g_mu.
 int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t count, uint32_t n,
                           const uint64_t* tickets, void* const* dsts, const uint8_t* keystream, uint32_t* status,
                           const secure_infer_codec* codec, cudaStream_t stream)
@@ -575,12 +570,48 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
     if (!codec_geometry(codec, &cp, &packet)) return -1;
     if (cp.bits && (count != packet || keystream == nullptr)) return -1;
     const uint64_t aligned = aligned32(count);
-    const uint64_t ks_stride = round16(count);
+    const uint64_t ks_stride = layer_ks_stride(count);
+    const bool rec_misaligned = misaligned(records);
+
+    if (keystream && cp.bits == 0) {
+        const uint32_t nseg = layer_segments_for(count);
+        std::vector<LayerRec> recs(std::min<uint32_t>(n, kLayerCapLarge));
+        for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
+            const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
+            LaunchSlot& slot = g_s.launch[g_s.launch_next];
+            g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
+            if (!ensure_launch_slot(slot, m, nseg * m)) return -1;
+            LayerHeader h{};
+            h.sched = g_s.sched;
+            h.records = records + first * stride;
+            h.stride = stride;
+            h.count = count;
+            h.ks = const_cast<uint8_t*>(keystream) + first * ks_stride;
+            h.ks_stride = ks_stride;
+            h.status = status + first;
+            h.partials = slot.partials;
+            h.counters = slot.counters;
+            h.iv0 = load_be32(g_s.salt);
+            h.n = m;
+            h.nseg = nseg;
+            bool unaligned = rec_misaligned || misaligned(keystream);
+            for (uint32_t i = 0; i < m; ++i) {
+                recs[i] = LayerRec{static_cast<uint8_t*>(dsts[first + i]), tickets[first + i]};
+                unaligned = unaligned || misaligned(dsts[first + i]);
+            }
+            h.unaligned = unaligned ? 1u : 0u;
+            if (launch_layer_verify(h, recs.data(), stream) != cudaSuccess) return -1;
+            cudaEventRecord(slot.free_ev, stream);
+            slot.used = true;
+        }
+        g_ks_hit += n;
+        return 0;
+    }
+
     const uint32_t nseg = segments_for(count, kAadBytes);
     LaunchSlot& slot = g_s.launch[g_s.launch_next];
     g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
     if (!ensure_launch_slot(slot, n, nseg * n)) return -1;
-    const bool rec_misaligned = misaligned(records);
     for (uint32_t i = 0; i < n; ++i) {
         const uint8_t* base = records + i * stride;
         GcmRecord& r = slot.host_recs[i];
@@ -667,7 +698,7 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     StageSlot& slot = g_s.h2d[g_s.h2d_next];
     g_s.h2d_next = (g_s.h2d_next + 1) % g_s.h2d.size();
     if (slot.owner) harvest(*slot.owner);   // statuses leave the slot before reuse
-    if (!ensure_stage(slot, stride * n, round16(count) * n, n)) return nullptr;
+    if (!ensure_stage(slot, stride * n, layer_ks_stride(count) * n, n)) return nullptr;
     if (slot.done) cudaEventSynchronize(slot.done);
 
     std::vector<uint64_t> tickets(n);

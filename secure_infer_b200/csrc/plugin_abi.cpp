@@ -101,11 +101,11 @@ int run_records(cudaStream_t stream, const void* key, const void* h, GcmRecord* 
     bool inline_aes = false;
     for (uint32_t i = 0; i < n; ++i) {
         if (recs[i].aad_bytes > (1u << 20)) return -1;
+        const bool needs_ks = recs[i].op == kOpDecrypt || recs[i].op == kOpEncrypt;
+        inline_aes = inline_aes || (needs_ks && recs[i].ks == nullptr);
         recs[i].seg_first = total;
         recs[i].nseg = segments_for(recs[i].count, recs[i].aad_bytes);
         total += recs[i].nseg;
-        const bool needs_ks = recs[i].op == kOpDecrypt || recs[i].op == kOpEncrypt;
-        inline_aes = inline_aes || (needs_ks && recs[i].ks == nullptr);
         L.inl[i] = recs[i];
     }
     if (total > kScratchSegments) return -1;

@@ -183,7 +183,7 @@ def test_reload_records_device_resident(nl):
     srcs = nl._ptrs(host.data_ptr() + i * count for i in range(n))
     assert lib.secure_infer_h2d_encrypt_records(srcs, count, n, recs.data_ptr(), stride, tickets) == 0
     drecs = recs.cuda()
-    ks = torch.empty(n * count, dtype=torch.uint8, device="cuda")
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
     status = torch.zeros(n, dtype=torch.int32, device="cuda")
     dest = torch.zeros((n, 128, heads, 128), dtype=torch.bfloat16, device="cuda")
     order = list(reversed(range(n)))
