@@ -294,24 +294,25 @@ __device__ inline void build_nibble_table_warp(uint4 m_be, uint4* dst, int lane)
 //   S_seg = sum_t Y_t * H^(256 - t),  t = 32 w + l,  256 - t = 32 (7 - w) + (32 - l).
 // Each warp first scales its lanes by H^(32 (7 - w)), warps are XOR-combined,
 // then lane l scales by H^(32 - l): every lane multiplies once, no idle lanes.
-// Segments of one record are joined by Horner with H^kSegBlocks.
-// The layer kernel (raw records with a prefetched keystream) gives each warp
-// 512 blocks, Horner stride H^32, lane scaling H^(32 - l), and joins warp
-// segments with H^512.
+// CTA segments of one record are joined by Horner with H^kSegBlocks.
+// The layer kernel gives each warp a segment of 32 k blocks (k = 1..64,
+// chosen per launch so the segments fill the GPU's warps once), Horner stride
+// H^32, a two-stage lane combine (lane 8q + r: H^(8 - r) then H^(24 - 8q)),
+// and joins the segments with H^(32 k).
 //   tab[e - 1]         H^e,      e = 1..32
-//   tab[30 + k]        H^(32 k), k = 2..8   (tab[38] = H^256, the CTA stride)
-//   tab[39]            H^4096 (CTA segment join)
-//   tab[40]            H^512 (warp segment join)
-constexpr int kGhashTables = 41;
+//   tab[30 + k]        H^(32 k), k = 2..64  (tab[38] = H^256, the CTA stride)
+//   tab[95]            H^4096 (CTA segment join)
+// rep32 / lane8 hold shared-memory-ready copies: H^32 replicated 8x, and the
+// eight tables H^(8 - r) interleaved by r, both in the (p, v, r) layout.
+constexpr int kGhashTables = 96;
 constexpr int kThreads = 256;                       // threads per segment CTA
 constexpr int kSegBlocks = 4096;                    // 16-byte blocks per segment
 constexpr int kTabStride = 38;                      // H^256
-constexpr int kTabSeg = 39;                         // H^4096
-constexpr int kWarpSegBlocks = 512;                 // 16-byte blocks per warp segment
-constexpr int kTabWarpSeg = 40;                     // H^512
+constexpr int kTabSeg = 95;                         // H^4096
+constexpr int kMaxWarpSegSteps = 64;                // layer kernel: segment <= 64 x 32 blocks
 
-__host__ __device__ constexpr int tab_pow_small(int e) { return e - 1; }            // H^e, 1 <= e <= 32
-__host__ __device__ constexpr int tab_pow_32k(int k) { return k == 1 ? 31 : 30 + k; }  // H^(32k), 1 <= k <= 8
+__host__ __device__ constexpr int tab_pow_small(int e) { return e - 1; }             // H^e, 1 <= e <= 32
+__host__ __device__ constexpr int tab_pow_32k(int k) { return k == 1 ? 31 : 30 + k; }  // H^(32k), 1 <= k <= 64
 
 struct __align__(16) GcmSchedule {
     uint32_t rk[44];          // AES-128 round keys, LE layout
@@ -322,6 +323,8 @@ struct __align__(16) GcmSchedule {
     uint32_t reserved[2];
     uint4 h_le;               // hash subkey H (memory bytes, LE words)
     uint4 tab[kGhashTables][32 * 16];
+    uint4 rep32[32 * 16 * 8]; // H^32, entry (p, v) replicated: [(p * 16 + v) * 8 + r]
+    uint4 lane8[32 * 16 * 8]; // H^(8 - r) at [(p * 16 + v) * 8 + r], r = 0..7
 };
 
 }  // namespace sib

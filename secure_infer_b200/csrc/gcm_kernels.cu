@@ -142,25 +142,29 @@ __global__ void __launch_bounds__(256) gcm_schedule_kernel(const uint8_t* key, c
             if (lane == 0) pow_le[tab_pow_small(e)] = cur;
         }
         __syncwarp();
-        // H^64..H^256 with H^32's table.
+        // H^64..H^2048 with H^32's table.
         build_nibble_table_warp(bswap4(cur), tab_s, lane);
         __syncwarp();
-        for (int k = 2; k <= 8; ++k) {
+        for (int k = 2; k <= 64; ++k) {
             cur = gf_mul_warp<false>(cur, tab_s, lane);
             if (lane == 0) pow_le[tab_pow_32k(k)] = cur;
         }
-        // H^512 and H^4096 by squaring H^256 once and four times.
-        for (int i = 0; i < 4; ++i) {
-            __syncwarp();
-            build_nibble_table_warp(bswap4(cur), tab_s, lane);
-            __syncwarp();
-            cur = gf_mul_warp<false>(cur, tab_s, lane);
-            if (i == 0 && lane == 0) pow_le[kTabWarpSeg] = cur;
-        }
+        // H^4096 = (H^2048)^2.
+        __syncwarp();
+        build_nibble_table_warp(bswap4(cur), tab_s, lane);
+        __syncwarp();
+        cur = gf_mul_warp<false>(cur, tab_s, lane);
         if (lane == 0) pow_le[kTabSeg] = cur;
     }
     __syncthreads();
     for (int t = warp; t < kGhashTables; t += 8) build_nibble_table_warp(bswap4(pow_le[t]), S->tab[t], lane);
+    __syncthreads();
+    // Shared-memory-ready layouts for the layer kernel.
+    for (int i = tid; i < 32 * 16 * 8; i += 256) {
+        const int e = i >> 3, r = i & 7;
+        S->rep32[i] = S->tab[tab_pow_small(32)][e];
+        S->lane8[i] = S->tab[tab_pow_small(8 - r)][e];
+    }
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -503,9 +507,15 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
         if (warp == 0) {
             uint4 acc = zero4();
             if (op != kOpXorOnly) {
-                for (uint32_t kk = 0; kk < nseg; ++kk) {
-                    const uint4 p = __ldcg(&L.partials[R.seg_first + kk]);
-                    acc = kk == 0 ? p : xor4(gf_mul_warp<true>(acc, S->tab[kTabSeg], lane), p);
+                for (uint32_t k0 = 0; k0 < nseg; k0 += 32) {
+                    const uint32_t cnt = nseg - k0 < 32 ? nseg - k0 : 32;
+                    const uint4 mine = lane < cnt ? __ldcg(&L.partials[R.seg_first + k0 + lane]) : zero4();
+                    for (uint32_t kk = 0; kk < cnt; ++kk) {
+                        const uint4 p = make_uint4(
+                            __shfl_sync(0xffffffffu, mine.x, kk), __shfl_sync(0xffffffffu, mine.y, kk),
+                            __shfl_sync(0xffffffffu, mine.z, kk), __shfl_sync(0xffffffffu, mine.w, kk));
+                        acc = (k0 == 0 && kk == 0) ? p : xor4(gf_mul_warp<true>(acc, S->tab[kTabSeg], lane), p);
+                    }
                 }
             }
             if (lane == 0) {
@@ -576,49 +586,67 @@ __global__ void __launch_bounds__(kCtrThreads, 1) gcm_layer_ctr_kernel(const __g
     }
 }
 
-// Fused verify + XOR + scatter, one warp per 512-block segment (aligned to the
-// END of X = AAD || payload || len; the first segment takes the remainder).
-// Lane l hashes blocks base + l + 32 j with Horner stride H^32 (8x-replicated
-// shared table), prefetching the next two steps; the warp partial is
-// sum_l Y_l H^(32 - l).  The last warp of a record joins the partials with
-// H^512 (unreplicated shared table), XORs the tag mask the keystream kernel
-// left behind, compares, writes the status and zeroes the record's output on
-// a mismatch ("write then gate").
-constexpr uint32_t kLayerThreads = 512;
-constexpr size_t kLayerSmem = kGhashSmem + 512 * sizeof(uint4);
+// Fused verify + XOR + scatter.  One CTA of 8 warps per SM; each warp takes
+// one segment of 32 k blocks (k <= 64, chosen per launch so the segments fill
+// the warps once) of X = AAD || payload || len, aligned to the END of X (the
+// first segment takes the shorter remainder).  Lane l = 8 q + r hashes blocks
+// base + l + 32 j with Horner stride H^32 (8x-replicated shared table),
+// prefetching four steps ahead.  The segment partial
+//   sum_l Y_l H^(32 - l),  32 - l = (8 - r) + (24 - 8 q)
+// is formed in shared memory: every lane scales by H^(8 - r) (eight tables
+// interleaved like replicas, so a quarter-warp is conflict-free), quarters
+// XOR-reduce and scale by H^(24 - 8 q), then the quarters XOR-reduce.  The
+// last warp of a record joins the partials with H^(32 k), XORs the tag mask
+// the keystream kernel left behind, compares, writes the status and zeroes
+// the record's output on a mismatch ("write then gate").
+constexpr uint32_t kLayerThreads = 256;
+constexpr uint32_t kLayerWarps = kLayerThreads / 32;
+constexpr size_t kLayerSmem = 2 * kGhashSmem + 4 * 512 * sizeof(uint4);   // rep32, lane8, H^8/16/24, join
+constexpr int kLayerPrefetch = 4;
 
 template <int kCap>
 __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* gtab = reinterpret_cast<uint4*>(smem);
-    uint4* jtab = reinterpret_cast<uint4*>(smem + kGhashSmem);
+    uint4* ltab = reinterpret_cast<uint4*>(smem + kGhashSmem);
+    uint4* qtab = reinterpret_cast<uint4*>(smem + 2 * kGhashSmem);   // [3][512]: H^8, H^16, H^24
+    uint4* jtab = qtab + 3 * 512;
     const GcmSchedule* __restrict__ S = L.h.sched;
-    const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u;
-    for (uint32_t i = tid; i < 4096; i += kLayerThreads) gtab[i] = __ldg(&S->tab[tab_pow_small(32)][i >> 3]);
-    for (uint32_t i = tid; i < 512; i += kLayerThreads) jtab[i] = __ldg(&S->tab[kTabWarpSeg][i]);
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u, quarter = lane >> 3;
+    const uint32_t seg_steps = L.h.seg_steps;
+    for (uint32_t i = tid; i < 4096; i += kLayerThreads) {
+        gtab[i] = __ldg(&S->rep32[i]);
+        ltab[i] = __ldg(&S->lane8[i]);
+    }
+    for (uint32_t i = tid; i < 512; i += kLayerThreads) {
+        qtab[i] = __ldg(&S->tab[tab_pow_small(8)][i]);
+        qtab[512 + i] = __ldg(&S->tab[tab_pow_small(16)][i]);
+        qtab[1024 + i] = __ldg(&S->tab[tab_pow_small(24)][i]);
+        jtab[i] = __ldg(&S->tab[tab_pow_32k(seg_steps)][i]);
+    }
     __syncthreads();
 
     const uint64_t count = L.h.count;
     const bool aligned = L.h.unaligned == 0;
+    const int64_t seg_blocks = 32 * static_cast<int64_t>(seg_steps);
     const int64_t a_blk = 4;   // 64-byte AAD
     const int64_t n_blk = static_cast<int64_t>((count + 15) >> 4);
     const int64_t m = a_blk + n_blk + 1;
     const uint32_t nseg = L.h.nseg;
-    const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * kWarpSegBlocks;
+    const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * seg_blocks;
     const uint64_t tag_off = ((count + 31) & ~uint64_t(31)) ? ((count + 31) & ~uint64_t(31)) : 32;
     const uint32_t total = nseg * L.h.n;
-    const uint32_t warps_per_cta = kLayerThreads / 32;
     const uint4 len_blk = len_block_le(64, count);
 
-    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * warps_per_cta) {
+    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * kLayerWarps) {
         const uint32_t r = w / nseg, k = w - r * nseg;
         const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
         const uint8_t* aad = in + tag_off + 32;
         const uint8_t* ksp = L.h.ks + static_cast<uint64_t>(r) * L.h.ks_stride;
         uint8_t* out = L.rec[r].dst;
-        const int64_t seg_end = len0 + static_cast<int64_t>(k) * kWarpSegBlocks;
-        const int64_t seg_len = k == 0 ? len0 : kWarpSegBlocks;
+        const int64_t seg_end = len0 + static_cast<int64_t>(k) * seg_blocks;
+        const int64_t seg_len = k == 0 ? len0 : seg_blocks;
         const int J = static_cast<int>((seg_len + 31) / 32);
         const int64_t base = seg_end - static_cast<int64_t>(J) * 32;
 
@@ -628,7 +656,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
             const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
             if (j >= J || i < 0) return;
             if (i < a_blk) {
-                x = load_partial16(aad + 16 * i, 64 - 16 * i);
+                x = aligned ? ldg16(aad + 16 * i) : load_partial16(aad + 16 * i, 16);
             } else if (i < a_blk + n_blk) {
                 const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
                 const uint64_t avail = count - off;
@@ -643,24 +671,31 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
                 x = len_blk;
             }
         };
-        uint4 x0, k0, x1, k1;
-        load(0, x0, k0);
-        load(1, x1, k1);
+        uint4 xq[kLayerPrefetch], kq[kLayerPrefetch];
+#pragma unroll
+        for (int u = 0; u < kLayerPrefetch; ++u) load(u, xq[u], kq[u]);
         uint4 Y = zero4();
 #pragma unroll 1
         for (int j = 0; j < J; ++j) {
-            uint4 x2, k2;
-            load(j + 2, x2, k2);
+            const uint4 x0 = xq[0], k0 = kq[0];
+#pragma unroll
+            for (int u = 0; u + 1 < kLayerPrefetch; ++u) { xq[u] = xq[u + 1]; kq[u] = kq[u + 1]; }
+            load(j + kLayerPrefetch, xq[kLayerPrefetch - 1], kq[kLayerPrefetch - 1]);
             const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
             if (i >= a_blk && i < a_blk + n_blk) {
                 const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
                 store_block(out + off, xor4(x0, k0), count - off, aligned);
             }
             Y = j == 0 ? x0 : xor4(gf_mul_table<8, false>(Y, gtab, rep), x0);
-            x0 = x1; k0 = k1; x1 = x2; k1 = k2;
         }
-        Y = gf_mul_table<1, true>(Y, S->tab[tab_pow_small(32 - static_cast<int>(lane))], 0);
-        const uint4 part = warp_xor_reduce(Y);
+        // Two-stage lane combine in shared memory.
+        Y = gf_mul_table<8, false>(Y, ltab, rep);                       // * H^(8 - r)
+        Y = xor4(Y, shfl_xor4(Y, 1));
+        Y = xor4(Y, shfl_xor4(Y, 2));
+        Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
+        if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
+        Y = xor4(Y, shfl_xor4(Y, 8));
+        const uint4 part = xor4(Y, shfl_xor4(Y, 16));
 
         __threadfence();
         __syncwarp();
@@ -673,9 +708,18 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
-        uint4 acc = __ldcg(&L.h.partials[r * nseg]);
-        for (uint32_t kk = 1; kk < nseg; ++kk)
-            acc = xor4(gf_mul_warp<false>(acc, jtab, lane), __ldcg(&L.h.partials[r * nseg + kk]));
+        // Join the record's partials: lanes load 32 at a time in parallel, then
+        // Horner with H^(32 k) from registers (shuffle broadcast).
+        uint4 acc = zero4();
+        for (uint32_t k0 = 0; k0 < nseg; k0 += 32) {
+            const uint32_t cnt = nseg - k0 < 32 ? nseg - k0 : 32;
+            const uint4 mine = lane < cnt ? __ldcg(&L.h.partials[r * nseg + k0 + lane]) : zero4();
+            for (uint32_t kk = 0; kk < cnt; ++kk) {
+                const uint4 p = make_uint4(__shfl_sync(0xffffffffu, mine.x, kk), __shfl_sync(0xffffffffu, mine.y, kk),
+                                           __shfl_sync(0xffffffffu, mine.z, kk), __shfl_sync(0xffffffffu, mine.w, kk));
+                acc = (k0 == 0 && kk == 0) ? p : xor4(gf_mul_warp<false>(acc, jtab, lane), p);
+            }
+        }
         const uint4 mask = *reinterpret_cast<const uint4*>(ksp + (L.h.ks_stride - 16));
         const bool ok = equal4(xor4(acc, mask), load_partial16(in + tag_off, 16));
         if (lane == 0) {
@@ -891,13 +935,6 @@ int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool nee
 int launch_ctr(const CtrLaunch& args, cudaStream_t stream)
 {
     if (args.total_blocks == 0) return cudaSuccess;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int sms;
-    {
-        std::lock_guard<std::mutex> lock(g_dev_mu);
-        sms = device_info(dev).sms;
-    }
     const CtrJob* jobs = args.jobs ? nullptr : args.inl;
     uint64_t uniform = 0;
     if (jobs) {
@@ -933,16 +970,30 @@ int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStrea
     return cudaGetLastError();
 }
 
-uint32_t layer_segments_for(uint64_t count)
+void layer_segments_for(uint64_t count, uint32_t n, uint32_t* seg_steps, uint32_t* nseg)
 {
+    // Pick the segment length (32 k blocks, k <= 16) so that n * nseg fills
+    // the resident warps once (2 CTAs x 16 warps per SM); long layers fall
+    // back to the longest segment.
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        sms = device_info(dev).sms;
+    }
     const uint64_t m = 4u + (count + 15u) / 16u + 1u;
-    const uint64_t n = m / kWarpSegBlocks;
-    return static_cast<uint32_t>(n ? n : 1u);
+    const uint64_t warps = static_cast<uint64_t>(sms) * kLayerWarps;
+    const uint64_t per_record = warps / (n ? n : 1u);
+    uint64_t k = per_record ? (m + 32u * per_record - 1) / (32u * per_record) : kMaxWarpSegSteps;
+    if (k < 1) k = 1;
+    if (k > static_cast<uint64_t>(kMaxWarpSegSteps)) k = kMaxWarpSegSteps;
+    *seg_steps = static_cast<uint32_t>(k);
+    *nseg = static_cast<uint32_t>((m + 32u * k - 1) / (32u * k));
 }
 
 template <int kCap, class Kernel>
 int layer_launch(Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint32_t threads, size_t smem,
-                 uint32_t items, bool& attr_set, cudaStream_t stream)
+                 uint32_t items, bool& attr_set, cudaStream_t stream, uint32_t ctas_per_sm = 1)
 {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -960,7 +1011,8 @@ int layer_launch(Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint3
     LayerLaunch<kCap> L;
     L.h = h;
     for (uint32_t i = 0; i < h.n; ++i) L.rec[i] = rec[i];
-    const uint32_t grid = items < static_cast<uint32_t>(sms) ? items : static_cast<uint32_t>(sms);
+    const uint32_t cap = static_cast<uint32_t>(sms) * ctas_per_sm;
+    const uint32_t grid = items < cap ? items : cap;
     kernel<<<grid, threads, smem, stream>>>(L);
     return cudaGetLastError();
 }
@@ -989,11 +1041,13 @@ int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t 
     static bool set_small[64], set_large[64];
     int dev = 0;
     cudaGetDevice(&dev);
+    // One CTA of 8 warps per SM (160 KiB of tables in shared memory).
     if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
         return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall>, h, rec, kLayerThreads,
-                                            kLayerSmem, items, set_small[dev & 63], stream);
+                                            kLayerSmem, (items + kLayerWarps - 1) / kLayerWarps,
+                                            set_small[dev & 63], stream, 1);
     return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge>, h, rec, kLayerThreads, kLayerSmem,
-                                        items, set_large[dev & 63], stream);
+                                        (items + kLayerWarps - 1) / kLayerWarps, set_large[dev & 63], stream, 1);
 }
 
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream)

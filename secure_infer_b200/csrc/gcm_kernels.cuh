@@ -119,7 +119,8 @@ struct LayerHeader {
     uint32_t* counters;     // [n], zero on entry and exit
     uint32_t iv0;
     uint32_t n;
-    uint32_t nseg;
+    uint32_t nseg;          // segments per record
+    uint32_t seg_steps;     // segment = 32 * seg_steps blocks (1..16)
     uint32_t unaligned;
 };
 
@@ -133,7 +134,8 @@ constexpr int kLayerCapSmall = 128;
 constexpr int kLayerCapLarge = 1024;
 
 inline uint64_t layer_ks_stride(uint64_t count) { return ((count + 15) & ~uint64_t(15)) + 16; }
-uint32_t layer_segments_for(uint64_t count);
+// Segment length (seg_steps) and count (nseg) per record for a launch of n records.
+void layer_segments_for(uint64_t count, uint32_t n, uint32_t* seg_steps, uint32_t* nseg);
 
 // Keystream (+ tag masks) and fused verify/XOR/scatter for up to
 // kLayerCapLarge records; rec points at n LayerRec entries.

@@ -574,10 +574,11 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
     const bool rec_misaligned = misaligned(records);
 
     if (keystream && cp.bits == 0) {
-        const uint32_t nseg = layer_segments_for(count);
         std::vector<LayerRec> recs(std::min<uint32_t>(n, kLayerCapLarge));
         for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
             const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
+            uint32_t seg_steps = 0, nseg = 0;
+            layer_segments_for(count, m, &seg_steps, &nseg);
             LaunchSlot& slot = g_s.launch[g_s.launch_next];
             g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
             if (!ensure_launch_slot(slot, m, nseg * m)) return -1;
@@ -594,6 +595,7 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
             h.iv0 = load_be32(g_s.salt);
             h.n = m;
             h.nseg = nseg;
+            h.seg_steps = seg_steps;
             bool unaligned = rec_misaligned || misaligned(keystream);
             for (uint32_t i = 0; i < m; ++i) {
                 recs[i] = LayerRec{static_cast<uint8_t*>(dsts[first + i]), tickets[first + i]};
