@@ -80,6 +80,56 @@ __device__ __forceinline__ void store_block(uint8_t* p, uint4 v, uint64_t avail,
 
 __device__ __forceinline__ bool equal4(uint4 a, uint4 b) { return is_zero4(xor4(a, b)); }
 
+// 16-byte global -> shared asynchronous copy (bypasses registers and L1).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
+{
+    const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(gmem_src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// mbarrier + bulk (TMA, non-multicast) global -> shared copy of this GPU's
+// own memory.  Used to fetch tables in the background of a kernel's main loop.
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init_expect(uint64_t* bar, uint32_t tx_bytes)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n"
+                 "fence.mbarrier_init.release.cluster;\n"
+                 "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(tx_bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(smem_dst)),
+                 "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Waits for phase `parity` of the barrier; gives up after a bounded number of
+// polls (returns false) so a lost completion can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity)
+{
+    for (uint32_t it = 0; it < (1u << 22); ++it) {
+        uint32_t done;
+        asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
+                     : "=r"(done)
+                     : "r"(smem_u32(bar)), "r"(parity)
+                     : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
 // ----------------------------------------------------------------------------
 // Key schedule: one CTA of 8 warps.  Reuses the previous build when the key
 // (and H) bytes are unchanged, so per-call plugin launches stay cheap.
@@ -615,17 +665,25 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
     const GcmSchedule* __restrict__ S = L.h.sched;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u, quarter = lane >> 3;
     const uint32_t seg_steps = L.h.seg_steps;
-    for (uint32_t i = tid; i < 4096; i += kLayerThreads) {
-        gtab[i] = __ldg(&S->rep32[i]);
-        ltab[i] = __ldg(&S->lane8[i]);
+    __shared__ __align__(8) uint64_t tables_bar;
+    // Tables used only after a warp's main loop (lane, quarter and join
+    // tables, 96 KiB) stream in by bulk copy while the main loop runs.
+    if (tid == 0) {
+        mbar_init_expect(&tables_bar, 65536u + 4u * 8192u);
+        bulk_g2s(ltab, S->lane8, 65536u, &tables_bar);
+        bulk_g2s(qtab, S->tab[tab_pow_small(8)], 8192u, &tables_bar);
+        bulk_g2s(qtab + 512, S->tab[tab_pow_small(16)], 8192u, &tables_bar);
+        bulk_g2s(qtab + 1024, S->tab[tab_pow_small(24)], 8192u, &tables_bar);
+        bulk_g2s(jtab, S->tab[tab_pow_32k(seg_steps)], 8192u, &tables_bar);
     }
-    for (uint32_t i = tid; i < 512; i += kLayerThreads) {
-        qtab[i] = __ldg(&S->tab[tab_pow_small(8)][i]);
-        qtab[512 + i] = __ldg(&S->tab[tab_pow_small(16)][i]);
-        qtab[1024 + i] = __ldg(&S->tab[tab_pow_small(24)][i]);
-        jtab[i] = __ldg(&S->tab[tab_pow_32k(seg_steps)][i]);
+    // The Horner table H^32 is replicated 8x from its 8 KiB original.
+    for (uint32_t e = tid; e < 512; e += kLayerThreads) {
+        const uint4 v = __ldg(&S->tab[tab_pow_small(32)][e]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) gtab[e * 8 + r] = v;
     }
     __syncthreads();
+    bool tables_ready = false;
 
     const uint64_t count = L.h.count;
     const bool aligned = L.h.unaligned == 0;
@@ -688,7 +746,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
             }
             Y = j == 0 ? x0 : xor4(gf_mul_table<8, false>(Y, gtab, rep), x0);
         }
-        // Two-stage lane combine in shared memory.
+        // Two-stage lane combine in shared memory.  If the table copy never
+        // completes the partial is poisoned, so the record fails closed
+        // (status 0, output zeroed) instead of waiting forever.
+        if (!tables_ready) tables_ready = mbar_wait_bounded(&tables_bar, 0);
+        if (!tables_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
         Y = gf_mul_table<8, false>(Y, ltab, rep);                       // * H^(8 - r)
         Y = xor4(Y, shfl_xor4(Y, 1));
         Y = xor4(Y, shfl_xor4(Y, 2));
@@ -897,6 +959,9 @@ int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cud
             cudaError_t e = cudaFuncSetAttribute(gcm_segment_kernel<A, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(max_smem));
             if (e != cudaSuccess) return e;
+            e = cudaFuncSetAttribute(gcm_segment_kernel<A, C>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
+            if (e != cudaSuccess) return e;
             d.attr_set[variant] = true;
         }
         sms = d.sms;
@@ -957,8 +1022,11 @@ int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStrea
         DeviceInfo& d = device_info(dev);
         sms = d.sms;
         if (!d.ctr_attr_set) {
-            const cudaError_t e = cudaFuncSetAttribute(gcm_ctr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       static_cast<int>(kCtrSmem));
+            cudaError_t e = cudaFuncSetAttribute(gcm_ctr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kCtrSmem));
+            if (e != cudaSuccess) return e;
+            e = cudaFuncSetAttribute(gcm_ctr_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
             d.ctr_attr_set = true;
         }
@@ -1002,8 +1070,13 @@ int layer_launch(Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint3
         std::lock_guard<std::mutex> lock(g_dev_mu);
         sms = device_info(dev).sms;
         if (!attr_set) {
-            const cudaError_t e =
+            cudaError_t e =
                 cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            // Same (maximum) shared-memory carve-out for every large-table
+            // kernel, so back-to-back launches never reconfigure L1.
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
             attr_set = true;
         }
