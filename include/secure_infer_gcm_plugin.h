@@ -121,6 +121,25 @@ int secure_infer_aicpu_gcm_xor_only_do(void* stream, void* ciphertext, void* key
                                        void* status_output, uint64_t bytes, uint32_t iv_word0, uint32_t iv_word1,
                                        uint32_t iv_word2, uint32_t iv_word3);
 
+/* Allocation-free variant of secure_infer_aicpu_gcm_decrypt_verify_aad_do.
+ * No counterpart in the reference.  For callers that cannot call cudaMalloc
+ * (code inside an allocator or memory budget it does not own, or a path that
+ * must never pay for a device allocation): the entry points above allocate a
+ * per-stream scratch area on first use, this one keeps its scratch (key
+ * schedule, segment partials, arrival counter; about 0.9 MiB, held by every
+ * GPU that loads the library until exit) in a fixed device array.  Same
+ * arguments, meaning and results; returns -2 with a message on stderr when
+ * bytes > 16 MiB or aad_bytes > 4096.  The first call on a device looks up the
+ * array's address, so make it before any stream capture.  Every call shares
+ * the array: calls whose work overlaps on the GPU race and must be serialised
+ * by the caller. */
+int secure_infer_aicpu_gcm_decrypt_verify_aad_noalloc_do(void* stream, void* ciphertext, void* key,
+                                                         void* hash_subkey, void* expected_tag,
+                                                         void* plaintext_output, void* status_output,
+                                                         uint64_t bytes, uint32_t iv_word0, uint32_t iv_word1,
+                                                         uint32_t iv_word2, uint32_t iv_word3, void* aad,
+                                                         uint64_t aad_bytes);
+
 #ifdef __cplusplus
 }
 #endif

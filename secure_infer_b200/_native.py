@@ -36,6 +36,7 @@ PLUGIN_SIGNATURES = {
     "secure_infer_aicpu_gcm_verify_only_aad_do": ([P] * 6 + [U64] + [U32] * 4 + [P, U64], I32),
     "secure_infer_aicpu_gcm_verify_xor_batch_do": ([P, P, P, PP, PP, PP, PP, PP, PP, U64, U64, U32P, U32], I32),
     "secure_infer_aicpu_gcm_xor_only_do": ([P] * 8 + [U64] + [U32] * 4, I32),
+    "secure_infer_aicpu_gcm_decrypt_verify_aad_noalloc_do": ([P] * 7 + [U64] + [U32] * 4 + [P, U64], I32),
 }
 
 CHARP = ct.c_char_p

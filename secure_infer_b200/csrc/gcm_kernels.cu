@@ -1152,3 +1152,119 @@ int launch_auth_gate(uint8_t* data, const uint32_t* status, uint64_t bytes, cuda
 }
 
 }  // namespace sib
+
+// ----------------------------------------------------------------------------
+// Allocation-free entry point.
+// ----------------------------------------------------------------------------
+// Some callers cannot call cudaMalloc: code running under an allocator or
+// memory budget they do not own, or paths that must never pay for a first-call
+// device allocation.  The plugin entry points above allocate one scratch area
+// per stream on first use.  secure_infer_aicpu_gcm_decrypt_verify_aad_noalloc_do
+// runs the same key-schedule and fused decrypt/verify kernels with their
+// scratch in the fixed array below instead, so it never allocates.
+#include <cstdio>
+
+namespace sib {
+namespace {
+
+constexpr uint64_t kNoAllocMaxBytes = 16ull << 20;   // payload bytes per call
+constexpr uint64_t kNoAllocMaxAad = 4096;             // AAD bytes per call
+constexpr uint32_t kNoAllocMaxSegs =
+    static_cast<uint32_t>((kNoAllocMaxAad / 16 + kNoAllocMaxBytes / 16 + 1) / kSegBlocks + 1);
+
+struct NoAllocScratch {
+    GcmSchedule sched;                 // key schedule (rebuilt when key or H change)
+    uint4 partials[kNoAllocMaxSegs];   // per-segment GHASH partials
+    uint32_t counters[4];              // segment arrival counter (must start at zero)
+};
+
+}  // namespace
+}  // namespace sib
+
+// The scratch itself: about 0.9 MiB, held by every GPU that loads this library
+// until the process exits.  Static device memory starts zeroed.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[sizeof(sib::NoAllocScratch)];
+
+namespace sib {
+namespace {
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code the
+// array's name is only a host-side stand-in; the address comes from the
+// runtime, once per device, with that device current.
+NoAllocScratch* noalloc_scratch()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
+        g_noalloc_ptr[dev] = p;
+    }
+    return static_cast<NoAllocScratch*>(g_noalloc_ptr[dev]);
+}
+
+}  // namespace
+}  // namespace sib
+
+// Same arguments, meaning and results as
+// secure_infer_aicpu_gcm_decrypt_verify_aad_do; returns -2 (with a message on
+// stderr) when bytes exceed 16 MiB or aad_bytes exceed 4096.  The first call on
+// a device looks up the scratch address, so make it before any stream capture.
+// All calls share the one scratch array: calls whose work overlaps on the GPU
+// (for example on two streams at once) race and must be serialised by the
+// caller.
+extern "C" __attribute__((visibility("default"))) int secure_infer_aicpu_gcm_decrypt_verify_aad_noalloc_do(
+    void* stream, void* ciphertext, void* key, void* hash_subkey, void* expected_tag, void* plaintext_output,
+    void* status_output, uint64_t bytes, uint32_t iv_word0, uint32_t iv_word1, uint32_t iv_word2, uint32_t iv_word3,
+    void* aad, uint64_t aad_bytes)
+{
+    using namespace sib;
+    if (ciphertext == nullptr || key == nullptr || hash_subkey == nullptr || expected_tag == nullptr ||
+        plaintext_output == nullptr || status_output == nullptr || bytes == 0 || (aad_bytes != 0 && aad == nullptr))
+        return -1;
+    if (bytes > kNoAllocMaxBytes || aad_bytes > kNoAllocMaxAad) {
+        std::fprintf(stderr,
+                     "secure_infer_aicpu_gcm_decrypt_verify_aad_noalloc_do: %llu payload / %llu AAD bytes exceed "
+                     "the fixed scratch limit of %llu / %llu bytes\n",
+                     static_cast<unsigned long long>(bytes), static_cast<unsigned long long>(aad_bytes),
+                     static_cast<unsigned long long>(kNoAllocMaxBytes),
+                     static_cast<unsigned long long>(kNoAllocMaxAad));
+        return -2;
+    }
+    NoAllocScratch* scratch = noalloc_scratch();
+    if (scratch == nullptr) return -1;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The arrival counter must start at zero; the kernel leaves it zero, but a
+    // call that never completed would not, so clear it every time.
+    if (cudaMemsetAsync(scratch->counters, 0, sizeof(scratch->counters), s) != cudaSuccess) return -1;
+    if (launch_schedule(&scratch->sched, key, hash_subkey, true, s) != cudaSuccess) return -1;
+
+    GcmRecord r{};
+    r.op = kOpDecrypt;
+    r.in = static_cast<const uint8_t*>(ciphertext);
+    r.aad = static_cast<const uint8_t*>(aad_bytes ? aad : nullptr);
+    r.aad_bytes = static_cast<uint32_t>(aad_bytes);
+    r.tag_in = static_cast<const uint8_t*>(expected_tag);
+    r.out = static_cast<uint8_t*>(plaintext_output);
+    r.status = static_cast<uint32_t*>(status_output);
+    r.count = bytes;
+    r.iv[0] = iv_word0; r.iv[1] = iv_word1; r.iv[2] = iv_word2; r.iv[3] = iv_word3;
+    const auto misaligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; };
+    if (misaligned(ciphertext) || misaligned(plaintext_output)) r.flags |= kRecUnaligned;
+    r.seg_first = 0;
+    r.nseg = segments_for(bytes, r.aad_bytes);
+
+    SegmentLaunch L{};
+    L.sched = &scratch->sched;
+    L.recs = nullptr;
+    L.inl[0] = r;
+    L.nrec = 1;
+    L.total_segs = r.nseg;
+    L.partials = scratch->partials;
+    L.counters = scratch->counters;
+    return launch_segments(L, true, s) == cudaSuccess ? 0 : -1;
+}
