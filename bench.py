@@ -65,6 +65,24 @@ def layer_bits(mode, layer, layers):
     return 0 if mode == "none" else (8 if mode == "int8" or (mode == "mixed" and layer < math.ceil(layers / 3)) else 4)
 
 
+def rank_session_material(rank: int) -> tuple[bytes, bytes]:
+    """Seeded per-rank AES-128 key and 4-byte IV salt: every rank (TP shard)
+    owns an independent session, as each reference rank does."""
+    key = bytes((rank * 31 + i * 7 + 3) & 0xFF for i in range(16))
+    salt = bytes((rank * 13 + i + 1) & 0xFF for i in range(4))
+    return key, salt
+
+
+def max_over_ranks(x: float, dist=None, device: str = "cuda") -> float:
+    """Largest value of x over all ranks (the job's time is its slowest rank)."""
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -176,8 +194,7 @@ def run_gpu(args, cfg):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    key = bytes((rank * 31 + i * 7 + 3) & 0xFF for i in range(16))
-    salt = bytes((rank * 13 + i + 1) & 0xFF for i in range(4))
+    key, salt = rank_session_material(rank)
     nl.Session(local, key, salt)
     L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
     W = build_workload(cfg, rank, torch, nl)
@@ -244,12 +261,6 @@ def run_gpu(args, cfg):
         if dist is not None:
             dist.barrier()
 
-    def max_over_ranks(x):
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     # ---- device-resident throughput (value) ----
     for _ in range(args.warmup):
@@ -272,7 +283,7 @@ def run_gpu(args, cfg):
         end.record(stream)
         torch.cuda.synchronize()
     barrier()
-    dev_ms = max_over_ranks(start.elapsed_time(end))
+    dev_ms = max_over_ranks(start.elapsed_time(end), dist)
     ks_us = [evs[k][layer][0].elapsed_time(evs[k][layer][1]) * 1e3 for k in range(args.steps) for layer in range(L)]
     vf_us = [evs[k][layer][1].elapsed_time(evs[k][layer][2]) * 1e3 for k in range(args.steps) for layer in range(L)]
     assert int(status.min().item()) == 1
@@ -311,7 +322,7 @@ def run_gpu(args, cfg):
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), dist) / args.steps
     e2e_value = world * algo / (e2e_ms * 1e-3) / 1e9
     h2d_bytes = sum(strides[layer] * n for layer in range(L))
     d2h_bytes = L * n * 4
