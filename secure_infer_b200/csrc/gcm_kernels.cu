@@ -654,7 +654,80 @@ constexpr uint32_t kLayerWarps = kLayerThreads / 32;
 constexpr size_t kLayerSmem = 2 * kGhashSmem + 4 * 512 * sizeof(uint4);   // rep32, lane8, H^8/16/24, join
 constexpr int kLayerPrefetch = 4;
 
-template <int kCap>
+// Decrypted fp32 parameters (scale or low) of a codec packet: N consecutive
+// words at byte `off`, each C ^ KS (16-byte aligned).
+template <int N>
+__device__ __forceinline__ void load_params(const uint8_t* in, const uint8_t* ks, uint64_t off, float (&v)[32])
+{
+#pragma unroll
+    for (int k = 0; k < N; k += 4) {
+        const uint4 c = ldg16(in + off + 4 * k), m = ldg16(ks + off + 4 * k);
+        v[k] = __uint_as_float(c.x ^ m.x);
+        v[k + 1] = __uint_as_float(c.y ^ m.y);
+        v[k + 2] = __uint_as_float(c.z ^ m.z);
+        v[k + 3] = __uint_as_float(c.w ^ m.w);
+    }
+}
+
+// One 16-byte block of quantised bytes (16 int8 or 32 int4 elements) of
+// packet block c -> bf16 at out + 2 e0: v = fp32(q * scale) then fp32(v + low),
+// round-to-nearest-even bf16 (optimized_decode.py:18-25).  For K (64-token
+// groups per channel) the lane's 16/32 consecutive channel parameters are
+// kept in registers, keyed by their first index, and reloaded only when the
+// token group or channel set changes.
+template <int N>
+__device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecParams& cp, const uint8_t* in,
+                                              const uint8_t* ksp, uint8_t* out, uint32_t& key, float (&sc)[32],
+                                              float (&lo)[32])
+{
+    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+    float q[N];
+    if constexpr (N == 16) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) q[k] = static_cast<float>((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            const uint32_t byte = (w[k >> 2] >> (8 * (k & 3))) & 0xffu;
+            q[2 * k] = static_cast<float>(byte & 0xfu);
+            q[2 * k + 1] = static_cast<float>(byte >> 4);
+        }
+    }
+    const uint32_t e0 = static_cast<uint32_t>(c) * N;
+    float v[N];
+    if (cp.kind == 0) {
+        const uint32_t hd = cp.heads * 128u;
+        const uint32_t sidx0 = (e0 / (64u * hd)) * hd + (e0 % hd);
+        if (sidx0 != key) {
+            load_params<N>(in, ksp, cp.qb + 4ull * sidx0, sc);
+            load_params<N>(in, ksp, cp.qb + cp.sb + 4ull * sidx0, lo);
+            key = sidx0;
+        }
+#pragma unroll
+        for (int k = 0; k < N; ++k) v[k] = __fadd_rn(__fmul_rn(q[k], sc[k]), lo[k]);
+    } else {
+        const uint64_t so = cp.qb + 4ull * (e0 / 64u), lo_off = so + cp.sb;
+        const float s1 = __uint_as_float(__ldg(reinterpret_cast<const uint32_t*>(in + so)) ^
+                                         __ldg(reinterpret_cast<const uint32_t*>(ksp + so)));
+        const float l1 = __uint_as_float(__ldg(reinterpret_cast<const uint32_t*>(in + lo_off)) ^
+                                         __ldg(reinterpret_cast<const uint32_t*>(ksp + lo_off)));
+#pragma unroll
+        for (int k = 0; k < N; ++k) v[k] = __fadd_rn(__fmul_rn(q[k], s1), l1);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + 2u * static_cast<size_t>(e0));
+#pragma unroll
+    for (int k = 0; k < N; k += 8) {
+        uint4 o;
+        __nv_bfloat162 b;
+        b = __floats2bfloat162_rn(v[k + 0], v[k + 1]); o.x = *reinterpret_cast<uint32_t*>(&b);
+        b = __floats2bfloat162_rn(v[k + 2], v[k + 3]); o.y = *reinterpret_cast<uint32_t*>(&b);
+        b = __floats2bfloat162_rn(v[k + 4], v[k + 5]); o.z = *reinterpret_cast<uint32_t*>(&b);
+        b = __floats2bfloat162_rn(v[k + 6], v[k + 7]); o.w = *reinterpret_cast<uint32_t*>(&b);
+        dst[k / 8] = o;
+    }
+}
+
+template <int kCap, bool kCodec>
 __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -696,6 +769,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
     const uint64_t tag_off = ((count + 31) & ~uint64_t(31)) ? ((count + 31) & ~uint64_t(31)) : 32;
     const uint32_t total = nseg * L.h.n;
     const uint4 len_blk = len_block_le(64, count);
+    const CodecParams cp = L.h.codec;
+    // On a tag mismatch the record's destination is zeroed: raw bytes, or the
+    // whole bf16 block a codec packet decodes into.
+    const uint64_t out_bytes = kCodec ? 2ull * 128u * cp.heads * 128u : count;
 
     for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * kLayerWarps) {
         const uint32_t r = w / nseg, k = w - r * nseg;
@@ -733,6 +810,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
 #pragma unroll
         for (int u = 0; u < kLayerPrefetch; ++u) load(u, xq[u], kq[u]);
         uint4 Y = zero4();
+        uint32_t pkey = ~0u;          // codec: index of the cached K parameters
+        float psc[32], plo[32];
 #pragma unroll 1
         for (int j = 0; j < J; ++j) {
             const uint4 x0 = xq[0], k0 = kq[0];
@@ -742,7 +821,16 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
             const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
             if (i >= a_blk && i < a_blk + n_blk) {
                 const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
-                store_block(out + off, xor4(x0, k0), count - off, aligned);
+                if constexpr (kCodec) {
+                    if (off < cp.qb) {
+                        if (cp.bits == 8)
+                            layer_dequant<16>(xor4(x0, k0), off >> 4, cp, in, ksp, out, pkey, psc, plo);
+                        else
+                            layer_dequant<32>(xor4(x0, k0), off >> 4, cp, in, ksp, out, pkey, psc, plo);
+                    }
+                } else {
+                    store_block(out + off, xor4(x0, k0), count - off, aligned);
+                }
             }
             Y = j == 0 ? x0 : xor4(gf_mul_table<8, false>(Y, gtab, rep), x0);
         }
@@ -789,8 +877,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
             L.h.counters[r] = 0u;
         }
         if (!ok) {
-            for (uint64_t off = static_cast<uint64_t>(lane) * 16u; off < count; off += 512u)
-                store_block(out + off, zero4(), count - off, aligned);
+            for (uint64_t off = static_cast<uint64_t>(lane) * 16u; off < out_bytes; off += 512u)
+                store_block(out + off, zero4(), out_bytes - off, aligned);
         }
     }
 }
@@ -1115,12 +1203,21 @@ int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t 
     int dev = 0;
     cudaGetDevice(&dev);
     // One CTA of 8 warps per SM (160 KiB of tables in shared memory).
-    if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
-        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall>, h, rec, kLayerThreads,
-                                            kLayerSmem, (items + kLayerWarps - 1) / kLayerWarps,
-                                            set_small[dev & 63], stream, 1);
-    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge>, h, rec, kLayerThreads, kLayerSmem,
-                                        (items + kLayerWarps - 1) / kLayerWarps, set_large[dev & 63], stream, 1);
+    static bool set_small_c[64], set_large_c[64];
+    const uint32_t grid = (items + kLayerWarps - 1) / kLayerWarps;
+    const bool small = h.n <= static_cast<uint32_t>(kLayerCapSmall);
+    if (h.codec.bits) {
+        if (small)
+            return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, true>, h, rec, kLayerThreads,
+                                                kLayerSmem, grid, set_small_c[dev & 63], stream, 1);
+        return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, true>, h, rec, kLayerThreads,
+                                            kLayerSmem, grid, set_large_c[dev & 63], stream, 1);
+    }
+    if (small)
+        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, false>, h, rec, kLayerThreads,
+                                            kLayerSmem, grid, set_small[dev & 63], stream, 1);
+    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, false>, h, rec, kLayerThreads,
+                                        kLayerSmem, grid, set_large[dev & 63], stream, 1);
 }
 
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream)

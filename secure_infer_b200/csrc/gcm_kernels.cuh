@@ -120,8 +120,9 @@ struct LayerHeader {
     uint32_t iv0;
     uint32_t n;
     uint32_t nseg;          // segments per record
-    uint32_t seg_steps;     // segment = 32 * seg_steps blocks (1..16)
+    uint32_t seg_steps;     // segment = 32 * seg_steps blocks (1..64)
     uint32_t unaligned;
+    CodecParams codec;      // bits 0: raw payload; 8/4: codec packets dequantised into bf16 blocks
 };
 
 template <int kCap>

@@ -573,7 +573,7 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
     const uint64_t ks_stride = layer_ks_stride(count);
     const bool rec_misaligned = misaligned(records);
 
-    if (keystream && cp.bits == 0) {
+    if (keystream) {
         std::vector<LayerRec> recs(std::min<uint32_t>(n, kLayerCapLarge));
         for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
             const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
@@ -596,11 +596,15 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
             h.n = m;
             h.nseg = nseg;
             h.seg_steps = seg_steps;
+            h.codec = cp;
             bool unaligned = rec_misaligned || misaligned(keystream);
             for (uint32_t i = 0; i < m; ++i) {
                 recs[i] = LayerRec{static_cast<uint8_t*>(dsts[first + i]), tickets[first + i]};
                 unaligned = unaligned || misaligned(dsts[first + i]);
             }
+            // Codec packets are read with 16-byte loads and decoded with
+            // 16-byte stores: they need aligned records, keystream and blocks.
+            if (cp.bits && unaligned) return -1;
             h.unaligned = unaligned ? 1u : 0u;
             if (launch_layer_verify(h, recs.data(), stream) != cudaSuccess) return -1;
             cudaEventRecord(slot.free_ev, stream);
