@@ -80,10 +80,14 @@ int secure_infer_h2d_encrypt_records(const void* const* srcs, uint64_t count, ui
 
 typedef struct {
     uint32_t bits;    /* 0 = KV_CODEC none (raw bf16 bytes), 8 = int8, 4 = int4 */
-    uint32_t kind;    /* 0 = K, 1 = V (grouping axis) */
+    uint32_t kind;    /* 0 = K, 1 = V (grouping axis); reloads also take
+                         SECURE_INFER_KIND_KV: n even, records [0, n/2) are K
+                         packets and [n/2, n) V packets of the same layer */
     uint32_t heads;   /* KV heads per 128-token block; head_dim is 128 */
     uint32_t layer;   /* written into the packet header on encode */
 } secure_infer_codec;
+
+#define SECURE_INFER_KIND_KV 2u
 
 /* Packet row bytes for (heads, bits): q || scale || low || int32[4], padded
  * to 16 (transport_codec.py:35-41).  0 for bits not in {8, 4}. */
@@ -98,11 +102,13 @@ uint64_t secure_infer_codec_packet_bytes(uint32_t heads, uint32_t bits);
  * keystream is generated on `producer_stream` (null: the session's producer
  * stream) into `keystream` (device, n * (round16(count) + 16) bytes: record i
  * at i * (round16(count) + 16), its last 16 bytes holding the tag mask
- * E_K(J0); null: AES is computed inside the fused kernel) while the caller's
- * stream waits only where it needs it; then one fused kernel verifies every
- * tag, XORs, dequantises and scatters, zeroing the destination of any record
- * that fails.  status[i] (device) receives 1/0.  Host arrays are captured at
- * call time. */
+ * E_K(J0); null: AES is computed inside the fused kernel); on a separate
+ * producer stream the keystream launch waits for the work the caller's stream
+ * had queued (so one keystream buffer may serve consecutive calls), and the
+ * caller's stream waits for the keystream.  Then one fused kernel verifies
+ * every tag, XORs, dequantises and scatters, zeroing the destination of any
+ * record that fails.  status[i] (device) receives 1/0.  Host arrays are
+ * captured at call time. */
 int secure_infer_reload_records(uint32_t layer, const void* records, uint64_t record_stride, uint64_t count,
                                 uint32_t n, const uint64_t* tickets, void* const* dsts, void* keystream,
                                 uint32_t* status, const secure_infer_codec* codec, void* stream,

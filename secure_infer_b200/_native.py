@@ -88,6 +88,10 @@ class Codec(ct.Structure):
     """secure_infer_codec (include/secure_infer.h)."""
     _fields_ = [("bits", ct.c_uint32), ("kind", ct.c_uint32), ("heads", ct.c_uint32), ("layer", ct.c_uint32)]
 
+
+# SECURE_INFER_KIND_KV: a reload of 2n records, K packets first, V packets after.
+KIND_KV = 2
+
 _lib: ct.CDLL | None = None
 
 

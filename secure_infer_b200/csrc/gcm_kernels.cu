@@ -676,9 +676,9 @@ __device__ __forceinline__ void load_params(const uint8_t* in, const uint8_t* ks
 // kept in registers, keyed by their first index, and reloaded only when the
 // token group or channel set changes.
 template <int N>
-__device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecParams& cp, const uint8_t* in,
-                                              const uint8_t* ksp, uint8_t* out, uint32_t& key, float (&sc)[32],
-                                              float (&lo)[32])
+__device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecParams& cp, uint32_t kind,
+                                              const uint8_t* in, const uint8_t* ksp, uint8_t* out, uint32_t& key,
+                                              float (&sc)[32], float (&lo)[32])
 {
     const uint32_t w[4] = {p.x, p.y, p.z, p.w};
     float q[N];
@@ -695,7 +695,7 @@ __device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecPa
     }
     const uint32_t e0 = static_cast<uint32_t>(c) * N;
     float v[N];
-    if (cp.kind == 0) {
+    if (kind == 0) {
         const uint32_t hd = cp.heads * 128u;
         const uint32_t sidx0 = (e0 / (64u * hd)) * hd + (e0 % hd);
         if (sidx0 != key) {
@@ -812,6 +812,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
         uint4 Y = zero4();
         uint32_t pkey = ~0u;          // codec: index of the cached K parameters
         float psc[32], plo[32];
+        const uint32_t kind = r >= L.h.v_first ? 1u : 0u;
 #pragma unroll 1
         for (int j = 0; j < J; ++j) {
             const uint4 x0 = xq[0], k0 = kq[0];
@@ -824,9 +825,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
                 if constexpr (kCodec) {
                     if (off < cp.qb) {
                         if (cp.bits == 8)
-                            layer_dequant<16>(xor4(x0, k0), off >> 4, cp, in, ksp, out, pkey, psc, plo);
+                            layer_dequant<16>(xor4(x0, k0), off >> 4, cp, kind, in, ksp, out, pkey, psc, plo);
                         else
-                            layer_dequant<32>(xor4(x0, k0), off >> 4, cp, in, ksp, out, pkey, psc, plo);
+                            layer_dequant<32>(xor4(x0, k0), off >> 4, cp, kind, in, ksp, out, pkey, psc, plo);
                     }
                 } else {
                     store_block(out + off, xor4(x0, k0), count - off, aligned);

@@ -123,6 +123,7 @@ struct LayerHeader {
     uint32_t seg_steps;     // segment = 32 * seg_steps blocks (1..64)
     uint32_t unaligned;
     CodecParams codec;      // bits 0: raw payload; 8/4: codec packets dequantised into bf16 blocks
+    uint32_t v_first;       // codec: records r >= v_first decode as V packets, the rest as K
 };
 
 template <int kCap>

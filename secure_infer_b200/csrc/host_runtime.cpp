@@ -360,6 +360,9 @@ struct Session {
     uint8_t salt[4] = {};
     GcmSchedule* sched = nullptr;
     cudaStream_t producer = nullptr;
+    // Cross-stream fences of reload_records when the keystream is produced on
+    // another stream than the one that consumes it.
+    cudaEvent_t consumed_ev = nullptr, produced_ev = nullptr;
     std::atomic<uint64_t> next_ticket{1};
     std::mutex replay_mu;
     std::unordered_set<uint64_t> replay;
@@ -509,12 +512,13 @@ void iv_words_for(uint64_t ticket, uint32_t w[4])
     w[3] = 2u;
 }
 
-bool codec_geometry(const secure_infer_codec* codec, CodecParams* cp, uint64_t* packet)
+bool codec_geometry(const secure_infer_codec* codec, CodecParams* cp, uint64_t* packet, bool kv_pair = false)
 {
     *cp = CodecParams{};
     *packet = 0;
     if (codec == nullptr || codec->bits == 0) return true;
-    if ((codec->bits != 8 && codec->bits != 4) || codec->kind > 1 || codec->heads == 0 || codec->heads > 16)
+    const uint32_t max_kind = kv_pair ? SECURE_INFER_KIND_KV : 1u;
+    if ((codec->bits != 8 && codec->bits != 4) || codec->kind > max_kind || codec->heads == 0 || codec->heads > 16)
         return false;
     const uint64_t elements = 128ull * codec->heads * 128ull;
     cp->bits = codec->bits;
@@ -567,8 +571,9 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
         return -1;
     CodecParams cp;
     uint64_t packet = 0;
-    if (!codec_geometry(codec, &cp, &packet)) return -1;
+    if (!codec_geometry(codec, &cp, &packet, true)) return -1;
     if (cp.bits && (count != packet || keystream == nullptr)) return -1;
+    if (cp.bits && cp.kind == SECURE_INFER_KIND_KV && (n & 1u)) return -1;
     const uint64_t aligned = aligned32(count);
     const uint64_t ks_stride = layer_ks_stride(count);
     const bool rec_misaligned = misaligned(records);
@@ -597,6 +602,9 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
             h.nseg = nseg;
             h.seg_steps = seg_steps;
             h.codec = cp;
+            // Records of this chunk from index v_first on are V packets.
+            const uint32_t v_global = cp.kind == SECURE_INFER_KIND_KV ? n / 2 : (cp.kind == 1 ? 0u : n);
+            h.v_first = v_global > first ? std::min<uint32_t>(v_global - first, m) : 0u;
             bool unaligned = rec_misaligned || misaligned(keystream);
             for (uint32_t i = 0; i < m; ++i) {
                 recs[i] = LayerRec{static_cast<uint8_t*>(dsts[first + i]), tickets[first + i]};
@@ -664,14 +672,17 @@ int reload_records_locked(uint32_t layer, const uint8_t* records, uint64_t strid
 {
     (void)layer;
     if (keystream) {
+        // The caller may reuse one keystream buffer for every call: on a
+        // separate producer stream the keystream launch first waits for the
+        // consumer stream's earlier work (the previous verify reading it).
+        const bool cross = producer != stream;
+        if (cross && (!CUDA_OK(cudaEventRecord(g_s.consumed_ev, stream)) ||
+                      !CUDA_OK(cudaStreamWaitEvent(producer, g_s.consumed_ev, 0))))
+            return -1;
         if (keystream_records_locked(tickets, n, count, keystream, producer) != 0) return -1;
-        if (producer != stream) {
-            cudaEvent_t ev = nullptr;
-            if (!CUDA_OK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming))) return -1;
-            cudaEventRecord(ev, producer);
-            cudaStreamWaitEvent(stream, ev, 0);
-            cudaEventDestroy(ev);
-        }
+        if (cross && (!CUDA_OK(cudaEventRecord(g_s.produced_ev, producer)) ||
+                      !CUDA_OK(cudaStreamWaitEvent(stream, g_s.produced_ev, 0))))
+            return -1;
     }
     return verify_records_locked(records, stride, count, n, tickets, dsts, keystream, status, codec, stream);
 }
@@ -699,7 +710,8 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     if (!g_s.ready || srcs == nullptr || dsts == nullptr || n == 0 || count == 0) return nullptr;
     CodecParams cp;
     uint64_t packet = 0;
-    if (!codec_geometry(codec, &cp, &packet)) return nullptr;
+    if (!codec_geometry(codec, &cp, &packet, true)) return nullptr;
+    if (cp.bits && cp.kind == SECURE_INFER_KIND_KV && (n & 1u)) return nullptr;
     const uint64_t stride = record_bytes(count);
     StageSlot& slot = g_s.h2d[g_s.h2d_next];
     g_s.h2d_next = (g_s.h2d_next + 1) % g_s.h2d.size();
@@ -1017,6 +1029,9 @@ void shutdown_locked()
     g_s.sched = nullptr;
     if (g_s.producer) cudaStreamDestroy(g_s.producer);
     g_s.producer = nullptr;
+    if (g_s.consumed_ev) cudaEventDestroy(g_s.consumed_ev);
+    if (g_s.produced_ev) cudaEventDestroy(g_s.produced_ev);
+    g_s.consumed_ev = g_s.produced_ev = nullptr;
     g_s.ready = false;
 }
 
@@ -1055,7 +1070,9 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
     if (!CUDA_OK(cudaMalloc(&g_s.sched, sib::schedule_bytes())) ||
         !CUDA_OK(cudaMemset(g_s.sched, 0, sib::schedule_bytes())) || !CUDA_OK(cudaMalloc(&dkey, 16)) ||
         !CUDA_OK(cudaMemcpy(dkey, key16, 16, cudaMemcpyHostToDevice)) ||
-        !CUDA_OK(cudaStreamCreateWithFlags(&g_s.producer, cudaStreamNonBlocking))) {
+        !CUDA_OK(cudaStreamCreateWithFlags(&g_s.producer, cudaStreamNonBlocking)) ||
+        !CUDA_OK(cudaEventCreateWithFlags(&g_s.consumed_ev, cudaEventDisableTiming)) ||
+        !CUDA_OK(cudaEventCreateWithFlags(&g_s.produced_ev, cudaEventDisableTiming))) {
         cudaFree(dkey);
         return -1;
     }

@@ -127,31 +127,37 @@ class NativeTransfer:
         self.layer = 0
 
     def single_layer_kv_transfer(self, payload, destination, stream=None):
+        """K and V of the layer go out as one reload of 2n records (K records
+        first), so both kinds share one staged copy and one fused kernel."""
         host, mapping = payload
         layer = self.layer
         src_idx = mapping[:, 0].tolist()
         dst_idx = mapping[:, 1].tolist()
         n = len(src_idx)
-        for kind, (src, dst) in enumerate(zip(host, destination)):
-            heads = dst.shape[2]
-            if self.mode == "none":
-                codec = None
-                count = src[0].numel() * src.element_size()
-            else:
-                bits = layer_bits(self.mode, layer, self.layers)
-                codec = _native.Codec(bits, kind, heads, layer)
-                count = packet_bytes(heads, bits)
+        heads = destination[0].shape[2]
+        if self.mode == "none":
+            codec = None
+            counts = {src[0].numel() * src.element_size() for src in host}
+            if len(counts) != 1:
+                raise ValueError("K and V blocks differ in size")
+            count = counts.pop()
+        else:
+            bits = layer_bits(self.mode, layer, self.layers)
+            codec = _native.Codec(bits, _native.KIND_KV, heads, layer)
+            count = packet_bytes(heads, bits)
+            for src in host:
                 if src.shape[1] != count:
                     raise ValueError(f"packet width {src.shape[1]} != {count}")
+        srcs, dsts = [], []
+        for src, dst in zip(host, destination):
             stride = src.stride(0) * src.element_size()
             dstride = dst.stride(0) * dst.element_size()
-            srcs = _ptrs(src.data_ptr() + i * stride for i in src_idx)
-            dsts = _ptrs(dst.data_ptr() + i * dstride for i in dst_idx)
-            rc = self.lib.secure_infer_h2d_reload_layer(layer, srcs, dsts, n, count,
-                                                        ct.byref(codec) if codec else None, 0, None,
-                                                        _stream(stream))
-            if rc != 0:
-                raise RuntimeError(f"secure_infer_h2d_reload_layer failed for layer {layer} kind {kind}")
+            srcs += [src.data_ptr() + i * stride for i in src_idx]
+            dsts += [dst.data_ptr() + i * dstride for i in dst_idx]
+        rc = self.lib.secure_infer_h2d_reload_layer(layer, _ptrs(srcs), _ptrs(dsts), 2 * n, count,
+                                                    ct.byref(codec) if codec else None, 0, None, _stream(stream))
+        if rc != 0:
+            raise RuntimeError(f"secure_infer_h2d_reload_layer failed for layer {layer}")
         self.layer += 1
 
     def wait_for_layer_load(self, layer: int):

@@ -96,6 +96,36 @@ def test_reload_codec_matches_reference_decode(nl, heads, kind, bits):
     assert not got[others].any()
 
 
+@pytest.mark.parametrize("heads", [1, 2])
+@pytest.mark.parametrize("bits", [8, 4])
+def test_reload_codec_kv_pair_matches_reference_decode(nl, heads, bits):
+    """K and V packets of one layer reloaded as one 2n-record request
+    (SECURE_INFER_KIND_KV), both decoded bit-exact like decode_into."""
+    g = load_codec(heads)
+    layer = 2 if bits == 8 else 21
+    lib = nl._native.lib()
+    dst_idx = [int(i) for i in g["dst_idx"]]
+    dest = [torch.zeros((6, 128, heads, 128), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    packets, srcs, dsts = [], [], []
+    for kind in range(2):
+        pk = torch.from_numpy(g[f"packet_k{kind}_b{bits}"]).pin_memory()
+        nl.register_host_range(pk, layer, kind)
+        packets.append(pk)
+        b, width = pk.shape
+        srcs += [pk.data_ptr() + i * width for i in range(b)]
+        dsts += [dest[kind].data_ptr() + i * dest[kind].stride(0) * 2 for i in dst_idx]
+    codec = nl._native.Codec(bits, nl._native.KIND_KV, heads, layer)
+    assert lib.secure_infer_h2d_reload_layer(layer, nl._ptrs(srcs), nl._ptrs(dsts), len(srcs), width,
+                                             ct.byref(codec), 0, None, nl._stream()) == 0
+    assert lib.secure_infer_recovery_wait_layer_authentication(layer) == 0
+    for kind in range(2):
+        got = u16(dest[kind])
+        assert np.array_equal(got[dst_idx], g[f"dest_k{kind}_b{bits}"]), kind
+    # An odd record count cannot be split into K and V halves.
+    assert lib.secure_infer_h2d_reload_layer(layer, nl._ptrs(srcs), nl._ptrs(dsts), len(srcs) - 1, width,
+                                             ct.byref(codec), 0, None, nl._stream()) == -1
+
+
 @pytest.mark.parametrize("mode", ["int8", "int4", "mixed"])
 def test_native_transfer_codec_layers(nl, mode):
     """NativeTransfer over several layers with the per-layer bit split."""
@@ -196,6 +226,40 @@ def test_reload_records_device_resident(nl):
         torch.cuda.synchronize()
         assert status.cpu().tolist() == [1] * n
         assert torch.equal(dest.cpu()[order], host)
+
+
+def test_reload_records_shared_keystream_across_streams(nl):
+    """Consecutive reloads that share one keystream buffer, with the keystream
+    on the session's producer stream: each layer's output must be its own."""
+    heads, n, layers = 2, 6, 4
+    lib = nl._native.lib()
+    count = 128 * heads * 128 * 2
+    stride = nl.record_bytes(count)
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
+    side = torch.cuda.Stream()
+    hosts, drecs, tks, dests, status = [], [], [], [], torch.zeros((layers, n), dtype=torch.int32, device="cuda")
+    for layer in range(layers):
+        host = bf16_random((n, 128, heads, 128), 300 + layer).pin_memory()
+        nl.register_host_range(host, 40 + layer, 0)
+        recs = torch.zeros((n, stride), dtype=torch.uint8).pin_memory()
+        tk = (ct.c_uint64 * n)()
+        srcs = nl._ptrs(host.data_ptr() + i * count for i in range(n))
+        assert lib.secure_infer_h2d_encrypt_records(srcs, count, n, recs.data_ptr(), stride, tk) == 0
+        hosts.append(host)
+        drecs.append(recs.cuda())
+        tks.append(tk)
+        dests.append(torch.zeros((n, 128, heads, 128), dtype=torch.bfloat16, device="cuda"))
+    torch.cuda.synchronize()
+    with torch.cuda.stream(side):
+        for layer in range(layers):
+            dsts = nl._ptrs(dests[layer].data_ptr() + i * count for i in range(n))
+            assert lib.secure_infer_reload_records(40 + layer, drecs[layer].data_ptr(), stride, count, n, tks[layer],
+                                                   dsts, ks.data_ptr(), status[layer].data_ptr(), None,
+                                                   nl._stream(side), None) == 0
+    torch.cuda.synchronize()
+    assert status.cpu().eq(1).all()
+    for layer in range(layers):
+        assert torch.equal(dests[layer].cpu(), hosts[layer]), layer
 
 
 def test_group_bracket_and_job_auth(nl):
