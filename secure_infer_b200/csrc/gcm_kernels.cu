@@ -605,6 +605,16 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
 // ----------------------------------------------------------------------------
 // Layer kernels: uniform records, descriptors in kernel parameters.
 // ----------------------------------------------------------------------------
+// Programmatic dependent launch.  The layer kernels are launched so that the
+// next kernel in the stream may start once every CTA of the current one has
+// passed launch_dependents (its CTAs then fill their shared-memory tables
+// while this grid drains); grid_dependency_wait() returns when the previous
+// grid has completed and its writes are visible.  Both are no-ops for a
+// normal launch.  Every CTA of a layer grid is resident at once (grid <= one
+// CTA per SM), so a dependent grid never waits on CTAs that cannot start.
+__device__ __forceinline__ void allow_dependent_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void layer_iv(uint32_t iv0, uint64_t ticket, uint32_t iv[4])
 {
     iv[0] = iv0;
@@ -620,6 +630,9 @@ __global__ void __launch_bounds__(kCtrThreads, 1) gcm_layer_ctr_kernel(const __g
     extern __shared__ __align__(16) uint8_t smem[];
     fill_aes4_smem(smem, L.h.sched);
     __syncthreads();
+    // The keystream buffer may still be read by the previous verify grid.
+    allow_dependent_launch();
+    grid_dependency_wait();
     const uint32_t* rk = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
     const Aes4Tables T = aes4_view(smem);
     const uint32_t payload_blocks = static_cast<uint32_t>((L.h.count + 15) >> 4);
@@ -756,6 +769,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
         for (int r = 0; r < 8; ++r) gtab[e * 8 + r] = v;
     }
     __syncthreads();
+    // Records, keystream and destinations are touched only after the
+    // previous grid (the keystream kernel) has completed.
+    allow_dependent_launch();
+    grid_dependency_wait();
     bool tables_ready = false;
 
     const uint64_t count = L.h.count;
@@ -1175,8 +1192,19 @@ int layer_launch(Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint3
     for (uint32_t i = 0; i < h.n; ++i) L.rec[i] = rec[i];
     const uint32_t cap = static_cast<uint32_t>(sms) * ctas_per_sm;
     const uint32_t grid = items < cap ? items : cap;
-    kernel<<<grid, threads, smem, stream>>>(L);
-    return cudaGetLastError();
+    // Programmatic stream serialisation: the kernel's launch and table
+    // prologue overlap the tail of the previous layer kernel in the stream.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, L);
 }
 
 int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
