@@ -58,7 +58,17 @@ CONFIGS = {
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the fused kernel,
 # from the ncu capture summarised in profiles/ (scaled per launch); None until
 # captured for a config.
-NCU_TRAFFIC_BYTES = {}
+NCU_TRAFFIC_BYTES = {
+    # one c2 layer (96 records x 256 KiB): ciphertext + keystream read, bf16 out mostly still in L2 at exit
+    ("c2", "gcm_layer_verify_kernel"): 50_543_360 + 1_207_808,
+    # one c5 layer (128 records x 10256 B, K+V in one launch)
+    ("c5", "gcm_layer_verify_kernel"): 2_836_224,
+}
+
+# Shared-memory wavefronts per 16-byte block that the algorithm needs (the
+# binding pipe): GHASH = 32 LDS.128 per lane per block = 4 wavefronts;
+# AES-128 = 160 T-table LDS.32 + 16 final-round = 176 per 32 blocks = 5.5.
+SMEM_WAVEFRONTS_PER_BLOCK = {"gcm_layer_verify_kernel": 4.0, "gcm_layer_ctr_kernel": 5.5}
 
 
 def layer_bits(mode, layer, layers):
@@ -334,6 +344,18 @@ def run_gpu(args, cfg):
         dom_us = vf_mean if dominant == "gcm_layer_verify_kernel" else ks_mean
         achieved = layer_algo / (dom_us * 1e-6) / 1e9
         traffic = NCU_TRAFFIC_BYTES.get((args.config, dominant))
+        # Binding pipe: shared-memory wavefronts (1 per SM per clock) at the
+        # clock sampled during the timed region.
+        clk = clocks.summary()
+        sm_hz = (clk["sm_mhz"] or clk["sm_max_mhz"] or 1965.0) * 1e6
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        payload_blocks = sum((count[layer] + 15) // 16 for layer in range(L)) * n / L
+        # verify hashes AAD (4) + payload + length block; keystream adds E_K(J0)
+        blocks_per_layer = {"gcm_layer_verify_kernel": payload_blocks + 5 * n, "gcm_layer_ctr_kernel": payload_blocks + n}
+        smem = {}
+        for name, us in (("gcm_layer_verify_kernel", vf_mean), ("gcm_layer_ctr_kernel", ks_mean)):
+            wf = SMEM_WAVEFRONTS_PER_BLOCK[name] * blocks_per_layer[name]
+            smem[name] = round(wf / (us * 1e-6 * sms * sm_hz), 4)
         result = {
             "metric": "Verified KV reload GB/s/GPU (AES-GCM+dequant+scatter); per-layer reload us",
             "value": round(value, 3),
@@ -369,10 +391,12 @@ def run_gpu(args, cfg):
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 2),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "traffic": traffic,
+                         "smem_pipe_frac": smem,
                          "note": "achieved = per-layer algorithmic bytes (ciphertext in + bf16 out) / dominant "
-                                 "kernel time; peak = measured HBM copy bandwidth (of measured). The kernels are "
-                                 "bound by the shared-memory table pipe (AES T-tables, GHASH nibble tables), not "
-                                 "HBM: see profiles/."},
+                                 "kernel time; peak = measured HBM copy bandwidth (of measured). The binding "
+                                 "resource is the shared-memory pipe (AES T-tables, GHASH nibble tables): "
+                                 "smem_pipe_frac = algorithmic wavefronts (GHASH 4, AES 5.5 per 16-byte block) / "
+                                 "(kernel time x SMs x sampled SM clock), 1 wavefront per SM per clock peak."},
             "clocks": clocks.summary(),
         }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
