@@ -187,6 +187,21 @@ int secure_infer_d2h_writeback_layer(const void* const* src_blocks, void* const*
                                      const secure_infer_codec* codec, void* stream);
 int secure_infer_d2h_wait(void);
 
+/* Device half of a writeback, the mirror of secure_infer_reload_records (no
+ * single reference function: it is the device part of the D2H path,
+ * ghash.aicpu:656-699 encrypt_tag after transport_codec.py:22-42 encode).
+ * srcs[i]: device bf16 block (128 tokens x heads x 128); for codec bits 8/4
+ * the blocks are quantised into packets first (kind 0 = K, 1 = V,
+ * SECURE_INFER_KIND_KV = first n/2 K, rest V).  Each record gets a fresh
+ * ticket (tickets_out[i], host) and its AAD names host_dsts[i] (the host-pool
+ * slot it is meant for; may be null) with direction D2H.  Records
+ * C || tag || 0^16 || AAD (count = packet bytes, or 2*128*heads*128 raw) go to
+ * `records` (device, record_stride >= secure_infer_record_bytes(count)),
+ * ordered on `stream`; they reload through secure_infer_reload_records. */
+int secure_infer_writeback_records(const void* const* srcs, void* const* host_dsts, uint32_t n,
+                                   const secure_infer_codec* codec, void* records, uint64_t record_stride,
+                                   uint64_t* tickets_out, void* stream);
+
 /* ------------------------------------------------- prediction scope */
 
 /* secure_infer.cpp:1102-1146.  Keystreams here are derived from tickets at

@@ -740,9 +740,13 @@ __device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecPa
     }
 }
 
-template <int kCap, bool kCodec>
+enum : int { kLayerVerifyRaw = 0, kLayerVerifyCodec = 1, kLayerEncrypt = 2 };
+
+template <int kCap, int kMode>
 __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
+    constexpr bool kCodec = kMode == kLayerVerifyCodec;
+    constexpr bool kEncrypt = kMode == kLayerEncrypt;
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* gtab = reinterpret_cast<uint4*>(smem);
     uint4* ltab = reinterpret_cast<uint4*>(smem + kGhashSmem);
@@ -793,10 +797,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
 
     for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * kLayerWarps) {
         const uint32_t r = w / nseg, k = w - r * nseg;
-        const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
-        const uint8_t* aad = in + tag_off + 32;
+        // Verify: record -> plaintext destination.  Encrypt: plaintext
+        // source -> record (C || tag || 0^16 || AAD).
+        uint8_t* rec_ptr = const_cast<uint8_t*>(L.h.records) + static_cast<uint64_t>(r) * L.h.stride;
+        const uint8_t* in = kEncrypt ? L.rec[r].dst : rec_ptr;
+        const uint8_t* aad = kEncrypt ? L.h.aad + 64ull * r : rec_ptr + tag_off + 32;
         const uint8_t* ksp = L.h.ks + static_cast<uint64_t>(r) * L.h.ks_stride;
-        uint8_t* out = L.rec[r].dst;
+        uint8_t* out = kEncrypt ? rec_ptr : L.rec[r].dst;
         const int64_t seg_end = len0 + static_cast<int64_t>(k) * seg_blocks;
         const int64_t seg_len = k == 0 ? len0 : seg_blocks;
         const int J = static_cast<int>((seg_len + 31) / 32);
@@ -846,11 +853,17 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
                         else
                             layer_dequant<32>(xor4(x0, k0), off >> 4, cp, kind, in, ksp, out, pkey, psc, plo);
                     }
+                } else if constexpr (kEncrypt) {
+                    // C is zero past `count` (both loads are), so the whole
+                    // block goes out: the record's padding must be zero.
+                    store_block(out + off, xor4(x0, k0), 16, aligned);
                 } else {
                     store_block(out + off, xor4(x0, k0), count - off, aligned);
                 }
             }
-            Y = j == 0 ? x0 : xor4(gf_mul_table<8, false>(Y, gtab, rep), x0);
+            // GHASH runs over the ciphertext: loaded (verify) or just formed (encrypt).
+            const uint4 h0 = kEncrypt ? xor4(x0, k0) : x0;
+            Y = j == 0 ? h0 : xor4(gf_mul_table<8, false>(Y, gtab, rep), h0);
         }
         // Two-stage lane combine in shared memory.  If the table copy never
         // completes the partial is poisoned, so the record fails closed
@@ -889,6 +902,20 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
             }
         }
         const uint4 mask = *reinterpret_cast<const uint4*>(ksp + (L.h.ks_stride - 16));
+        if constexpr (kEncrypt) {
+            // tag, zero block, AAD copy, and zeros over [round16(count), tag_off).
+            const uint64_t pad_first = (count + 15) & ~uint64_t(15);
+            if (lane == 0) store_block(out + tag_off, xor4(acc, mask), 16, aligned);
+            if (lane == 1) store_block(out + tag_off + 16, zero4(), 16, aligned);
+            if (lane >= 2 && lane < 6)
+                store_block(out + tag_off + 16 * lane, load_partial16(aad + 16 * (lane - 2), 16), 16, aligned);
+            if (lane == 6 && pad_first < tag_off) store_block(out + pad_first, zero4(), 16, aligned);
+            if (lane == 0) {
+                L.h.status[r] = 1u;
+                L.h.counters[r] = 0u;
+            }
+            continue;
+        }
         const bool ok = equal4(xor4(acc, mask), load_partial16(in + tag_off, 16));
         if (lane == 0) {
             L.h.status[r] = ok ? 1u : 0u;
@@ -916,6 +943,7 @@ __global__ void __launch_bounds__(256) kv_encode_kernel(const __grid_constant__ 
     const CodecParams cp = L.codec;
     const uint32_t hd = cp.heads * 128u, elements = 128u * hd, groups = elements / 64u;
     const uint32_t rec = blockIdx.y;
+    const uint32_t kind = rec >= L.v_first ? 1u : 0u;
     const uint16_t* src = reinterpret_cast<const uint16_t*>(L.srcs[rec]);
     uint8_t* pkt = L.packets + static_cast<size_t>(rec) * L.width;
     float* scale = reinterpret_cast<float*>(pkt + cp.qb);
@@ -924,7 +952,7 @@ __global__ void __launch_bounds__(256) kv_encode_kernel(const __grid_constant__ 
     const uint32_t lane = threadIdx.x & 31u;
 
     for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += gridDim.x * blockDim.x) {
-        if (cp.kind == 0) {
+        if (kind == 0) {
             // 64 tokens of channel ch in token group tg; element e = (64 tg + t) hd + ch.
             const uint32_t tg = g / hd, ch = g % hd;
             const uint16_t* col = src + static_cast<size_t>(tg) * 64u * hd + ch;
@@ -1013,7 +1041,7 @@ __global__ void __launch_bounds__(256) kv_encode_kernel(const __grid_constant__ 
         for (uint32_t i = threadIdx.x; i < L.width - hdr; i += blockDim.x) {
             uint8_t v = 0;
             if (i < 16) {
-                const uint32_t word = i < 4 ? 1u : i < 8 ? L.layer : i < 12 ? cp.kind : cp.bits;
+                const uint32_t word = i < 4 ? 1u : i < 8 ? L.layer : i < 12 ? kind : cp.bits;
                 v = static_cast<uint8_t>(word >> (8 * (i & 3)));
             }
             pkt[hdr + i] = v;
@@ -1237,16 +1265,32 @@ int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t 
     const bool small = h.n <= static_cast<uint32_t>(kLayerCapSmall);
     if (h.codec.bits) {
         if (small)
-            return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, true>, h, rec, kLayerThreads,
-                                                kLayerSmem, grid, set_small_c[dev & 63], stream, 1);
-        return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, true>, h, rec, kLayerThreads,
-                                            kLayerSmem, grid, set_large_c[dev & 63], stream, 1);
+            return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec>, h, rec,
+                                                kLayerThreads, kLayerSmem, grid, set_small_c[dev & 63], stream, 1);
+        return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec>, h, rec,
+                                            kLayerThreads, kLayerSmem, grid, set_large_c[dev & 63], stream, 1);
     }
     if (small)
-        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, false>, h, rec, kLayerThreads,
-                                            kLayerSmem, grid, set_small[dev & 63], stream, 1);
-    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, false>, h, rec, kLayerThreads,
-                                        kLayerSmem, grid, set_large[dev & 63], stream, 1);
+        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyRaw>, h, rec,
+                                            kLayerThreads, kLayerSmem, grid, set_small[dev & 63], stream, 1);
+    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyRaw>, h, rec,
+                                        kLayerThreads, kLayerSmem, grid, set_large[dev & 63], stream, 1);
+}
+
+int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
+{
+    if (h.n == 0) return cudaSuccess;
+    if (h.n > static_cast<uint32_t>(kLayerCapLarge) || h.aad == nullptr) return cudaErrorInvalidValue;
+    const uint32_t items = h.nseg * h.n;
+    static bool set_small[64], set_large[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint32_t grid = (items + kLayerWarps - 1) / kLayerWarps;
+    if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
+        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, kLayerEncrypt>, h, rec,
+                                            kLayerThreads, kLayerSmem, grid, set_small[dev & 63], stream, 1);
+    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, kLayerEncrypt>, h, rec,
+                                        kLayerThreads, kLayerSmem, grid, set_large[dev & 63], stream, 1);
 }
 
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream)

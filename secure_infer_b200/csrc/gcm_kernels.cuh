@@ -95,6 +95,7 @@ struct EncodeLaunch {
     uint32_t width;
     uint32_t layer;
     CodecParams codec;
+    uint32_t v_first;              // records r >= v_first are V blocks, the rest K
 };
 
 // A layer of uniform records laid out as C[aligned32(count)] || tag || 0^16 ||
@@ -124,6 +125,7 @@ struct LayerHeader {
     uint32_t unaligned;
     CodecParams codec;      // bits 0: raw payload; 8/4: codec packets dequantised into bf16 blocks
     uint32_t v_first;       // codec: records r >= v_first decode as V packets, the rest as K
+    const uint8_t* aad;     // encrypt: AAD of record r at aad + 64 r (records are the output)
 };
 
 template <int kCap>
@@ -140,9 +142,13 @@ inline uint64_t layer_ks_stride(uint64_t count) { return ((count + 15) & ~uint64
 void layer_segments_for(uint64_t count, uint32_t n, uint32_t* seg_steps, uint32_t* nseg);
 
 // Keystream (+ tag masks) and fused verify/XOR/scatter for up to
-// kLayerCapLarge records; rec points at n LayerRec entries.
+// kLayerCapLarge records; rec points at n LayerRec entries.  The encrypt
+// launch is the writeback mirror: rec[i].dst is the plaintext (raw block or
+// codec packet) of record i, written as C || tag || 0^16 || AAD into
+// records + i * stride.
 int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
+int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 
 // Host-side launchers (gcm_kernels.cu).  Return a cudaError_t value.
 // key may be null (GHASH-only requests); h null -> H = E_K(0^128) on device.

@@ -305,7 +305,9 @@ struct StageSlot {
     uint32_t cap_recs = 0;
     uint8_t* host = nullptr;       // pinned records
     uint8_t* dev = nullptr;        // device records
-    uint8_t* ks = nullptr;         // device keystream / D2H plaintext packets
+    uint8_t* ks = nullptr;         // device keystream
+    uint8_t* pkt = nullptr;        // device codec packets (writeback plaintext)
+    uint64_t pkt_cap = 0;
     uint8_t* host_aad = nullptr;   // pinned [cap_recs][64] (D2H)
     uint8_t* dev_aad = nullptr;
     const uint8_t** host_ptrs = nullptr;   // pinned [cap_recs] (D2H encode gather)
@@ -373,6 +375,8 @@ struct Session {
     size_t h2d_next = 0;
     std::vector<StageSlot> d2h;       // ring
     size_t d2h_next = 0;
+    std::vector<StageSlot> wb;        // ring: scratch of device-resident writebacks
+    size_t wb_next = 0;
 
     std::map<uint32_t, std::vector<std::shared_ptr<LayerBatch>>> pending;
     std::map<uint32_t, cudaEvent_t> last_event;   // not owned: batch->done
@@ -443,22 +447,24 @@ bool ensure_launch_slot(LaunchSlot& s, uint32_t recs, uint32_t segs)
 void free_stage(StageSlot& s)
 {
     cudaFreeHost(s.host); cudaFreeHost(s.host_aad); cudaFreeHost(s.host_ptrs); cudaFreeHost(s.host_status);
-    cudaFree(s.dev); cudaFree(s.ks); cudaFree(s.dev_aad); cudaFree(s.dev_ptrs); cudaFree(s.dev_status);
-    s.host = s.dev = s.ks = s.host_aad = s.dev_aad = nullptr;
+    cudaFree(s.dev); cudaFree(s.ks); cudaFree(s.pkt); cudaFree(s.dev_aad); cudaFree(s.dev_ptrs); cudaFree(s.dev_status);
+    s.host = s.dev = s.ks = s.pkt = s.host_aad = s.dev_aad = nullptr;
+    s.pkt_cap = 0;
     s.host_ptrs = s.dev_ptrs = nullptr;
     s.host_status = s.dev_status = nullptr;
     s.cap = s.ks_cap = 0;
     s.cap_recs = 0;
 }
 
-bool ensure_stage(StageSlot& s, uint64_t bytes, uint64_t ks_bytes, uint32_t recs)
+bool ensure_stage(StageSlot& s, uint64_t bytes, uint64_t ks_bytes, uint32_t recs, uint64_t pkt_bytes = 0)
 {
-    if (s.cap >= bytes && s.ks_cap >= ks_bytes && s.cap_recs >= recs) return true;
+    if (s.cap >= bytes && s.ks_cap >= ks_bytes && s.cap_recs >= recs && s.pkt_cap >= pkt_bytes) return true;
     if (s.done) cudaEventSynchronize(s.done);
     free_stage(s);
     const uint32_t r = std::max<uint32_t>(recs, 256);
     if (!CUDA_OK(cudaHostAlloc(&s.host, bytes, cudaHostAllocDefault)) || !CUDA_OK(cudaMalloc(&s.dev, bytes)) ||
         (ks_bytes && !CUDA_OK(cudaMalloc(&s.ks, ks_bytes))) ||
+        (pkt_bytes && !CUDA_OK(cudaMalloc(&s.pkt, pkt_bytes))) ||
         !CUDA_OK(cudaHostAlloc(&s.host_aad, 64ull * r, cudaHostAllocDefault)) ||
         !CUDA_OK(cudaMalloc(&s.dev_aad, 64ull * r)) ||
         !CUDA_OK(cudaHostAlloc(reinterpret_cast<void**>(&s.host_ptrs), sizeof(void*) * r, cudaHostAllocDefault)) ||
@@ -470,6 +476,7 @@ bool ensure_stage(StageSlot& s, uint64_t bytes, uint64_t ks_bytes, uint32_t recs
     }
     s.cap = bytes;
     s.ks_cap = ks_bytes;
+    s.pkt_cap = pkt_bytes;
     s.cap_recs = r;
     return true;
 }
@@ -849,17 +856,93 @@ void d2h_worker()
     }
 }
 
+// Device half of a writeback of n blocks (transport_codec.py:22-42 encode,
+// ghash.aicpu:656-699 encrypt_tag): for codec blocks quantise into packets,
+// then keystream + tag masks, then the fused encrypt/GHASH/tag kernel writing
+// records C || tag || 0^16 || AAD into `records` (device, `stride` apart).
+// Each record gets a fresh ticket; its AAD names host_dsts[i] with direction
+// D2H (secure_infer.cpp:730-775).  tickets/ivs/aads (host, optional) receive
+// what the host verify needs.  `slot` must hold n records of scratch.
+// Caller holds g_mu.
+int writeback_device_locked(const void* const* srcs, void* const* host_dsts, uint32_t n, const CodecParams& cp,
+                            uint32_t codec_layer, uint64_t count, uint8_t* records, uint64_t stride, StageSlot& slot,
+                            uint64_t* tickets, uint8_t* ivs, uint8_t* aads, cudaStream_t stream)
+{
+    const uint64_t ks_stride = layer_ks_stride(count);
+    std::vector<uint64_t> tk(n);
+    bool unaligned = misaligned(records) || (stride & 15u);
+    for (uint32_t i = 0; i < n; ++i) {
+        tk[i] = reserve_ticket();
+        if (tickets) tickets[i] = tk[i];
+        if (ivs) iv_for(tk[i], ivs + 16ull * i);
+        build_aad(host_dsts ? host_dsts[i] : nullptr, count, SECURE_INFER_DIRECTION_D2H, tk[i], 0, 0,
+                  slot.host_aad + 64ull * i);
+        if (aads) std::memcpy(aads + 64ull * i, slot.host_aad + 64ull * i, 64);
+        slot.host_ptrs[i] = static_cast<const uint8_t*>(srcs[i]);
+        if (!cp.bits && misaligned(srcs[i])) unaligned = true;
+    }
+    if (!CUDA_OK(cudaMemcpyAsync(slot.dev_aad, slot.host_aad, 64ull * n, cudaMemcpyHostToDevice, stream))) return -1;
+    const uint32_t v_first = cp.kind == SECURE_INFER_KIND_KV ? n / 2 : (cp.kind == 1 ? 0u : n);
+    if (cp.bits) {
+        if (!CUDA_OK(cudaMemcpyAsync(slot.dev_ptrs, slot.host_ptrs, sizeof(void*) * n, cudaMemcpyHostToDevice, stream)))
+            return -1;
+        EncodeLaunch E{};
+        E.srcs = slot.dev_ptrs;
+        E.packets = slot.pkt;
+        E.n = n;
+        E.width = static_cast<uint32_t>(count);
+        E.layer = codec_layer;
+        E.codec = cp;
+        E.v_first = v_first;
+        if (launch_encode(E, stream) != cudaSuccess) return -1;
+    }
+    if (keystream_records_locked(tk.data(), n, count, slot.ks, stream) != 0) return -1;
+    std::vector<LayerRec> recs(std::min<uint32_t>(n, kLayerCapLarge));
+    for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
+        const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
+        uint32_t seg_steps = 0, nseg = 0;
+        layer_segments_for(count, m, &seg_steps, &nseg);
+        LaunchSlot& ls = g_s.launch[g_s.launch_next];
+        g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
+        if (!ensure_launch_slot(ls, m, nseg * m)) return -1;
+        LayerHeader h{};
+        h.sched = g_s.sched;
+        h.records = records + first * stride;
+        h.stride = stride;
+        h.count = count;
+        h.ks = slot.ks + first * ks_stride;
+        h.ks_stride = ks_stride;
+        h.status = slot.dev_status + first;
+        h.partials = ls.partials;
+        h.counters = ls.counters;
+        h.iv0 = load_be32(g_s.salt);
+        h.n = m;
+        h.nseg = nseg;
+        h.seg_steps = seg_steps;
+        h.aad = slot.dev_aad + 64ull * first;
+        h.unaligned = unaligned ? 1u : 0u;
+        for (uint32_t i = 0; i < m; ++i) {
+            uint8_t* plain = cp.bits ? slot.pkt + (first + i) * count : const_cast<uint8_t*>(slot.host_ptrs[first + i]);
+            recs[i] = LayerRec{plain, tk[first + i]};
+        }
+        if (launch_layer_encrypt(h, recs.data(), stream) != cudaSuccess) return -1;
+        cudaEventRecord(ls.free_ev, stream);
+        ls.used = true;
+    }
+    return 0;
+}
+
 int d2h_submit_group(const void* const* srcs, void* const* dsts, uint32_t n, uint64_t count,
                      const secure_infer_codec* codec, cudaStream_t stream)
 {
     CodecParams cp;
     uint64_t packet = 0;
-    if (!codec_geometry(codec, &cp, &packet) || n == 0 || srcs == nullptr || dsts == nullptr) return -1;
+    if (!codec_geometry(codec, &cp, &packet, true) || n == 0 || srcs == nullptr || dsts == nullptr) return -1;
     if (cp.bits) count = packet;
-    if (count == 0) return -1;
+    if (count == 0 || (cp.bits && cp.kind == SECURE_INFER_KIND_KV && (n & 1u))) return -1;
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     if (!g_s.ready) return -1;
-    const uint64_t stride = record_bytes(count), aligned = aligned32(count);
+    const uint64_t stride = record_bytes(count);
     StageSlot& slot = g_s.d2h[g_s.d2h_next];
     g_s.d2h_next = (g_s.d2h_next + 1) % g_s.d2h.size();
     {
@@ -871,7 +954,7 @@ int d2h_submit_group(const void* const* srcs, void* const* dsts, uint32_t n, uin
             return true;
         });
     }
-    if (!ensure_stage(slot, stride * n, cp.bits ? packet * n : 0, n)) return -1;
+    if (!ensure_stage(slot, stride * n, layer_ks_stride(count) * n, n, cp.bits ? packet * n : 0)) return -1;
     auto g = std::make_shared<D2HGroup>();
     g->n = n;
     g->count = count;
@@ -881,60 +964,9 @@ int d2h_submit_group(const void* const* srcs, void* const* dsts, uint32_t n, uin
     g->ivs.resize(16ull * n);
     g->aads.resize(64ull * n);
     if (!CUDA_OK(cudaEventCreateWithFlags(&g->copied, cudaEventDisableTiming))) return -1;
-    std::vector<GcmRecord> recs(n);
-    for (uint32_t i = 0; i < n; ++i) {
-        const uint64_t t = reserve_ticket();
-        iv_for(t, &g->ivs[16 * i]);
-        build_aad(dsts[i], count, SECURE_INFER_DIRECTION_D2H, t, 0, 0, &g->aads[64 * i]);
-        std::memcpy(slot.host_aad + 64ull * i, &g->aads[64 * i], 64);
-        slot.host_ptrs[i] = static_cast<const uint8_t*>(srcs[i]);
-    }
-    if (!CUDA_OK(cudaMemcpyAsync(slot.dev_aad, slot.host_aad, 64ull * n, cudaMemcpyHostToDevice, stream))) return -1;
-    if (cp.bits) {
-        if (!CUDA_OK(cudaMemcpyAsync(slot.dev_ptrs, slot.host_ptrs, sizeof(void*) * n, cudaMemcpyHostToDevice, stream)))
-            return -1;
-        EncodeLaunch E{};
-        E.srcs = slot.dev_ptrs;
-        E.packets = slot.ks;
-        E.n = n;
-        E.width = static_cast<uint32_t>(packet);
-        E.layer = codec->layer;
-        E.codec = cp;
-        if (launch_encode(E, stream) != cudaSuccess) return -1;
-    }
-    // Device records: op Encrypt, C into the staging records, tag after C.
-    const uint32_t nseg = segments_for(count, kAadBytes);
-    LaunchSlot& ls = g_s.launch[g_s.launch_next];
-    g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
-    if (!ensure_launch_slot(ls, n, nseg * n)) return -1;
-    for (uint32_t i = 0; i < n; ++i) {
-        GcmRecord& r = ls.host_recs[i];
-        r = GcmRecord{};
-        r.op = kOpEncrypt;
-        r.in = cp.bits ? slot.ks + i * packet : static_cast<const uint8_t*>(srcs[i]);
-        r.aad = slot.dev_aad + 64ull * i;
-        r.aad_bytes = static_cast<uint32_t>(kAadBytes);
-        r.out = slot.dev + i * stride;
-        r.tag_out = slot.dev + i * stride + aligned;
-        r.count = count;
-        const uint8_t* iv = &g->ivs[16 * i];
-        r.iv[0] = load_be32(iv); r.iv[1] = load_be32(iv + 4); r.iv[2] = load_be32(iv + 8); r.iv[3] = 2u;
-        r.seg_first = i * nseg;
-        r.nseg = nseg;
-        if (misaligned(r.in)) r.flags |= kRecUnaligned;
-    }
-    if (!CUDA_OK(cudaMemcpyAsync(ls.dev_recs, ls.host_recs, sizeof(GcmRecord) * n, cudaMemcpyHostToDevice, stream)))
+    if (writeback_device_locked(srcs, dsts, n, cp, codec ? codec->layer : 0, count, slot.dev, stride, slot, nullptr,
+                                g->ivs.data(), g->aads.data(), stream) != 0)
         return -1;
-    SegmentLaunch L{};
-    L.sched = g_s.sched;
-    L.recs = ls.dev_recs;
-    L.nrec = n;
-    L.total_segs = nseg * n;
-    L.partials = ls.partials;
-    L.counters = ls.counters;
-    if (launch_segments(L, true, stream) != cudaSuccess) return -1;
-    cudaEventRecord(ls.free_ev, stream);
-    ls.used = true;
     if (!CUDA_OK(cudaMemcpyAsync(slot.host, slot.dev, stride * n, cudaMemcpyDeviceToHost, stream))) return -1;
     cudaEventRecord(g->copied, stream);
     {
@@ -1017,6 +1049,11 @@ void shutdown_locked()
     g_s.last_batch.clear();
     for (auto& s : g_s.h2d) { s.owner.reset(); free_stage(s); }
     for (auto& s : g_s.d2h) free_stage(s);
+    for (auto& s : g_s.wb) {
+        free_stage(s);
+        if (s.done) cudaEventDestroy(s.done);
+        s.done = nullptr;
+    }
     for (auto& s : g_s.launch) {
         cudaFreeHost(s.host_recs); cudaFreeHost(s.host_jobs);
         cudaFree(s.dev_recs); cudaFree(s.dev_jobs); cudaFree(s.partials); cudaFree(s.counters);
@@ -1025,6 +1062,7 @@ void shutdown_locked()
     g_s.launch.clear();
     g_s.h2d.clear();
     g_s.d2h.clear();
+    g_s.wb.clear();
     cudaFree(g_s.sched);
     g_s.sched = nullptr;
     if (g_s.producer) cudaStreamDestroy(g_s.producer);
@@ -1086,6 +1124,7 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
     g_s.launch.resize(kLaunchSlots);
     for (auto& s : g_s.launch) cudaEventCreateWithFlags(&s.free_ev, cudaEventDisableTiming);
     g_s.h2d.resize(stage_slot_count());
+    g_s.wb.resize(stage_slot_count());
     g_s.d2h.resize(stage_slot_count());
     g_s.d2h_stop = false;
     g_s.d2h_thread = std::thread(d2h_worker);
@@ -1381,6 +1420,35 @@ SI_EXPORT int secure_infer_d2h_writeback_layer(const void* const* src_blocks, vo
 }
 
 SI_EXPORT int secure_infer_d2h_wait(void) { return d2h_join(0, false); }
+
+SI_EXPORT int secure_infer_writeback_records(const void* const* srcs, void* const* host_dsts, uint32_t n,
+                                             const secure_infer_codec* codec, void* records, uint64_t record_stride,
+                                             uint64_t* tickets_out, void* stream)
+{
+    sib::CodecParams cp;
+    uint64_t packet = 0;
+    if (codec == nullptr || srcs == nullptr || records == nullptr || tickets_out == nullptr || n == 0 ||
+        !codec_geometry(codec, &cp, &packet, true))
+        return -1;
+    const uint64_t count = cp.bits ? packet : 2ull * 128u * codec->heads * 128u;
+    if (codec->heads == 0 || record_stride < record_bytes(count) || (record_stride & 15u) ||
+        (cp.bits && cp.kind == SECURE_INFER_KIND_KV && (n & 1u)))
+        return -1;
+    for (uint32_t i = 0; i < n; ++i)
+        if (srcs[i] == nullptr) return -1;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!g_s.ready) return -1;
+    StageSlot& slot = g_s.wb[g_s.wb_next];
+    g_s.wb_next = (g_s.wb_next + 1) % g_s.wb.size();
+    if (slot.done) cudaEventSynchronize(slot.done);   // its pinned AAD copy and scratch are free
+    if (!slot.done && !CUDA_OK(cudaEventCreateWithFlags(&slot.done, cudaEventDisableTiming))) return -1;
+    if (!ensure_stage(slot, 16, sib::layer_ks_stride(count) * n, n, cp.bits ? packet * n : 0)) return -1;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (writeback_device_locked(srcs, host_dsts, n, cp, codec->layer, count, static_cast<uint8_t*>(records),
+                                record_stride, slot, tickets_out, nullptr, nullptr, s) != 0)
+        return -1;
+    return CUDA_OK(cudaEventRecord(slot.done, s)) ? 0 : -1;
+}
 
 SI_EXPORT void secure_infer_invalidate_transfer_prefetches(void) { ++g_generation; }
 SI_EXPORT void secure_infer_retire_transfer_prefetches(void) { ++g_generation; }

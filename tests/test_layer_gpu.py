@@ -317,6 +317,69 @@ def test_writeback_roundtrip(nl, bits, kind):
         assert np.array_equal(u16(host)[host_ids], src)
 
 
+@pytest.mark.parametrize("bits,kind", [(0, 0), (8, 0), (8, 1), (4, 0), (4, 1), (8, 2), (4, 2)])
+def test_writeback_records_device_roundtrip(nl, bits, kind):
+    """Device writeback (quantise + keystream + fused encrypt/tag) of a shuffled
+    set of paged-cache blocks: every record must equal the oracle's OpenSSL
+    view (C, tag and AAD decrypt-verify to the oracle packet or the raw block),
+    then reload through reload_records back into the paged cache."""
+    from oracle import gcm as orc
+    heads, layer = 2, 9
+    lib = nl._native.lib()
+    cache = bf16_random((12, 128, heads, 128), 500 + 10 * bits + kind, outliers=True).cuda()
+    ids = [7, 2, 9, 0, 11, 4] if kind == 2 else [7, 2, 9, 0, 5]
+    n = len(ids)
+    kinds = [0] * (n // 2) + [1] * (n - n // 2) if kind == 2 else [kind] * n
+    bb = 128 * heads * 128 * 2
+    count = nl.packet_bytes(heads, bits) if bits else bb
+    stride = nl.record_bytes(count)
+    aligned = orc.record_aligned_bytes(count)
+    records = torch.zeros((n, stride), dtype=torch.uint8, device="cuda")
+    tickets = (ct.c_uint64 * n)()
+    srcs = nl._ptrs(cache.data_ptr() + i * bb for i in ids)
+    codec = nl._native.Codec(bits, kind, heads, layer)
+    assert lib.secure_infer_writeback_records(srcs, None, n, ct.byref(codec), records.data_ptr(), stride, tickets,
+                                              nl._stream()) == 0
+    torch.cuda.synchronize()
+    recs = records.cpu().numpy()
+    src = u16(cache)
+    for i in range(n):
+        rec = recs[i].tobytes()
+        if bits:
+            want, _, _ = codec_oracle.encode(src, [ids[i]], bits, kinds[i], layer)
+            want = want[0].tobytes()
+        else:
+            want = src[ids[i]].tobytes()
+        aad = rec[aligned + 32:aligned + 96]
+        assert aad[:4] == b"SFAD" and aad[5] == 2           # direction D2H
+        assert int.from_bytes(aad[36:44], "big") == tickets[i]
+        assert rec[count:aligned] == bytes(aligned - count) and rec[aligned + 16:aligned + 32] == bytes(16)
+        iv = orc.derive_transfer_iv(SALT, tickets[i])
+        plain, ok = orc.host_decrypt_verify(KEY, iv, aad, rec[:count], rec[aligned:aligned + 16])
+        assert ok == 1 and plain == want, i
+        # The oracle's own encryption of the same plaintext gives the same record bytes.
+        assert orc.host_encrypt_record(KEY, iv, aad, want)[:aligned + 16] == rec[:aligned + 16], i
+    # Back through the authenticated reload path.
+    dest = torch.zeros((n, 128, heads, 128), dtype=torch.bfloat16, device="cuda")
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
+    status = torch.zeros(n, dtype=torch.int32, device="cuda")
+    dsts = nl._ptrs(dest.data_ptr() + i * bb for i in range(n))
+    assert lib.secure_infer_reload_records(layer, records.data_ptr(), stride, count, n, tickets, dsts, ks.data_ptr(),
+                                           status.data_ptr(), ct.byref(codec) if bits else None, nl._stream(),
+                                           None) == 0
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == [1] * n
+    got = u16(dest)
+    for i in range(n):
+        if bits:
+            pk, qb, sb = codec_oracle.encode(src, [ids[i]], bits, kinds[i], layer)
+            exp = np.zeros((1, 128, heads, 128), np.uint16)
+            codec_oracle.decode_into(pk, exp, [0], bits, kinds[i], qb, sb)
+            assert np.array_equal(got[i], exp[0]), i
+        else:
+            assert np.array_equal(got[i], src[ids[i]]), i
+
+
 def test_writeback_tamper_withheld(nl):
     heads, layer = 1, 12
     cache = bf16_random((3, 128, heads, 128), 5).cuda()
