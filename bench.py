@@ -53,6 +53,9 @@ CONFIGS = {
     "c2": dict(model="Llama-3-8B", layers=32, heads=8, blocks=48, codec="none", outliers=False),
     "c3": dict(model="Qwen2.5-7B", layers=28, heads=4, blocks=48, codec="int8", outliers=True),
     "c5": dict(model="Llama-3-70B-TP8", layers=80, heads=1, blocks=64, codec="int4", outliers=False),
+    # writeback direction (gather + quantise + encrypt + tag; e2e adds D2H + host verify)
+    "c4": dict(model="Llama-3-8B", layers=32, heads=8, blocks=64, codec="int4", outliers=False, direction="d2h"),
+    "c4m": dict(model="Llama-3-8B", layers=32, heads=8, blocks=64, codec="mixed", outliers=False, direction="d2h"),
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the fused kernel,
@@ -149,6 +152,30 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def kernel_profile(lib, torch, enqueue_step, layers):
+    """Per-kernel device time of one step from the library's own launch
+    events.  The step is queued behind a device-side sleep so that each
+    kernel's events bracket the kernel, not the host's enqueue time.
+    Returns {kernel name: (mean us per launch, launches)}."""
+    kinds = 16
+    torch.cuda.synchronize()
+    assert lib.secure_infer_kernel_profile_enable(1) == 0
+    torch.cuda._sleep(int(layers * 60e-6 * 2.0e9))
+    enqueue_step()
+    torch.cuda.synchronize()
+    us = (ct.c_double * kinds)()
+    cnt = (ct.c_uint64 * kinds)()
+    rc = lib.secure_infer_kernel_profile_collect(us, cnt, kinds)
+    lib.secure_infer_kernel_profile_enable(0)
+    assert rc == 0
+    out = {}
+    for k in range(kinds):
+        name = lib.secure_infer_kernel_name(k)
+        if name and cnt[k]:
+            out[name.decode()] = (us[k] / cnt[k], int(cnt[k]))
+    return out
 
 
 def build_workload(cfg, rank, torch, nl):
@@ -288,22 +315,9 @@ def run_gpu(args, cfg):
     value = world * algo / (ms_per_step * 1e-3) / 1e9
 
     # ---- per-kernel device time (roofline) ----
-    # Each layer's two kernels are queued behind a device-side sleep, so the
-    # events bracket the kernels alone, not the host's enqueue time.
-    ks_us, vf_us = [], []
-    for layer in range(L):
-        c, s_ = count[layer], strides[layer]
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        torch.cuda._sleep(200_000)
-        ev[0].record(stream)
-        assert lib.secure_infer_keystream_records(tickets[layer], n, c, ks_ptr, sp) == 0
-        ev[1].record(stream)
-        assert lib.secure_infer_verify_records(layer, rec_ptr[layer], s_, c, n, tickets[layer], dst_all[layer],
-                                               ks_ptr, st_ptr[layer], codec_arg[layer], sp) == 0
-        ev[2].record(stream)
-        torch.cuda.synchronize()
-        ks_us.append(ev[0].elapsed_time(ev[1]) * 1e3)
-        vf_us.append(ev[1].elapsed_time(ev[2]) * 1e3)
+    prof = kernel_profile(lib, torch, device_step, L)
+    ks_us = prof["gcm_layer_ctr_kernel"][0]
+    vf_us = prof["gcm_layer_verify_kernel"][0]
     assert int(status.min().item()) == 1
 
     # ---- end to end through the C ABI from host plaintext ----
@@ -335,8 +349,7 @@ def run_gpu(args, cfg):
 
     result = None
     if rank == 0:
-        ks_mean = statistics.mean(ks_us)
-        vf_mean = statistics.mean(vf_us)
+        ks_mean, vf_mean = ks_us, vf_us
         dominant = "gcm_layer_verify_kernel" if vf_mean >= ks_mean else "gcm_layer_ctr_kernel"
         layer_algo = algo / L
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
@@ -386,8 +399,8 @@ def run_gpu(args, cfg):
             "gpu_launches": launches,
             "kernels": {"gcm_layer_ctr_kernel_us_per_layer": round(ks_mean, 2),
                         "gcm_layer_verify_kernel_us_per_layer": round(vf_mean, 2),
-                        "timing": "CUDA events on the launching stream around each kernel, queued behind a "
-                                  "device sleep so host enqueue time is excluded"},
+                        "timing": "the library's CUDA events around each launch (secure_infer_kernel_profile_*), "
+                                  "one step queued behind a device sleep so host enqueue time is excluded"},
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 2),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "traffic": traffic,
@@ -406,6 +419,243 @@ def run_gpu(args, cfg):
         dist.destroy_process_group()
     nl._native.lib().secure_infer_session_shutdown()
     return result
+
+
+def run_gpu_writeback(args, cfg):
+    """Writeback (C4): per layer, the K and V blocks of the prefix are gathered
+    from a paged bf16 cache through a shuffled block table, quantised
+    (int4, or the mixed int8/int4 layer split), encrypted and tagged.
+
+    value: secure_infer_writeback_records per layer into device records.
+    e2e:   secure_infer_d2h_writeback_layer per layer (device work + D2H into a
+           pinned staging ring + OpenSSL verify/decrypt on host threads into
+           the pinned host pool), joined by secure_infer_d2h_wait each step.
+    """
+    import torch
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    from secure_infer_b200 import _native, native_layerwise as nl
+    lib = _native.lib()
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    key, salt = rank_session_material(rank)
+    nl.Session(local, key, salt)
+    L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
+    n = 2 * B
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    sp = ct.c_void_p(stream.cuda_stream)
+    gen = torch.Generator(device="cuda").manual_seed(4321 + rank)
+    num_gpu_blocks = B + 16
+    perm = torch.randperm(num_gpu_blocks, generator=torch.Generator().manual_seed(77 + rank))[:B].tolist()
+    cache = [[torch.randn((num_gpu_blocks, 128, H, 128), generator=gen, device="cuda").to(torch.bfloat16)
+              for _ in range(2)] for _ in range(L)]
+    bits = [layer_bits(cfg["codec"], layer, L) for layer in range(L)]
+    bb = 128 * H * 128 * 2
+    count = [nl.packet_bytes(H, bits[layer]) for layer in range(L)]
+    strides = [nl.record_bytes(c) for c in count]
+    records = [torch.empty((n, strides[layer]), dtype=torch.uint8, device="cuda") for layer in range(L)]
+    host = []
+    for layer in range(L):
+        pair = []
+        for k in range(2):
+            t = torch.zeros((B, count[layer]), dtype=torch.uint8).pin_memory()
+            nl.register_host_range(t, layer, k)
+            pair.append(t)
+        host.append(pair)
+    srcs = [nl._ptrs(cache[layer][k].data_ptr() + perm[i] * bb for k in range(2) for i in range(B)) for layer in range(L)]
+    hdst = [nl._ptrs(host[layer][k].data_ptr() + i * count[layer] for k in range(2) for i in range(B))
+            for layer in range(L)]
+    codecs = [_native.Codec(bits[layer], _native.KIND_KV, H, layer) for layer in range(L)]
+    cargs = [ct.byref(c) for c in codecs]
+    tickets = [(ct.c_uint64 * n)() for _ in range(L)]
+    rec_ptr = [r.data_ptr() for r in records]
+    torch.cuda.synchronize()
+
+    def device_step():
+        for layer in range(L):
+            assert lib.secure_infer_writeback_records(srcs[layer], hdst[layer], n, cargs[layer], rec_ptr[layer],
+                                                      strides[layer], tickets[layer], sp) == 0
+        return 3 * L
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        device_step()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
+    barrier()
+    torch.cuda.synchronize()
+    launches = 0
+    with ClockSampler(gpu_id) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            launches += device_step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    dev_ms = max_over_ranks(start.elapsed_time(end), dist)
+    ms_per_step = dev_ms / args.steps
+    wire = sum(count[layer] * n for layer in range(L))
+    algo = L * n * bb + wire          # bf16 read + wire written
+    value = world * algo / (ms_per_step * 1e-3) / 1e9
+    prof = kernel_profile(lib, torch, device_step, L)
+
+    # ---- end to end: device writeback + D2H + host verify into the host pool ----
+    def e2e_step():
+        for layer in range(L):
+            assert lib.secure_infer_d2h_writeback_layer(srcs[layer], hdst[layer], n, cargs[layer], sp) == 0
+        assert lib.secure_infer_d2h_wait() == 0
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), dist) / args.steps
+    e2e_value = world * algo / (e2e_ms * 1e-3) / 1e9
+
+    # Round trip: the host pool of layer 0 reloads through the authenticated
+    # path and dequantises to within half a quantisation step of the source.
+    back = [torch.zeros((B, 128, H, 128), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    rsrc = nl._ptrs(host[0][k].data_ptr() + i * count[0] for k in range(2) for i in range(B))
+    rdst = nl._ptrs(back[k].data_ptr() + i * bb for k in range(2) for i in range(B))
+    assert lib.secure_infer_h2d_reload_layer(0, rsrc, rdst, n, count[0], cargs[0], 0, None, sp) == 0
+    assert lib.secure_infer_recovery_wait_layer_authentication(0) == 0
+    torch.cuda.synchronize()
+    tol = 0.6 if bits[0] == 4 else 0.05
+    for k in range(2):
+        err = (back[k].float() - cache[0][k][perm].float()).abs().max().item()
+        assert err < tol, f"round trip error {err} (kind {k})"
+
+    result = None
+    if rank == 0:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        hbm_peak = peaks.get("hbm_gbs", 6650.0)
+        dominant = max(prof, key=lambda k: prof[k][0])
+        dom_us = prof[dominant][0]
+        achieved = (algo / L) / (dom_us * 1e-6) / 1e9
+        clk = clocks.summary()
+        sm_hz = (clk["sm_mhz"] or clk["sm_max_mhz"] or 1965.0) * 1e6
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        payload_blocks = sum((c + 15) // 16 for c in count) * n / L
+        per_block = {"gcm_layer_ctr_kernel": (5.5, payload_blocks + n), "gcm_layer_encrypt": (4.0, payload_blocks + 5 * n)}
+        smem = {k: round(w * b / (prof[k][0] * 1e-6 * sms * sm_hz), 4) for k, (w, b) in per_block.items() if k in prof}
+        result = {
+            "metric": "Verified KV writeback GB/s/GPU (gather+quantise+AES-GCM encrypt+tag); per-layer us",
+            "value": round(value, 3),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "per_layer_us": round(ms_per_step * 1e3 / L, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "u8",
+            "data": "synthetic: N(0,1) bf16 KV from seed, seeded AES-128 key/salt per rank, shuffled block table",
+            "config": {"workload": f"{args.config}: {cfg['model']} writeback, {L} layers x {H} KV heads x 128 dim, "
+                                   f"{B} blocks x 128 tokens, KV_CODEC={cfg['codec']}, per-rank session",
+                       "layers": L, "kv_heads": H, "blocks": B, "records_per_layer": n,
+                       "packet_bytes": sorted(set(count)), "codec": cfg["codec"], "algorithmic_bytes_per_step": algo,
+                       "l2": "inputs larger than L2 (%.0f MB of bf16 KV read per step)" % (L * n * bb / 1e6),
+                       "parallelism": f"{world} independent per-GPU sessions, no collective"},
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                    "per_layer_us": round(e2e_ms * 1e3 / L, 2),
+                    "h2d_bytes_per_step": L * n * (64 + 8),
+                    "d2h_bytes_per_step": sum(strides[layer] * n for layer in range(L)),
+                    "path": "secure_infer_d2h_writeback_layer (device quantise + encrypt + tag, D2H to a pinned "
+                            "ring, OpenSSL verify + decrypt on host threads into the pinned host pool) + "
+                            "secure_infer_d2h_wait per step"},
+            "gpu_launches": launches,
+            "kernels": {k + "_us_per_layer": round(v[0], 2) for k, v in prof.items()},
+            "roofline": {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": NCU_TRAFFIC_BYTES.get(
+                             (args.config, dominant)), "smem_pipe_frac": smem,
+                         "note": "achieved = per-layer algorithmic bytes (bf16 read + wire written) / dominant kernel "
+                                 "time; peak = measured HBM copy bandwidth (of measured); kernels timed by the "
+                                 "library's launch events behind a device sleep."},
+            "clocks": clocks.summary(),
+        }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_reference_writeback(cfg, args, sample_layers=args.cpu_layers)["cpu_baseline"]
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    lib.secure_infer_session_shutdown()
+    return result
+
+
+def cpu_reference_writeback(cfg, args, sample_layers=2, steps=1):
+    """The reference's CPU side of a writeback on all host cores: the codec
+    encode (transport_codec.py:22-42, its torch CPU ops restated with
+    torch.set_num_threads(all cores)) of the layer's K and V
+    blocks, OpenSSL AES-128-GCM encrypt of every packet (standing in for the
+    device encrypt_tag) and the host's OpenSSL decrypt + verify into the host
+    pool (secure_infer.cpp:2470-2547).  A bounded sample of `sample_layers`
+    layers per step, scaled by the per-layer algorithmic bytes."""
+    import torch
+    from oracle import codec_oracle, gcm as orc
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
+    L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
+    n = 2 * B
+    rng = np.random.default_rng(11)
+    key = np.frombuffer(bytes(range(16)), np.uint8).copy()
+    x = (rng.standard_normal((2, B + 16, 128, H, 128)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    perm = rng.permutation(B + 16)[:B]
+    bits_per_layer = [layer_bits(cfg["codec"], layer, L) for layer in range(L)]
+    sample = [layer for layer in range(L)][:sample_layers]
+    ivs = np.zeros((n, 16), np.uint8)
+    for i in range(n):
+        ivs[i] = np.frombuffer(orc.derive_transfer_iv(b"\x01\x02\x03\x04", i + 1), np.uint8)
+    st = np.zeros(n, np.uint32)
+    bb = 128 * H * 128 * 2
+
+    def one_layer(layer):
+        b = bits_per_layer[layer]
+        pk0, _, _ = codec_oracle.encode_torch(x[0], perm, b, 0, layer)
+        pk1, _, _ = codec_oracle.encode_torch(x[1], perm, b, 1, layer)
+        pk = np.ascontiguousarray(np.concatenate([pk0, pk1]))
+        count = pk.shape[1]
+        recs = np.zeros((n, orc.record_bytes(count)), np.uint8)
+        aligned = orc.record_aligned_bytes(count)
+        for i in range(n):
+            recs[i, aligned + 32:] = np.frombuffer(orc.build_gcm_aad(2, i // B, layer, i % B, 0, count, i + 1),
+                                                   np.uint8)
+        orc.host_batch(key, ivs, recs, count, [pk[i] for i in range(n)], st, threads, encrypt=True)
+        outs = [np.zeros(count, np.uint8) for _ in range(n)]
+        orc.host_batch(key, ivs, recs, count, outs, st, threads, encrypt=False)
+        assert st.all()
+        return n * bb + n * count
+
+    one_layer(sample[0])   # warm up
+    t0 = time.perf_counter()
+    algo = 0
+    for _ in range(steps):
+        for layer in sample:
+            algo += one_layer(layer)
+    elapsed = time.perf_counter() - t0
+    value = algo / elapsed / 1e9
+    per_layer_ms = elapsed / (steps * len(sample)) * 1e3
+    return {"value": round(value, 3), "ms_per_step": round(per_layer_ms * L, 3),
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{steps * len(sample)} layers of {args.config} ({n} blocks each: torch CPU "
+                                       f"reference encode + OpenSSL GCM encrypt + OpenSSL decrypt/verify), "
+                                       f"scaled by algorithmic bytes"}}
 
 
 def cpu_reference(cfg, args, sample_steps=3):
@@ -489,6 +739,17 @@ def run_reference(args, cfg):
     rank, world, _ = dist_env()
     if rank != 0:
         return None
+    if cfg.get("direction") == "d2h":
+        r = cpu_reference_writeback(cfg, args, sample_layers=args.cpu_layers, steps=args.steps)
+        L = cfg["layers"]
+        return {"impl": "reference",
+                "metric": "Verified KV writeback GB/s/GPU (gather+quantise+AES-GCM encrypt+tag); per-layer us",
+                "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": r["ms_per_step"], "per_layer_us": round(r["ms_per_step"] * 1e3 / L, 2),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+                "data": "synthetic N(0,1) bf16 KV", "config": {"workload": args.config, **cfg},
+                "cpu_baseline": r["cpu_baseline"],
+                "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     r = cpu_reference(cfg, args, sample_steps=args.steps)
     L = cfg["layers"]
     return {"impl": "reference",
@@ -509,6 +770,8 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     parser.add_argument("--cpu-steps", type=int, default=3)
+    parser.add_argument("--cpu-layers", type=int, default=2,
+                        help="writeback configs: layers per CPU-baseline step (a bounded sample)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--layers", type=int, default=None,
                         help="override the layer count (smaller cases for profiling)")
@@ -519,6 +782,8 @@ def main():
         cfg["layers"] = args.layers
     if args.impl == "reference":
         out = run_reference(args, cfg)
+    elif cfg.get("direction") == "d2h":
+        out = run_gpu_writeback(args, cfg)
     else:
         out = run_gpu(args, cfg)
     if out is not None:

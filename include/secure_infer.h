@@ -202,6 +202,18 @@ int secure_infer_writeback_records(const void* const* srcs, void* const* host_ds
                                    const secure_infer_codec* codec, void* records, uint64_t record_stride,
                                    uint64_t* tickets_out, void* stream);
 
+/* ------------------------------------------------------ kernel profile */
+
+/* No reference counterpart (the reference's h2d profile hooks below print
+ * transfer timings): while enabled, every kernel launch of this library is
+ * bracketed by CUDA timing events on its stream.  collect() waits for the
+ * recorded launches, fills total_us[k] / launches[k] for kinds
+ * k < `kinds` (names from secure_infer_kernel_name; null past the last
+ * kind) and clears the record.  Returns 0, or -1 if an event failed. */
+int secure_infer_kernel_profile_enable(int on);
+int secure_infer_kernel_profile_collect(double* total_us, uint64_t* launches, uint32_t kinds);
+const char* secure_infer_kernel_name(uint32_t kind);
+
 /* ------------------------------------------------- prediction scope */
 
 /* secure_infer.cpp:1102-1146.  Keystreams here are derived from tickets at

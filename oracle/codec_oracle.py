@@ -88,6 +88,39 @@ def encode(source_bf16: np.ndarray, indices, bits: int, kind: int, layer: int):
     return packet, qb, sb
 
 
+def encode_torch(source_bf16, indices, bits: int, kind: int, layer: int):
+    """transport_codec.py:22-42 with torch CPU ops, as the reference runs it
+    (amin/amax over the group axis, true division, round-half-even, clamp);
+    multi-threaded by torch.  source_bf16: uint16 numpy array or bf16 tensor
+    [num_blocks, 128, heads, dim].  Same packets as ``encode``."""
+    import torch
+    src = source_bf16 if isinstance(source_bf16, torch.Tensor) else \
+        torch.from_numpy(np.ascontiguousarray(source_bf16).view(np.int16)).view(torch.bfloat16)
+    x = src[torch.as_tensor(np.asarray(indices, dtype=np.int64))].float()
+    b, t, h, d = x.shape
+    if kind == 0:
+        xg, axis = x.view(b, t // GROUP, GROUP, h, d), 2
+    else:
+        xg, axis = x.view(b, t, h, d // GROUP, GROUP), 4
+    low = xg.amin(dim=axis, keepdim=True)
+    high = xg.amax(dim=axis, keepdim=True)
+    levels = float((1 << bits) - 1)
+    scale = torch.clamp((high - low) / levels, min=1e-12)
+    q = torch.clamp(torch.round((xg - low) / scale), 0, levels).reshape(b, -1)
+    if bits == 4:
+        q = q[:, 0::2] + 16 * q[:, 1::2]
+    q = q.to(torch.uint8)
+    qb = q.shape[1]
+    sb = scale[0].numel() * 4
+    width = (qb + 2 * sb + 16 + 15) // 16 * 16
+    packet = torch.zeros((b, width), dtype=torch.uint8)
+    packet[:, :qb] = q
+    packet[:, qb:qb + sb] = scale.reshape(b, -1).contiguous().view(torch.uint8)
+    packet[:, qb + sb:qb + 2 * sb] = low.reshape(b, -1).contiguous().view(torch.uint8)
+    packet[:, qb + 2 * sb:qb + 2 * sb + 16] = torch.tensor([1, layer, kind, bits], dtype=torch.int32).view(torch.uint8)
+    return packet.numpy(), qb, sb
+
+
 def decode_into(wire: np.ndarray, destination_bf16: np.ndarray, indices, bits: int,
                 kind: int, qbytes: int, sbytes: int) -> None:
     """wire: uint8 [b, width]; destination_bf16: uint16 [num_blocks, 128, H, D]."""

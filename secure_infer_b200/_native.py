@@ -71,6 +71,9 @@ HOST_SIGNATURES: dict[str, tuple[list, object]] = {
     "secure_infer_d2h_writeback_layer": ([PP, PP, U32, P, P], I32),
     "secure_infer_d2h_wait": ([], I32),
     "secure_infer_writeback_records": ([PP, PP, U32, P, P, U64, U64P, P], I32),
+    "secure_infer_kernel_profile_enable": ([I32], I32),
+    "secure_infer_kernel_profile_collect": ([ct.POINTER(ct.c_double), U64P, U32], I32),
+    "secure_infer_kernel_name": ([U32], ct.c_char_p),
     "secure_infer_invalidate_transfer_prefetches": ([], None),
     "secure_infer_retire_transfer_prefetches": ([], None),
     "secure_infer_get_transfer_prefetch_stats": ([U64P] * 3, None),

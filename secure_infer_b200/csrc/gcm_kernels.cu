@@ -19,7 +19,9 @@
 
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <mutex>
+#include <vector>
 
 namespace sib {
 
@@ -1079,6 +1081,52 @@ DeviceInfo& device_info(int dev)
     return d;
 }
 
+// ---------------------------------------------------------------- profile
+struct ProfileRec {
+    uint32_t kind;
+    cudaEvent_t start, end;
+};
+std::atomic<bool> g_prof_on{false};
+std::mutex g_prof_mu;
+std::vector<ProfileRec> g_prof_recs;
+std::vector<cudaEvent_t> g_prof_pool;
+
+cudaEvent_t prof_event()
+{
+    if (!g_prof_pool.empty()) {
+        cudaEvent_t e = g_prof_pool.back();
+        g_prof_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+// Brackets one launch with timing events when profiling is on.
+class ProfileScope {
+public:
+    ProfileScope(uint32_t kind, cudaStream_t stream) : stream_(stream)
+    {
+        if (!g_prof_on.load(std::memory_order_relaxed)) return;
+        std::lock_guard<std::mutex> lock(g_prof_mu);
+        rec_ = ProfileRec{kind, prof_event(), prof_event()};
+        active_ = rec_.start && rec_.end && cudaEventRecord(rec_.start, stream) == cudaSuccess;
+    }
+    ~ProfileScope()
+    {
+        if (!active_) return;
+        std::lock_guard<std::mutex> lock(g_prof_mu);
+        cudaEventRecord(rec_.end, stream_);
+        g_prof_recs.push_back(rec_);
+    }
+
+private:
+    cudaStream_t stream_;
+    ProfileRec rec_{};
+    bool active_ = false;
+};
+
 template <bool A, bool C>
 int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cudaStream_t stream)
 {
@@ -1109,11 +1157,45 @@ int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cud
     }
     const uint32_t grid = static_cast<uint32_t>(
         args.total_segs < static_cast<uint32_t>(sms * per_sm) ? args.total_segs : sms * per_sm);
+    ProfileScope prof(kKernSegment, stream);
     gcm_segment_kernel<A, C><<<grid, kThreads, smem, stream>>>(args);
     return cudaGetLastError();
 }
 
 }  // namespace
+
+void profile_enable(bool on) { g_prof_on.store(on); }
+
+int profile_collect(double* total_us, uint64_t* launches, uint32_t kinds)
+{
+    std::lock_guard<std::mutex> lock(g_prof_mu);
+    for (uint32_t k = 0; k < kinds; ++k) {
+        if (total_us) total_us[k] = 0.0;
+        if (launches) launches[k] = 0;
+    }
+    int rc = 0;
+    for (const ProfileRec& r : g_prof_recs) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(r.end) != cudaSuccess || cudaEventElapsedTime(&ms, r.start, r.end) != cudaSuccess)
+            rc = -1;
+        else if (r.kind < kinds) {
+            if (total_us) total_us[r.kind] += 1e3 * ms;
+            if (launches) ++launches[r.kind];
+        }
+        g_prof_pool.push_back(r.start);
+        g_prof_pool.push_back(r.end);
+    }
+    g_prof_recs.clear();
+    return rc;
+}
+
+const char* kernel_kind_name(uint32_t kind)
+{
+    static const char* names[kKernKinds] = {"gcm_layer_ctr_kernel", "gcm_layer_verify_kernel", "gcm_layer_encrypt",
+                                            "kv_encode_kernel", "gcm_segment_kernel", "gcm_ctr_kernel",
+                                            "gcm_schedule_kernel", "auth_gate_kernel"};
+    return kind < kKernKinds ? names[kind] : nullptr;
+}
 
 size_t schedule_bytes() { return sizeof(GcmSchedule); }
 
@@ -1126,6 +1208,7 @@ uint32_t segments_for(uint64_t count, uint32_t aad_bytes)
 
 int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream)
 {
+    ProfileScope prof(kKernSchedule, stream);
     gcm_schedule_kernel<<<1, 256, 0, stream>>>(static_cast<const uint8_t*>(key), static_cast<const uint8_t*>(h),
                                                sched, need_tables ? 1 : 0);
     return cudaGetLastError();
@@ -1168,6 +1251,7 @@ int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStrea
     const uint64_t want = (args.total_blocks + kCtrThreads - 1) / kCtrThreads;
     const uint64_t cap = static_cast<uint64_t>(sms);
     const uint32_t grid = static_cast<uint32_t>(want < cap ? want : cap);
+    ProfileScope prof(kKernCtr, stream);
     gcm_ctr_kernel<<<grid, kCtrThreads, kCtrSmem, stream>>>(args, uniform_blocks);
     return cudaGetLastError();
 }
@@ -1194,8 +1278,8 @@ void layer_segments_for(uint64_t count, uint32_t n, uint32_t* seg_steps, uint32_
 }
 
 template <int kCap, class Kernel>
-int layer_launch(Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint32_t threads, size_t smem,
-                 uint32_t items, bool& attr_set, cudaStream_t stream, uint32_t ctas_per_sm = 1)
+int layer_launch(uint32_t kind, Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint32_t threads,
+                 size_t smem, uint32_t items, bool& attr_set, cudaStream_t stream, uint32_t ctas_per_sm = 1)
 {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1232,6 +1316,7 @@ int layer_launch(Kernel kernel, const LayerHeader& h, const LayerRec* rec, uint3
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    ProfileScope prof(kind, stream);
     return cudaLaunchKernelEx(&cfg, kernel, L);
 }
 
@@ -1245,9 +1330,9 @@ int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream
     int dev = 0;
     cudaGetDevice(&dev);
     if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
-        return layer_launch<kLayerCapSmall>(gcm_layer_ctr_kernel<kLayerCapSmall>, h, rec, kCtrThreads, kCtrSmem, items,
+        return layer_launch<kLayerCapSmall>(kKernLayerCtr, gcm_layer_ctr_kernel<kLayerCapSmall>, h, rec, kCtrThreads, kCtrSmem, items,
                                             set_small[dev & 63], stream);
-    return layer_launch<kLayerCapLarge>(gcm_layer_ctr_kernel<kLayerCapLarge>, h, rec, kCtrThreads, kCtrSmem, items,
+    return layer_launch<kLayerCapLarge>(kKernLayerCtr, gcm_layer_ctr_kernel<kLayerCapLarge>, h, rec, kCtrThreads, kCtrSmem, items,
                                         set_large[dev & 63], stream);
 }
 
@@ -1265,15 +1350,15 @@ int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t 
     const bool small = h.n <= static_cast<uint32_t>(kLayerCapSmall);
     if (h.codec.bits) {
         if (small)
-            return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec>, h, rec,
+            return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec>, h, rec,
                                                 kLayerThreads, kLayerSmem, grid, set_small_c[dev & 63], stream, 1);
-        return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec>, h, rec,
+        return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec>, h, rec,
                                             kLayerThreads, kLayerSmem, grid, set_large_c[dev & 63], stream, 1);
     }
     if (small)
-        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyRaw>, h, rec,
+        return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyRaw>, h, rec,
                                             kLayerThreads, kLayerSmem, grid, set_small[dev & 63], stream, 1);
-    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyRaw>, h, rec,
+    return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyRaw>, h, rec,
                                         kLayerThreads, kLayerSmem, grid, set_large[dev & 63], stream, 1);
 }
 
@@ -1287,9 +1372,9 @@ int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t
     cudaGetDevice(&dev);
     const uint32_t grid = (items + kLayerWarps - 1) / kLayerWarps;
     if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
-        return layer_launch<kLayerCapSmall>(gcm_layer_verify_kernel<kLayerCapSmall, kLayerEncrypt>, h, rec,
+        return layer_launch<kLayerCapSmall>(kKernLayerEncrypt, gcm_layer_verify_kernel<kLayerCapSmall, kLayerEncrypt>, h, rec,
                                             kLayerThreads, kLayerSmem, grid, set_small[dev & 63], stream, 1);
-    return layer_launch<kLayerCapLarge>(gcm_layer_verify_kernel<kLayerCapLarge, kLayerEncrypt>, h, rec,
+    return layer_launch<kLayerCapLarge>(kKernLayerEncrypt, gcm_layer_verify_kernel<kLayerCapLarge, kLayerEncrypt>, h, rec,
                                         kLayerThreads, kLayerSmem, grid, set_large[dev & 63], stream, 1);
 }
 
@@ -1309,6 +1394,7 @@ int launch_encode(const EncodeLaunch& args, cudaStream_t stream)
     if (args.n == 0) return cudaSuccess;
     const uint32_t groups = 128u * args.codec.heads * 128u / 64u;
     const dim3 grid((groups + 255) / 256, args.n);
+    ProfileScope prof(kKernEncode, stream);
     kv_encode_kernel<<<grid, 256, 0, stream>>>(args);
     return cudaGetLastError();
 }
@@ -1317,6 +1403,7 @@ int launch_auth_gate(uint8_t* data, const uint32_t* status, uint64_t bytes, cuda
 {
     const uint64_t want = (bytes + 255) / 256;
     const uint32_t grid = static_cast<uint32_t>(want < 1024 ? (want ? want : 1) : 1024);
+    ProfileScope prof(kKernAuthGate, stream);
     auth_gate_kernel<<<grid, 256, 0, stream>>>(data, status, bytes);
     return cudaGetLastError();
 }

@@ -150,6 +150,16 @@ int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream
 int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 
+// Kernel profile: while enabled, every launch below is bracketed by timing
+// events on its stream; collect() sums device time and launches per kind.
+enum KernelKind : uint32_t {
+    kKernLayerCtr = 0, kKernLayerVerify, kKernLayerEncrypt, kKernEncode, kKernSegment, kKernCtr, kKernSchedule,
+    kKernAuthGate, kKernKinds
+};
+void profile_enable(bool on);
+int profile_collect(double* total_us, uint64_t* launches, uint32_t kinds);
+const char* kernel_kind_name(uint32_t kind);
+
 // Host-side launchers (gcm_kernels.cu).  Return a cudaError_t value.
 // key may be null (GHASH-only requests); h null -> H = E_K(0^128) on device.
 int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream);

@@ -1421,6 +1421,19 @@ SI_EXPORT int secure_infer_d2h_writeback_layer(const void* const* src_blocks, vo
 
 SI_EXPORT int secure_infer_d2h_wait(void) { return d2h_join(0, false); }
 
+SI_EXPORT int secure_infer_kernel_profile_enable(int on)
+{
+    sib::profile_enable(on != 0);
+    return 0;
+}
+
+SI_EXPORT int secure_infer_kernel_profile_collect(double* total_us, uint64_t* launches, uint32_t kinds)
+{
+    return sib::profile_collect(total_us, launches, kinds);
+}
+
+SI_EXPORT const char* secure_infer_kernel_name(uint32_t kind) { return sib::kernel_kind_name(kind); }
+
 SI_EXPORT int secure_infer_writeback_records(const void* const* srcs, void* const* host_dsts, uint32_t n,
                                              const secure_infer_codec* codec, void* records, uint64_t record_stride,
                                              uint64_t* tickets_out, void* stream)

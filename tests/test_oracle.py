@@ -141,6 +141,18 @@ def test_codec_oracle_bit_exact_vs_reference(heads, kind, bits):
     assert not dest[others].any()
 
 
+@pytest.mark.parametrize("heads", [1, 2])
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("bits", [8, 4])
+def test_codec_torch_encode_bit_exact_vs_reference(heads, kind, bits):
+    """The torch CPU restatement (the CPU baseline's encode) gives the
+    reference's own packets."""
+    pytest.importorskip("torch")
+    g = load_codec(heads)
+    packet, qb, sb = codec_oracle.encode_torch(g["source"], g["enc_idx"], bits, kind, layer=5)
+    assert np.array_equal(packet, g[f"packet_k{kind}_b{bits}"])
+
+
 def test_packet_geometry_matches_survey_sizes():
     # Llama-3-8B (8 heads): int8 147472 B, int4 81936 B; Qwen 4 heads int8 73744 B;
     # 70B/TP8 (1 head) int4 10256 B.
