@@ -940,113 +940,156 @@ __device__ __forceinline__ float quantise(float x, float low, float scale, float
     return fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(x, low), scale)), 0.0f), levels);
 }
 
-__global__ void __launch_bounds__(256) kv_encode_kernel(const __grid_constant__ EncodeLaunch L)
+// Tiled quantisation: one CTA of 256 threads per (record, 64-token group,
+// CW-channel chunk).  Thread (row slot, lane-in-row) loads 16 bytes (8
+// channels) of each of its rows with coalesced 16-byte loads and keeps the 64
+// (or 32) values in registers.  K groups (64 tokens of one channel) reduce
+// over the thread's rows, the lanes sharing its channels (shuffles) and the
+// warps (shared memory); V groups (64 dims of one token/head) reduce over the
+// 8 lanes that hold the group.  Quantised bytes go out as 8-byte (int8) or
+// 4-byte (int4) coalesced stores, element e = token * hd + channel.
+// q = clamp(round_half_even(fl((x - low) / scale)), 0, levels) without a
+// division per element: y = fl(fl(x - low) * fl(1 / scale)) differs from the
+// correctly rounded quotient Q by at most Q * 1.8e-7 <= 4.7e-5 (Q <= 256:
+// two roundings of 2^-24 relative error each, on top of Q's own rounding), so
+// round(y) == round(Q) unless y lies within 2^-13 of a half-integer; those
+// rare elements (and exact ties) take the IEEE division.
+__device__ __forceinline__ float quantise_fast(float x, float low, float scale, float inv_scale, float levels)
 {
+    const float d = __fsub_rn(x, low);
+    const float y = __fmul_rn(d, inv_scale);
+    const float frac = y - floorf(y);
+    const float q = fabsf(frac - 0.5f) < 0x1p-13f ? rintf(__fdiv_rn(d, scale)) : rintf(y);
+    return fminf(fmaxf(q, 0.0f), levels);
+}
+
+// Tiled quantisation: one CTA of 256 threads per (record, 64-token group,
+// CW-channel chunk).  Thread (row slot, lane-in-row) loads 16 bytes (8
+// channels) of each of its rows with coalesced 16-byte loads and keeps them
+// (packed bf16) in registers.  K groups (64 tokens of one channel) reduce
+// over the thread's rows and the row slots (shared memory); V groups (64
+// dims of one token/head) reduce over the 8 lanes that hold the group.
+// Quantised bytes go out as 8-byte (int8) or 4-byte (int4) coalesced stores,
+// element e = token * hd + channel.
+template <int CW>
+__global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant__ EncodeLaunch L)
+{
+    constexpr int kTpr = CW / 8;                 // threads per row
+    constexpr int kRowsPerPass = 256 / kTpr;
+    constexpr int kPasses = 64 / kRowsPerPass;
+    __shared__ float red_lo[kRowsPerPass][CW], red_hi[kRowsPerPass][CW];
+    __shared__ float fin_lo[CW], fin_sc[CW];
+
     const CodecParams cp = L.codec;
-    const uint32_t hd = cp.heads * 128u, elements = 128u * hd, groups = elements / 64u;
+    const uint32_t hd = cp.heads * 128u;
+    const uint32_t chunks = hd / CW;
     const uint32_t rec = blockIdx.y;
+    const uint32_t tg = blockIdx.x / chunks, chunk = blockIdx.x % chunks;
     const uint32_t kind = rec >= L.v_first ? 1u : 0u;
-    const uint16_t* src = reinterpret_cast<const uint16_t*>(L.srcs[rec]);
+    const uint32_t tid = threadIdx.x, slot = tid / kTpr, tl = tid % kTpr;
+    const uint32_t c0 = chunk * CW + 8u * tl;                 // first of the thread's 8 channels
+    const uint8_t* src = static_cast<const uint8_t*>(L.srcs[rec]);
     uint8_t* pkt = L.packets + static_cast<size_t>(rec) * L.width;
     float* scale = reinterpret_cast<float*>(pkt + cp.qb);
     float* lowp = reinterpret_cast<float*>(pkt + cp.qb + cp.sb);
     const float levels = static_cast<float>((1u << cp.bits) - 1u);
-    const uint32_t lane = threadIdx.x & 31u;
 
-    for (uint32_t g = blockIdx.x * blockDim.x + threadIdx.x; g < groups; g += gridDim.x * blockDim.x) {
-        if (kind == 0) {
-            // 64 tokens of channel ch in token group tg; element e = (64 tg + t) hd + ch.
-            const uint32_t tg = g / hd, ch = g % hd;
-            const uint16_t* col = src + static_cast<size_t>(tg) * 64u * hd + ch;
-            float lo = __int_as_float(0x7f800000), hi = -lo;
-            for (int t = 0; t < 64; ++t) {
-                const float x = bf16_bits_to_f32(__ldg(col + static_cast<size_t>(t) * hd));
-                lo = fminf(lo, x);
-                hi = fmaxf(hi, x);
+    uint4 raw[kPasses];
+#pragma unroll
+    for (int p = 0; p < kPasses; ++p) {
+        const uint32_t t = tg * 64u + p * kRowsPerPass + slot;
+        raw[p] = __ldg(reinterpret_cast<const uint4*>(src + (static_cast<size_t>(t) * hd + c0) * 2u));
+    }
+    auto val = [&](int p, int c) {
+        const uint32_t w = c < 2 ? raw[p].x : c < 4 ? raw[p].y : c < 6 ? raw[p].z : raw[p].w;
+        return bf16_bits_to_f32((c & 1) ? (w >> 16) : (w & 0xffffu));
+    };
+
+    float lo[8], sc[8], inv[8];   // K: low, scale, 1/scale of the thread's 8 channels
+    if (kind == 0) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            float l = val(0, c), h = l;
+#pragma unroll
+            for (int p = 1; p < kPasses; ++p) {
+                l = fminf(l, val(p, c));
+                h = fmaxf(h, val(p, c));
             }
-            const float sc = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), levels), 1e-12f);
-            scale[g] = sc;
-            lowp[g] = lo;
-            uint8_t* qcol = pkt;
-            for (int t = 0; t < 64; ++t) {
-                const size_t e = (static_cast<size_t>(tg) * 64u + t) * hd + ch;
-                const uint32_t q = static_cast<uint32_t>(
-                    quantise(bf16_bits_to_f32(__ldg(col + static_cast<size_t>(t) * hd)), lo, sc, levels));
-                if (cp.bits == 8) {
-                    qcol[e] = static_cast<uint8_t>(q);
-                } else {
-                    // Elements e (even ch) and e + 1 share a byte: low nibble = even.
-                    const uint32_t partner = __shfl_down_sync(0xffffffffu, q, 1);
-                    if ((lane & 1u) == 0) qcol[e >> 1] = static_cast<uint8_t>(q | (partner << 4));
-                }
+            red_lo[slot][8 * tl + c] = l;
+            red_hi[slot][8 * tl + c] = h;
+        }
+        __syncthreads();
+        if (tid < CW) {
+            float l = red_lo[0][tid], h = red_hi[0][tid];
+#pragma unroll
+            for (int r = 1; r < kRowsPerPass; ++r) {
+                l = fminf(l, red_lo[r][tid]);
+                h = fmaxf(h, red_hi[r][tid]);
             }
+            const float s1 = fmaxf(__fdiv_rn(__fsub_rn(h, l), levels), 1e-12f);
+            fin_lo[tid] = l;
+            fin_sc[tid] = s1;
+            const uint32_t sidx = tg * hd + chunk * CW + tid;
+            scale[sidx] = s1;
+            lowp[sidx] = l;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            lo[c] = fin_lo[8 * tl + c];
+            sc[c] = fin_sc[8 * tl + c];
+            inv[c] = __frcp_rn(sc[c]);
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < kPasses; ++p) {
+        const uint32_t t = tg * 64u + p * kRowsPerPass + slot;
+        if (kind != 0) {
+            // 64-dim group = 8 lanes (aligned, consecutive in the row).
+            float l = val(p, 0), h = l;
+#pragma unroll
+            for (int c = 1; c < 8; ++c) { l = fminf(l, val(p, c)); h = fmaxf(h, val(p, c)); }
+#pragma unroll
+            for (int m = 1; m < 8; m <<= 1) {
+                l = fminf(l, __shfl_xor_sync(0xffffffffu, l, m));
+                h = fmaxf(h, __shfl_xor_sync(0xffffffffu, h, m));
+            }
+            const float s1 = fmaxf(__fdiv_rn(__fsub_rn(h, l), levels), 1e-12f);
+            if ((tl & 7u) == 0) {
+                const uint32_t sidx = (t * hd + c0) / 64u;
+                scale[sidx] = s1;
+                lowp[sidx] = l;
+            }
+            const float r1 = __frcp_rn(s1);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) { lo[c] = l; sc[c] = s1; inv[c] = r1; }
+        }
+        const size_t e0 = static_cast<size_t>(t) * hd + c0;
+        if (cp.bits == 8) {
+            uint32_t wv[2] = {0u, 0u};
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                wv[c >> 2] |= static_cast<uint32_t>(quantise_fast(val(p, c), lo[c], sc[c], inv[c], levels))
+                              << (8 * (c & 3));
+            *reinterpret_cast<uint2*>(pkt + e0) = make_uint2(wv[0], wv[1]);
         } else {
-            // 64 consecutive dims of one (token, head): element e = 64 g + i.
-            const uint4* p4 = reinterpret_cast<const uint4*>(src + static_cast<size_t>(g) * 64u);
-            float x[64];
+            uint32_t word = 0;
 #pragma unroll
-            for (int v = 0; v < 8; ++v) {
-                const uint4 d = __ldg(p4 + v);
-                const uint32_t ws[4] = {d.x, d.y, d.z, d.w};
-#pragma unroll
-                for (int h2 = 0; h2 < 4; ++h2) {
-                    x[v * 8 + 2 * h2] = bf16_bits_to_f32(ws[h2] & 0xffffu);
-                    x[v * 8 + 2 * h2 + 1] = bf16_bits_to_f32(ws[h2] >> 16);
-                }
-            }
-            float lo = x[0], hi = x[0];
-#pragma unroll
-            for (int i = 1; i < 64; ++i) { lo = fminf(lo, x[i]); hi = fmaxf(hi, x[i]); }
-            const float sc = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), levels), 1e-12f);
-            scale[g] = sc;
-            lowp[g] = lo;
-            if (cp.bits == 8) {
-                uint4* dst = reinterpret_cast<uint4*>(pkt + static_cast<size_t>(g) * 64u);
-#pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                    uint32_t wv[4];
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        uint32_t word = 0;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            word |= static_cast<uint32_t>(quantise(x[v * 16 + b * 4 + i], lo, sc, levels)) << (8 * i);
-                        wv[b] = word;
-                    }
-                    dst[v] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-                }
-            } else {
-                uint4* dst = reinterpret_cast<uint4*>(pkt + static_cast<size_t>(g) * 32u);
-#pragma unroll
-                for (int v = 0; v < 2; ++v) {
-                    uint32_t wv[4];
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        uint32_t word = 0;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int e = v * 32 + b * 8 + 2 * i;
-                            const uint32_t byte = static_cast<uint32_t>(quantise(x[e], lo, sc, levels)) |
-                                                  (static_cast<uint32_t>(quantise(x[e + 1], lo, sc, levels)) << 4);
-                            word |= byte << (8 * i);
-                        }
-                        wv[b] = word;
-                    }
-                    dst[v] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-                }
-            }
+            for (int c = 0; c < 8; ++c)
+                word |= static_cast<uint32_t>(quantise_fast(val(p, c), lo[c], sc[c], inv[c], levels)) << (4 * c);
+            *reinterpret_cast<uint32_t*>(pkt + e0 / 2) = word;
         }
     }
     if (blockIdx.x == 0) {
         // int32 header {1, layer, kind, bits} then zero padding to width.
         const uint32_t hdr = cp.qb + 2u * cp.sb;
-        for (uint32_t i = threadIdx.x; i < L.width - hdr; i += blockDim.x) {
-            uint8_t v = 0;
+        for (uint32_t i = tid; i < L.width - hdr; i += blockDim.x) {
+            uint8_t b = 0;
             if (i < 16) {
                 const uint32_t word = i < 4 ? 1u : i < 8 ? L.layer : i < 12 ? kind : cp.bits;
-                v = static_cast<uint8_t>(word >> (8 * (i & 3)));
+                b = static_cast<uint8_t>(word >> (8 * (i & 3)));
             }
-            pkt[hdr + i] = v;
+            pkt[hdr + i] = b;
         }
     }
 }
@@ -1392,10 +1435,13 @@ int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t str
 int launch_encode(const EncodeLaunch& args, cudaStream_t stream)
 {
     if (args.n == 0) return cudaSuccess;
-    const uint32_t groups = 128u * args.codec.heads * 128u / 64u;
-    const dim3 grid((groups + 255) / 256, args.n);
+    const uint32_t hd = args.codec.heads * 128u;
     ProfileScope prof(kKernEncode, stream);
-    kv_encode_kernel<<<grid, 256, 0, stream>>>(args);
+    if (hd % 256u == 0) {
+        kv_encode_kernel<256><<<dim3(2u * (hd / 256u), args.n), 256, 0, stream>>>(args);
+    } else {
+        kv_encode_kernel<128><<<dim3(2u * (hd / 128u), args.n), 256, 0, stream>>>(args);
+    }
     return cudaGetLastError();
 }
 

@@ -160,3 +160,26 @@ def test_packet_geometry_matches_survey_sizes():
     assert codec_oracle.packet_geometry(8, 128, 4)[2] == 81936
     assert codec_oracle.packet_geometry(4, 128, 8)[2] == 73744
     assert codec_oracle.packet_geometry(1, 128, 4)[2] == 10256
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_reciprocal_quantise_matches_division(bits):
+    """The device encode replaces (x - low) / scale by (x - low) * fl(1/scale)
+    and falls back to the division only within 2^-13 of a half-integer; in
+    IEEE fp32 (numpy rounds like the device's _rn intrinsics) that gives the
+    same quantised levels as the reference's division on every sample."""
+    rng = np.random.default_rng(bits)
+    levels = np.float32((1 << bits) - 1)
+    n = 1_000_000
+    low = rng.standard_normal(n).astype(np.float32) * np.float32(3)
+    span = np.abs(rng.standard_normal(n).astype(np.float32)) * np.float32(rng.uniform(1e-6, 20, n).astype(np.float32))
+    high = (low + span).astype(np.float32)
+    scale = np.maximum(((high - low).astype(np.float32) / levels).astype(np.float32), np.float32(1e-12))
+    x = np.clip((low + rng.random(n).astype(np.float32) * (high - low)).astype(np.float32), low, high)
+    d = (x - low).astype(np.float32)
+    exact = np.rint((d / scale).astype(np.float32))
+    y = (d * (np.float32(1) / scale).astype(np.float32)).astype(np.float32)
+    near = np.abs((y - np.floor(y)).astype(np.float32) - np.float32(0.5)) < np.float32(2 ** -13)
+    fast = np.where(near, exact, np.rint(y))
+    assert np.array_equal(fast, exact)
+    assert near.mean() < 1e-3
