@@ -935,50 +935,85 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
 
-__device__ __forceinline__ float quantise(float x, float low, float scale, float levels)
-{
-    return fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(x, low), scale)), 0.0f), levels);
-}
-
-// Tiled quantisation: one CTA of 256 threads per (record, 64-token group,
-// CW-channel chunk).  Thread (row slot, lane-in-row) loads 16 bytes (8
-// channels) of each of its rows with coalesced 16-byte loads and keeps the 64
-// (or 32) values in registers.  K groups (64 tokens of one channel) reduce
-// over the thread's rows, the lanes sharing its channels (shuffles) and the
-// warps (shared memory); V groups (64 dims of one token/head) reduce over the
-// 8 lanes that hold the group.  Quantised bytes go out as 8-byte (int8) or
-// 4-byte (int4) coalesced stores, element e = token * hd + channel.
 // q = clamp(round_half_even(fl((x - low) / scale)), 0, levels) without a
 // division per element: y = fl(fl(x - low) * fl(1 / scale)) differs from the
 // correctly rounded quotient Q by at most Q * 1.8e-7 <= 4.7e-5 (Q <= 256:
 // two roundings of 2^-24 relative error each, on top of Q's own rounding), so
-// round(y) == round(Q) unless y lies within 2^-13 of a half-integer; those
-// rare elements (and exact ties) take the IEEE division.
-__device__ __forceinline__ float quantise_fast(float x, float low, float scale, float inv_scale, float levels)
+// round(y) == round(Q) unless y lies within 2^-13 of a half-integer; a row
+// holding such an element (or an exact tie) is redone with IEEE divisions.
+//
+// Rounding uses the fp32 adder: for 0 <= y < 2^22, m = fl(y + 1.5 * 2^23) holds
+// round_half_even(y) in its low mantissa bits, so neither a rounding nor a
+// conversion instruction is needed (y >= 0 because low is the group minimum).
+constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
+
+__device__ __forceinline__ uint32_t quantise_fast(float x, float low, float inv_scale, uint32_t levels, bool& near)
 {
-    const float d = __fsub_rn(x, low);
-    const float y = __fmul_rn(d, inv_scale);
-    const float frac = y - floorf(y);
-    const float q = fabsf(frac - 0.5f) < 0x1p-13f ? rintf(__fdiv_rn(d, scale)) : rintf(y);
-    return fminf(fmaxf(q, 0.0f), levels);
+    const float y = __fmul_rn(__fsub_rn(x, low), inv_scale);
+    const float m = __fadd_rn(y, kRoundMagic);
+    near |= fabsf(fabsf(__fsub_rn(y, __fsub_rn(m, kRoundMagic))) - 0.5f) < 0x1p-13f;
+    const uint32_t q = __float_as_uint(m) & 0x3fffffu;
+    return q < levels ? q : levels;
+}
+
+// The 8 elements of one row slice with the reference's division.  k_lo/k_sc:
+// per-channel parameters (K, shared memory) or null for one (v_lo, v_sc) (V).
+template <int BITS>
+__device__ __noinline__ uint2 quantise_row_exact(uint4 raw, const float* k_lo, const float* k_sc, float v_lo,
+                                                 float v_sc);
+
+template <int BITS>
+__device__ __forceinline__ uint2 quantise_row_exact(uint4 raw, const float (&k_lo)[8], const float (&k_sc)[8], float,
+                                                    float)
+{
+    // Per-channel parameters held in registers: go through the out-of-line
+    // version with a local copy (rare path).
+    float lo[8], sc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) { lo[c] = k_lo[c]; sc[c] = k_sc[c]; }
+    return quantise_row_exact<BITS>(raw, static_cast<const float*>(lo), static_cast<const float*>(sc), 0.0f, 0.0f);
+}
+
+template <int BITS>
+__device__ __noinline__ uint2 quantise_row_exact(uint4 raw, const float* k_lo, const float* k_sc, float v_lo,
+                                                 float v_sc)
+{
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    const uint32_t levels = (1u << BITS) - 1u;
+    uint2 out = make_uint2(0u, 0u);
+    for (int c = 0; c < 8; ++c) {
+        const float x = bf16_bits_to_f32((c & 1) ? (w[c >> 1] >> 16) : (w[c >> 1] & 0xffffu));
+        const float l = k_lo ? k_lo[c] : v_lo, sc = k_lo ? k_sc[c] : v_sc;
+        const float m = __fadd_rn(__fdiv_rn(__fsub_rn(x, l), sc), kRoundMagic);
+        uint32_t q = __float_as_uint(m) & 0x3fffffu;
+        q = q < levels ? q : levels;
+        if (BITS == 8) {
+            if (c < 4) out.x |= q << (8 * c); else out.y |= q << (8 * (c - 4));
+        } else {
+            out.x |= q << (4 * c);
+        }
+    }
+    return out;
 }
 
 // Tiled quantisation: one CTA of 256 threads per (record, 64-token group,
 // CW-channel chunk).  Thread (row slot, lane-in-row) loads 16 bytes (8
 // channels) of each of its rows with coalesced 16-byte loads and keeps them
 // (packed bf16) in registers.  K groups (64 tokens of one channel) reduce
-// over the thread's rows and the row slots (shared memory); V groups (64
+// over the thread's rows and the row slots (shared memory, laid out so both
+// the partial writes and the final reads are conflict-free); V groups (64
 // dims of one token/head) reduce over the 8 lanes that hold the group.
 // Quantised bytes go out as 8-byte (int8) or 4-byte (int4) coalesced stores,
 // element e = token * hd + channel.
-template <int CW>
+template <int CW, int BITS>
 __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant__ EncodeLaunch L)
 {
     constexpr int kTpr = CW / 8;                 // threads per row
     constexpr int kRowsPerPass = 256 / kTpr;
     constexpr int kPasses = 64 / kRowsPerPass;
-    __shared__ float red_lo[kRowsPerPass][CW], red_hi[kRowsPerPass][CW];
-    __shared__ float fin_lo[CW], fin_sc[CW];
+    constexpr uint32_t kLevels = (1u << BITS) - 1u;
+    __shared__ float red_lo[kRowsPerPass][8][kTpr], red_hi[kRowsPerPass][8][kTpr];
+    __shared__ float fin_lo[8][kTpr], fin_sc[8][kTpr];
 
     const CodecParams cp = L.codec;
     const uint32_t hd = cp.heads * 128u;
@@ -992,7 +1027,7 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
     uint8_t* pkt = L.packets + static_cast<size_t>(rec) * L.width;
     float* scale = reinterpret_cast<float*>(pkt + cp.qb);
     float* lowp = reinterpret_cast<float*>(pkt + cp.qb + cp.sb);
-    const float levels = static_cast<float>((1u << cp.bits) - 1u);
+    const float levels = static_cast<float>(kLevels);
 
     uint4 raw[kPasses];
 #pragma unroll
@@ -1005,7 +1040,7 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
         return bf16_bits_to_f32((c & 1) ? (w >> 16) : (w & 0xffffu));
     };
 
-    float lo[8], sc[8], inv[8];   // K: low, scale, 1/scale of the thread's 8 channels
+    float lo[8], sc[8], inv[8];   // K: low, scale and 1/scale of the thread's 8 channels
     if (kind == 0) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -1015,35 +1050,38 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
                 l = fminf(l, val(p, c));
                 h = fmaxf(h, val(p, c));
             }
-            red_lo[slot][8 * tl + c] = l;
-            red_hi[slot][8 * tl + c] = h;
+            red_lo[slot][c][tl] = l;
+            red_hi[slot][c][tl] = h;
         }
         __syncthreads();
         if (tid < CW) {
-            float l = red_lo[0][tid], h = red_hi[0][tid];
+            // channel chunk * CW + 8 * ttl + cc
+            const uint32_t ttl = tid % kTpr, cc = tid / kTpr;
+            float l = red_lo[0][cc][ttl], h = red_hi[0][cc][ttl];
 #pragma unroll
             for (int r = 1; r < kRowsPerPass; ++r) {
-                l = fminf(l, red_lo[r][tid]);
-                h = fmaxf(h, red_hi[r][tid]);
+                l = fminf(l, red_lo[r][cc][ttl]);
+                h = fmaxf(h, red_hi[r][cc][ttl]);
             }
             const float s1 = fmaxf(__fdiv_rn(__fsub_rn(h, l), levels), 1e-12f);
-            fin_lo[tid] = l;
-            fin_sc[tid] = s1;
-            const uint32_t sidx = tg * hd + chunk * CW + tid;
+            fin_lo[cc][ttl] = l;
+            fin_sc[cc][ttl] = s1;
+            const uint32_t sidx = tg * hd + chunk * CW + 8u * ttl + cc;
             scale[sidx] = s1;
             lowp[sidx] = l;
         }
         __syncthreads();
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            lo[c] = fin_lo[8 * tl + c];
-            sc[c] = fin_sc[8 * tl + c];
+            lo[c] = fin_lo[c][tl];
+            sc[c] = fin_sc[c][tl];
             inv[c] = __frcp_rn(sc[c]);
         }
     }
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
         const uint32_t t = tg * 64u + p * kRowsPerPass + slot;
+        float v_lo = 0.0f, v_sc = 0.0f;
         if (kind != 0) {
             // 64-dim group = 8 lanes (aligned, consecutive in the row).
             float l = val(p, 0), h = l;
@@ -1054,31 +1092,35 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
                 l = fminf(l, __shfl_xor_sync(0xffffffffu, l, m));
                 h = fmaxf(h, __shfl_xor_sync(0xffffffffu, h, m));
             }
-            const float s1 = fmaxf(__fdiv_rn(__fsub_rn(h, l), levels), 1e-12f);
+            v_lo = l;
+            v_sc = fmaxf(__fdiv_rn(__fsub_rn(h, l), levels), 1e-12f);
             if ((tl & 7u) == 0) {
                 const uint32_t sidx = (t * hd + c0) / 64u;
-                scale[sidx] = s1;
+                scale[sidx] = v_sc;
                 lowp[sidx] = l;
             }
-            const float r1 = __frcp_rn(s1);
+            const float r1 = __frcp_rn(v_sc);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) { lo[c] = l; sc[c] = s1; inv[c] = r1; }
+            for (int c = 0; c < 8; ++c) { lo[c] = l; inv[c] = r1; }
         }
         const size_t e0 = static_cast<size_t>(t) * hd + c0;
-        if (cp.bits == 8) {
-            uint32_t wv[2] = {0u, 0u};
+        bool near = false;
+        uint2 word = make_uint2(0u, 0u);
 #pragma unroll
-            for (int c = 0; c < 8; ++c)
-                wv[c >> 2] |= static_cast<uint32_t>(quantise_fast(val(p, c), lo[c], sc[c], inv[c], levels))
-                              << (8 * (c & 3));
-            *reinterpret_cast<uint2*>(pkt + e0) = make_uint2(wv[0], wv[1]);
-        } else {
-            uint32_t word = 0;
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-                word |= static_cast<uint32_t>(quantise_fast(val(p, c), lo[c], sc[c], inv[c], levels)) << (4 * c);
-            *reinterpret_cast<uint32_t*>(pkt + e0 / 2) = word;
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t q = quantise_fast(val(p, c), lo[c], inv[c], kLevels, near);
+            if (BITS == 8) {
+                if (c < 4) word.x |= q << (8 * c); else word.y |= q << (8 * (c - 4));
+            } else {
+                word.x |= q << (4 * c);
+            }
         }
+        if (near) word = kind == 0 ? quantise_row_exact<BITS>(raw[p], lo, sc, 0.0f, 0.0f)
+                                   : quantise_row_exact<BITS>(raw[p], nullptr, nullptr, v_lo, v_sc);
+        if (BITS == 8)
+            *reinterpret_cast<uint2*>(pkt + e0) = word;
+        else
+            *reinterpret_cast<uint32_t*>(pkt + e0 / 2) = word.x;
     }
     if (blockIdx.x == 0) {
         // int32 header {1, layer, kind, bits} then zero padding to width.
@@ -1436,11 +1478,15 @@ int launch_encode(const EncodeLaunch& args, cudaStream_t stream)
 {
     if (args.n == 0) return cudaSuccess;
     const uint32_t hd = args.codec.heads * 128u;
+    const bool wide = hd % 256u == 0;
+    const dim3 grid(2u * (hd / (wide ? 256u : 128u)), args.n);
     ProfileScope prof(kKernEncode, stream);
-    if (hd % 256u == 0) {
-        kv_encode_kernel<256><<<dim3(2u * (hd / 256u), args.n), 256, 0, stream>>>(args);
+    if (args.codec.bits == 8) {
+        if (wide) kv_encode_kernel<256, 8><<<grid, 256, 0, stream>>>(args);
+        else kv_encode_kernel<128, 8><<<grid, 256, 0, stream>>>(args);
     } else {
-        kv_encode_kernel<128><<<dim3(2u * (hd / 128u), args.n), 256, 0, stream>>>(args);
+        if (wide) kv_encode_kernel<256, 4><<<grid, 256, 0, stream>>>(args);
+        else kv_encode_kernel<128, 4><<<grid, 256, 0, stream>>>(args);
     }
     return cudaGetLastError();
 }
