@@ -178,6 +178,26 @@ def kernel_profile(lib, torch, enqueue_step, layers):
     return out
 
 
+def link_gbs(torch, stream, direction="h2d", nbytes=256 << 20, reps=5):
+    """Measured pinned-host <-> device copy bandwidth (GB/s), best of `reps`
+    one-shot copies of `nbytes` on `stream` (CUDA events)."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    best = 0.0
+    for _ in range(reps + 1):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        if direction == "h2d":
+            dev.copy_(host, non_blocking=True)
+        else:
+            host.copy_(dev, non_blocking=True)
+        e1.record(stream)
+        e1.synchronize()
+        best = max(best, nbytes / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+    del host, dev
+    return best
+
+
 def build_workload(cfg, rank, torch, nl):
     """Host pool (pinned, registered), device paged cache, block table, records."""
     L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
@@ -346,6 +366,7 @@ def run_gpu(args, cfg):
     e2e_value = world * algo / (e2e_ms * 1e-3) / 1e9
     h2d_bytes = sum(strides[layer] * n for layer in range(L))
     d2h_bytes = L * n * 4
+    link = link_gbs(torch, stream, "h2d")
 
     result = None
     if rank == 0:
@@ -394,6 +415,8 @@ def run_gpu(args, cfg):
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "per_layer_reload_us": round(e2e_ms * 1e3 / L, 2),
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+                    "link_h2d_gbs": round(link, 2),
+                    "link_frac": round(h2d_bytes / (e2e_ms * 1e-3) / 1e9 / link, 4),
                     "path": "secure_infer_h2d_reload_layer from pinned host plaintext (OpenSSL encrypt on host "
                             "threads + staged H2D + keystream + fused kernel) + status read per layer"},
             "gpu_launches": launches,
@@ -526,6 +549,8 @@ def run_gpu_writeback(args, cfg):
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), dist) / args.steps
     e2e_value = world * algo / (e2e_ms * 1e-3) / 1e9
+    link = link_gbs(torch, stream, "d2h")
+    d2h_step = sum(strides[layer] * n for layer in range(L))
 
     # Round trip: the host pool of layer 0 reloads through the authenticated
     # path and dequantises to within half a quantisation step of the source.
@@ -576,7 +601,9 @@ def run_gpu_writeback(args, cfg):
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "per_layer_us": round(e2e_ms * 1e3 / L, 2),
                     "h2d_bytes_per_step": L * n * (64 + 8),
-                    "d2h_bytes_per_step": sum(strides[layer] * n for layer in range(L)),
+                    "d2h_bytes_per_step": d2h_step,
+                    "link_d2h_gbs": round(link, 2),
+                    "link_frac": round(d2h_step / (e2e_ms * 1e-3) / 1e9 / link, 4),
                     "path": "secure_infer_d2h_writeback_layer (device quantise + encrypt + tag, D2H to a pinned "
                             "ring, OpenSSL verify + decrypt on host threads into the pinned host pool) + "
                             "secure_infer_d2h_wait per step"},

@@ -315,6 +315,7 @@ struct StageSlot {
     uint32_t* dev_status = nullptr;
     uint32_t* host_status = nullptr;
     cudaEvent_t done = nullptr;
+    cudaEvent_t ks_ready = nullptr, copied = nullptr;   // staged reload: keystream / records landed
     std::shared_ptr<LayerBatch> owner;
 };
 
@@ -362,6 +363,7 @@ struct Session {
     uint8_t salt[4] = {};
     GcmSchedule* sched = nullptr;
     cudaStream_t producer = nullptr;
+    cudaStream_t copier = nullptr;    // staged H2D record copies
     // Cross-stream fences of reload_records when the keystream is produced on
     // another stream than the one that consumes it.
     cudaEvent_t consumed_ev = nullptr, produced_ev = nullptr;
@@ -734,6 +736,17 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
         tickets.assign(given_tickets, given_tickets + n);
     } else {
         for (uint32_t i = 0; i < n; ++i) tickets[i] = reserve_ticket();
+    }
+    // The keystream depends only on the tickets: it is generated on the
+    // producer stream while the host encrypts and the records cross the link
+    // (the slot's previous batch has completed, see above).
+    if ((!slot.ks_ready && !CUDA_OK(cudaEventCreateWithFlags(&slot.ks_ready, cudaEventDisableTiming))) ||
+        (!slot.copied && !CUDA_OK(cudaEventCreateWithFlags(&slot.copied, cudaEventDisableTiming))))
+        return nullptr;
+    if (keystream_records_locked(tickets.data(), n, count, slot.ks, g_s.producer) != 0 ||
+        !CUDA_OK(cudaEventRecord(slot.ks_ready, g_s.producer)))
+        return nullptr;
+    if (!encrypted) {
         std::atomic<bool> ok{true};
         const uint8_t* key = g_s.key;
         pool().parallel_for(n, [&](size_t i) {
@@ -760,13 +773,17 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     for (uint32_t i = 0; i < n; ++i) batch->items[i] = RetryInfo{encrypted ? nullptr : srcs[i], dsts[i]};
     if (!CUDA_OK(cudaEventCreateWithFlags(&batch->done, cudaEventDisableTiming))) return nullptr;
 
-    // The keystream area of this slot may still be read by its previous
-    // kernel: the producer waits for the slot's last completion.
-    if (slot.done) cudaStreamWaitEvent(g_s.producer, slot.done, 0);
+    // Records cross the link on the copy stream, so the next layer's copy
+    // does not queue behind this layer's kernel; the caller's stream waits
+    // for the records and the keystream, then runs the fused kernel.
     const void* host_src = encrypted ? srcs[0] : slot.host;
-    if (!CUDA_OK(cudaMemcpyAsync(slot.dev, host_src, stride * n, cudaMemcpyHostToDevice, stream))) return nullptr;
-    if (reload_records_locked(layer, slot.dev, stride, count, n, tickets.data(), dsts, slot.ks, slot.dev_status,
-                              codec, stream, g_s.producer) != 0)
+    if (!CUDA_OK(cudaMemcpyAsync(slot.dev, host_src, stride * n, cudaMemcpyHostToDevice, g_s.copier)) ||
+        !CUDA_OK(cudaEventRecord(slot.copied, g_s.copier)) ||
+        !CUDA_OK(cudaStreamWaitEvent(stream, slot.copied, 0)) ||
+        !CUDA_OK(cudaStreamWaitEvent(stream, slot.ks_ready, 0)))
+        return nullptr;
+    if (verify_records_locked(slot.dev, stride, count, n, tickets.data(), dsts, slot.ks, slot.dev_status, codec,
+                              stream) != 0)
         return nullptr;
     cudaMemcpyAsync(slot.host_status, slot.dev_status, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, stream);
     cudaEventRecord(batch->done, stream);
@@ -1047,7 +1064,13 @@ void shutdown_locked()
     g_s.pending.clear();
     g_s.last_event.clear();
     g_s.last_batch.clear();
-    for (auto& s : g_s.h2d) { s.owner.reset(); free_stage(s); }
+    for (auto& s : g_s.h2d) {
+        s.owner.reset();
+        free_stage(s);
+        if (s.ks_ready) cudaEventDestroy(s.ks_ready);
+        if (s.copied) cudaEventDestroy(s.copied);
+        s.ks_ready = s.copied = nullptr;
+    }
     for (auto& s : g_s.d2h) free_stage(s);
     for (auto& s : g_s.wb) {
         free_stage(s);
@@ -1067,6 +1090,8 @@ void shutdown_locked()
     g_s.sched = nullptr;
     if (g_s.producer) cudaStreamDestroy(g_s.producer);
     g_s.producer = nullptr;
+    if (g_s.copier) cudaStreamDestroy(g_s.copier);
+    g_s.copier = nullptr;
     if (g_s.consumed_ev) cudaEventDestroy(g_s.consumed_ev);
     if (g_s.produced_ev) cudaEventDestroy(g_s.produced_ev);
     g_s.consumed_ev = g_s.produced_ev = nullptr;
@@ -1109,6 +1134,7 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
         !CUDA_OK(cudaMemset(g_s.sched, 0, sib::schedule_bytes())) || !CUDA_OK(cudaMalloc(&dkey, 16)) ||
         !CUDA_OK(cudaMemcpy(dkey, key16, 16, cudaMemcpyHostToDevice)) ||
         !CUDA_OK(cudaStreamCreateWithFlags(&g_s.producer, cudaStreamNonBlocking)) ||
+        !CUDA_OK(cudaStreamCreateWithFlags(&g_s.copier, cudaStreamNonBlocking)) ||
         !CUDA_OK(cudaEventCreateWithFlags(&g_s.consumed_ev, cudaEventDisableTiming)) ||
         !CUDA_OK(cudaEventCreateWithFlags(&g_s.produced_ev, cudaEventDisableTiming))) {
         cudaFree(dkey);
