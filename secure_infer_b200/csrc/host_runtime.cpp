@@ -30,6 +30,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
@@ -39,6 +40,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <shared_mutex>
 #include <thread>
 #include <unordered_set>
 #include <vector>
@@ -83,7 +85,9 @@ struct HostRange {
     size_t block_bytes;
 };
 
-std::mutex g_ranges_mu;
+// Lookups (one per record, from every crypto worker) share the lock;
+// registrations take it exclusively.
+std::shared_mutex g_ranges_mu;
 std::vector<HostRange> g_ranges;
 
 bool lookup_range(const void* p, size_t bytes, HostRange* out, uint64_t* block, uint64_t* offset)
@@ -91,7 +95,7 @@ bool lookup_range(const void* p, size_t bytes, HostRange* out, uint64_t* block, 
     const uintptr_t b = reinterpret_cast<uintptr_t>(p);
     if (bytes > UINTPTR_MAX - b) return false;
     const uintptr_t e = b + bytes;
-    std::lock_guard<std::mutex> lock(g_ranges_mu);
+    std::shared_lock<std::shared_mutex> lock(g_ranges_mu);
     // Newest registration first: a host allocation that reuses the address of
     // a freed, previously registered tensor must get its own metadata.
     for (auto it = g_ranges.rbegin(); it != g_ranges.rend(); ++it) {
@@ -233,27 +237,60 @@ Pool& pool()
 }
 
 // ---------------------------------------------------------------- OpenSSL
-struct CtxHolder {
+// Per-thread AES-128-GCM contexts keyed once per session key: a record then
+// only sets its IV (EVP_*Init_ex with key = null keeps the expanded key and
+// GHASH table), instead of re-expanding the key for every 10-256 KiB record.
+// A session (re)init bumps g_key_generation, which re-keys every context on
+// its next use.
+std::atomic<uint64_t> g_key_generation{1};
+
+struct KeyedCtx {
     EVP_CIPHER_CTX* ctx = EVP_CIPHER_CTX_new();
-    ~CtxHolder() { EVP_CIPHER_CTX_free(ctx); }
+    uint64_t generation = 0;
+    ~KeyedCtx() { EVP_CIPHER_CTX_free(ctx); }
 };
 
-EVP_CIPHER_CTX* thread_ctx()
+EVP_CIPHER_CTX* keyed_ctx(KeyedCtx& k, const uint8_t key[16], bool encrypt)
 {
-    thread_local CtxHolder holder;
-    return holder.ctx;
+    const uint64_t gen = g_key_generation.load(std::memory_order_acquire);
+    if (k.ctx == nullptr) return nullptr;
+    if (k.generation != gen) {
+        EVP_CIPHER_CTX_reset(k.ctx);
+        const bool ok =
+            (encrypt ? EVP_EncryptInit_ex(k.ctx, EVP_aes_128_gcm(), nullptr, nullptr, nullptr)
+                     : EVP_DecryptInit_ex(k.ctx, EVP_aes_128_gcm(), nullptr, nullptr, nullptr)) == 1 &&
+            EVP_CIPHER_CTX_ctrl(k.ctx, EVP_CTRL_GCM_SET_IVLEN, 12, nullptr) == 1 &&
+            (encrypt ? EVP_EncryptInit_ex(k.ctx, nullptr, nullptr, key, nullptr)
+                     : EVP_DecryptInit_ex(k.ctx, nullptr, nullptr, key, nullptr)) == 1;
+        if (!ok) {
+            k.generation = 0;
+            return nullptr;
+        }
+        k.generation = gen;
+    }
+    return k.ctx;
+}
+
+EVP_CIPHER_CTX* thread_enc_ctx(const uint8_t key[16])
+{
+    thread_local KeyedCtx k;
+    return keyed_ctx(k, key, true);
+}
+
+EVP_CIPHER_CTX* thread_dec_ctx(const uint8_t key[16])
+{
+    thread_local KeyedCtx k;
+    return keyed_ctx(k, key, false);
 }
 
 // Record = C (zero padded to 32) || tag || zero16 || AAD (secure_infer.cpp:6508-6537).
 bool encrypt_record(const uint8_t key[16], const uint8_t iv[16], const uint8_t aad[64], const uint8_t* src,
                     uint64_t count, uint8_t* rec)
 {
-    EVP_CIPHER_CTX* ctx = thread_ctx();
+    EVP_CIPHER_CTX* ctx = thread_enc_ctx(key);
     const uint64_t aligned = aligned32(count);
     int n = 0, fin = 0;
-    bool ok = EVP_EncryptInit_ex(ctx, EVP_aes_128_gcm(), nullptr, nullptr, nullptr) == 1 &&
-              EVP_CIPHER_CTX_ctrl(ctx, EVP_CTRL_GCM_SET_IVLEN, 12, nullptr) == 1 &&
-              EVP_EncryptInit_ex(ctx, nullptr, nullptr, key, iv) == 1 &&
+    bool ok = ctx != nullptr && EVP_EncryptInit_ex(ctx, nullptr, nullptr, nullptr, iv) == 1 &&
               EVP_EncryptUpdate(ctx, nullptr, &n, aad, static_cast<int>(kAadBytes)) == 1 &&
               EVP_EncryptUpdate(ctx, rec, &n, src, static_cast<int>(count)) == 1 &&
               EVP_EncryptFinal_ex(ctx, rec + n, &fin) == 1 &&
@@ -268,13 +305,11 @@ bool encrypt_record(const uint8_t key[16], const uint8_t iv[16], const uint8_t a
 bool decrypt_record(const uint8_t key[16], const uint8_t iv[16], const uint8_t aad[64], const uint8_t* c,
                     uint64_t count, const uint8_t tag[16], uint8_t* out)
 {
-    EVP_CIPHER_CTX* ctx = thread_ctx();
+    EVP_CIPHER_CTX* ctx = thread_dec_ctx(key);
     int n = 0, fin = 0;
     uint8_t tag_copy[16];
     std::memcpy(tag_copy, tag, 16);
-    const bool ok = EVP_DecryptInit_ex(ctx, EVP_aes_128_gcm(), nullptr, nullptr, nullptr) == 1 &&
-                    EVP_CIPHER_CTX_ctrl(ctx, EVP_CTRL_GCM_SET_IVLEN, 12, nullptr) == 1 &&
-                    EVP_DecryptInit_ex(ctx, nullptr, nullptr, key, iv) == 1 &&
+    const bool ok = ctx != nullptr && EVP_DecryptInit_ex(ctx, nullptr, nullptr, nullptr, iv) == 1 &&
                     EVP_DecryptUpdate(ctx, nullptr, &n, aad, static_cast<int>(kAadBytes)) == 1 &&
                     EVP_DecryptUpdate(ctx, out, &n, c, static_cast<int>(count)) == 1 &&
                     EVP_CIPHER_CTX_ctrl(ctx, EVP_CTRL_GCM_SET_TAG, 16, tag_copy) == 1 &&
@@ -489,6 +524,17 @@ void harvest(LayerBatch& b)
     cudaEventSynchronize(b.done);
     b.status.assign(b.slot->host_status, b.slot->host_status + b.n);
     b.harvested = true;
+}
+
+// n consecutive fresh tickets under one lock.
+void reserve_tickets(uint32_t n, uint64_t* out)
+{
+    const uint64_t first = g_s.next_ticket.fetch_add(n, std::memory_order_relaxed);
+    std::lock_guard<std::mutex> lock(g_s.replay_mu);
+    for (uint32_t i = 0; i < n; ++i) {
+        out[i] = first + i;
+        g_s.replay.insert(first + i);
+    }
 }
 
 uint64_t reserve_ticket()
@@ -735,7 +781,7 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
             if (!reserve_given_ticket(given_tickets[i])) return nullptr;
         tickets.assign(given_tickets, given_tickets + n);
     } else {
-        for (uint32_t i = 0; i < n; ++i) tickets[i] = reserve_ticket();
+        reserve_tickets(n, tickets.data());
     }
     // The keystream depends only on the tickets: it is generated on the
     // producer stream while the host encrypts and the records cross the link
@@ -888,8 +934,8 @@ int writeback_device_locked(const void* const* srcs, void* const* host_dsts, uin
     const uint64_t ks_stride = layer_ks_stride(count);
     std::vector<uint64_t> tk(n);
     bool unaligned = misaligned(records) || (stride & 15u);
+    reserve_tickets(n, tk.data());
     for (uint32_t i = 0; i < n; ++i) {
-        tk[i] = reserve_ticket();
         if (tickets) tickets[i] = tk[i];
         if (ivs) iv_for(tk[i], ivs + 16ull * i);
         build_aad(host_dsts ? host_dsts[i] : nullptr, count, SECURE_INFER_DIRECTION_D2H, tk[i], 0, 0,
@@ -1116,6 +1162,7 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
     g_s.device = device;
     std::memcpy(g_s.key, key16, 16);
     std::memcpy(g_s.salt, iv_salt4, 4);
+    g_key_generation.fetch_add(1, std::memory_order_acq_rel);   // re-key the host OpenSSL contexts
     g_s.next_ticket = 1;
     {
         std::lock_guard<std::mutex> rl(g_s.replay_mu);
@@ -1172,15 +1219,13 @@ SI_EXPORT void secure_infer_register_host_range_ex(const void* base, size_t byte
     if (base == nullptr || bytes == 0) return;
     const uintptr_t b = reinterpret_cast<uintptr_t>(base);
     if (bytes > UINTPTR_MAX - b) return;
-    std::lock_guard<std::mutex> lock(g_ranges_mu);
-    for (auto& r : g_ranges) {
-        if (r.begin == b && r.end == b + bytes) {
-            r.layer = layer_id;
-            r.kind = tensor_kind;
-            r.block_bytes = block_bytes;
-            return;
-        }
-    }
+    std::unique_lock<std::shared_mutex> lock(g_ranges_mu);
+    // The new registration is the newest; older ones it covers completely can
+    // never match again and are dropped, so re-registering a recycled buffer
+    // does not grow the list.
+    g_ranges.erase(std::remove_if(g_ranges.begin(), g_ranges.end(),
+                                  [&](const HostRange& r) { return r.begin >= b && r.end <= b + bytes; }),
+                   g_ranges.end());
     g_ranges.push_back({b, b + bytes, layer_id, tensor_kind, block_bytes});
 }
 
