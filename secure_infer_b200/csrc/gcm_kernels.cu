@@ -947,53 +947,44 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as
 // conversion instruction is needed (y >= 0 because low is the group minimum).
 constexpr float kRoundMagic = 12582912.0f;   // 1.5 * 2^23
 
-__device__ __forceinline__ uint32_t quantise_fast(float x, float low, float inv_scale, uint32_t levels, bool& near)
+// Quantises the 8 elements of one row slice into m[c] = fl(y + magic), whose
+// low byte is q = round(y) (q <= 255, and y <= levels (1 + 2^-23), so no
+// clamp is needed).  |y - round(y)| is exact; elements within 2^-13 of a
+// half-integer are flagged in the returned mask for the exact division.
+template <class Val, class Low, class Inv>
+__device__ __forceinline__ uint32_t quantise8_fast(Val val, Low low, Inv inv, uint32_t (&m)[8])
 {
-    const float y = __fmul_rn(__fsub_rn(x, low), inv_scale);
-    const float m = __fadd_rn(y, kRoundMagic);
-    near |= fabsf(fabsf(__fsub_rn(y, __fsub_rn(m, kRoundMagic))) - 0.5f) < 0x1p-13f;
-    const uint32_t q = __float_as_uint(m) & 0x3fffffu;
-    return q < levels ? q : levels;
-}
-
-// The 8 elements of one row slice with the reference's division.  k_lo/k_sc:
-// per-channel parameters (K, shared memory) or null for one (v_lo, v_sc) (V).
-template <int BITS>
-__device__ __noinline__ uint2 quantise_row_exact(uint4 raw, const float* k_lo, const float* k_sc, float v_lo,
-                                                 float v_sc);
-
-template <int BITS>
-__device__ __forceinline__ uint2 quantise_row_exact(uint4 raw, const float (&k_lo)[8], const float (&k_sc)[8], float,
-                                                    float)
-{
-    // Per-channel parameters held in registers: go through the out-of-line
-    // version with a local copy (rare path).
-    float lo[8], sc[8];
+    uint32_t near = 0;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) { lo[c] = k_lo[c]; sc[c] = k_sc[c]; }
-    return quantise_row_exact<BITS>(raw, static_cast<const float*>(lo), static_cast<const float*>(sc), 0.0f, 0.0f);
+    for (int c = 0; c < 8; ++c) {
+        const float y = __fmul_rn(__fsub_rn(val(c), low(c)), inv(c));
+        const float mf = __fadd_rn(y, kRoundMagic);
+        if (fabsf(__fsub_rn(y, __fsub_rn(mf, kRoundMagic))) > 0.5f - 0x1p-13f) near |= 1u << c;
+        m[c] = __float_as_uint(mf);
+    }
+    return near;
 }
 
-template <int BITS>
-__device__ __noinline__ uint2 quantise_row_exact(uint4 raw, const float* k_lo, const float* k_sc, float v_lo,
-                                                 float v_sc)
+// The reference's division for one element (rare path).
+__device__ __noinline__ uint32_t quantise_exact(float x, float low, float scale)
 {
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    const uint32_t levels = (1u << BITS) - 1u;
-    uint2 out = make_uint2(0u, 0u);
-    for (int c = 0; c < 8; ++c) {
-        const float x = bf16_bits_to_f32((c & 1) ? (w[c >> 1] >> 16) : (w[c >> 1] & 0xffffu));
-        const float l = k_lo ? k_lo[c] : v_lo, sc = k_lo ? k_sc[c] : v_sc;
-        const float m = __fadd_rn(__fdiv_rn(__fsub_rn(x, l), sc), kRoundMagic);
-        uint32_t q = __float_as_uint(m) & 0x3fffffu;
-        q = q < levels ? q : levels;
-        if (BITS == 8) {
-            if (c < 4) out.x |= q << (8 * c); else out.y |= q << (8 * (c - 4));
-        } else {
-            out.x |= q << (4 * c);
-        }
+    return __float_as_uint(__fadd_rn(__fdiv_rn(__fsub_rn(x, low), scale), kRoundMagic));
+}
+
+// Packs m[0..7] (q in the low byte) as 8 int8 bytes or 8 int4 nibbles (even
+// element in the low nibble).
+template <int BITS>
+__device__ __forceinline__ uint2 pack8(const uint32_t (&m)[8])
+{
+    if (BITS == 8) {
+        const uint32_t w0 = __byte_perm(__byte_perm(m[0], m[1], 0x0040u), __byte_perm(m[2], m[3], 0x0040u), 0x5410u);
+        const uint32_t w1 = __byte_perm(__byte_perm(m[4], m[5], 0x0040u), __byte_perm(m[6], m[7], 0x0040u), 0x5410u);
+        return make_uint2(w0, w1);
     }
-    return out;
+    // Low byte of m[c] + (m[c+1] << 4) is q[c] + 16 q[c+1] (both <= 15).
+    const uint32_t t0 = m[0] + (m[1] << 4), t1 = m[2] + (m[3] << 4);
+    const uint32_t t2 = m[4] + (m[5] << 4), t3 = m[6] + (m[7] << 4);
+    return make_uint2(__byte_perm(__byte_perm(t0, t1, 0x0040u), __byte_perm(t2, t3, 0x0040u), 0x5410u), 0u);
 }
 
 // Tiled quantisation: one CTA of 256 threads per (record, 64-token group,
@@ -1013,7 +1004,7 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
     constexpr int kPasses = 64 / kRowsPerPass;
     constexpr uint32_t kLevels = (1u << BITS) - 1u;
     __shared__ float red_lo[kRowsPerPass][8][kTpr], red_hi[kRowsPerPass][8][kTpr];
-    __shared__ float fin_lo[8][kTpr], fin_sc[8][kTpr];
+    __shared__ float fin_lo[8][kTpr], fin_sc[8][kTpr], fin_inv[8][kTpr];
 
     const CodecParams cp = L.codec;
     const uint32_t hd = cp.heads * 128u;
@@ -1040,18 +1031,29 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
         return bf16_bits_to_f32((c & 1) ? (w >> 16) : (w & 0xffffu));
     };
 
-    float lo[8], sc[8], inv[8];   // K: low, scale and 1/scale of the thread's 8 channels
+    float lo[8], sc[8], inv[8];   // K: per channel of the thread; V: per pass (group of the row)
     if (kind == 0) {
+        // Per-channel min/max over the thread's rows on packed bf16 pairs
+        // (exact: min and max select one of the inputs).
+        __nv_bfloat162 l2[4], h2[4];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            float l = val(0, c), h = l;
+        for (int w = 0; w < 4; ++w) {
+            const uint32_t first = w == 0 ? raw[0].x : w == 1 ? raw[0].y : w == 2 ? raw[0].z : raw[0].w;
+            l2[w] = h2[w] = *reinterpret_cast<const __nv_bfloat162*>(&first);
 #pragma unroll
             for (int p = 1; p < kPasses; ++p) {
-                l = fminf(l, val(p, c));
-                h = fmaxf(h, val(p, c));
+                const uint32_t v = w == 0 ? raw[p].x : w == 1 ? raw[p].y : w == 2 ? raw[p].z : raw[p].w;
+                const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&v);
+                l2[w] = __hmin2(l2[w], b);
+                h2[w] = __hmax2(h2[w], b);
             }
-            red_lo[slot][c][tl] = l;
-            red_hi[slot][c][tl] = h;
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            red_lo[slot][2 * w][tl] = __low2float(l2[w]);
+            red_lo[slot][2 * w + 1][tl] = __high2float(l2[w]);
+            red_hi[slot][2 * w][tl] = __low2float(h2[w]);
+            red_hi[slot][2 * w + 1][tl] = __high2float(h2[w]);
         }
         __syncthreads();
         if (tid < CW) {
@@ -1066,6 +1068,7 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
             const float s1 = fmaxf(__fdiv_rn(__fsub_rn(h, l), levels), 1e-12f);
             fin_lo[cc][ttl] = l;
             fin_sc[cc][ttl] = s1;
+            fin_inv[cc][ttl] = __frcp_rn(s1);
             const uint32_t sidx = tg * hd + chunk * CW + 8u * ttl + cc;
             scale[sidx] = s1;
             lowp[sidx] = l;
@@ -1075,52 +1078,79 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
         for (int c = 0; c < 8; ++c) {
             lo[c] = fin_lo[c][tl];
             sc[c] = fin_sc[c][tl];
-            inv[c] = __frcp_rn(sc[c]);
+            inv[c] = fin_inv[c][tl];
         }
-    }
+    } else {
+        // V: the 8 lanes of a 64-dim group reduce each pass's group; lane j of
+        // the group then divides for pass j, and the passes fetch their scale
+        // and reciprocal from that lane.
+        float vl[kPasses], vh[kPasses];
 #pragma unroll
-    for (int p = 0; p < kPasses; ++p) {
-        const uint32_t t = tg * 64u + p * kRowsPerPass + slot;
-        float v_lo = 0.0f, v_sc = 0.0f;
-        if (kind != 0) {
-            // 64-dim group = 8 lanes (aligned, consecutive in the row).
-            float l = val(p, 0), h = l;
-#pragma unroll
-            for (int c = 1; c < 8; ++c) { l = fminf(l, val(p, c)); h = fmaxf(h, val(p, c)); }
+        for (int p = 0; p < kPasses; ++p) {
+            const __nv_bfloat162 w0 = *reinterpret_cast<const __nv_bfloat162*>(&raw[p].x);
+            const __nv_bfloat162 w1 = *reinterpret_cast<const __nv_bfloat162*>(&raw[p].y);
+            const __nv_bfloat162 w2 = *reinterpret_cast<const __nv_bfloat162*>(&raw[p].z);
+            const __nv_bfloat162 w3 = *reinterpret_cast<const __nv_bfloat162*>(&raw[p].w);
+            const __nv_bfloat162 l2 = __hmin2(__hmin2(w0, w1), __hmin2(w2, w3));
+            const __nv_bfloat162 h2 = __hmax2(__hmax2(w0, w1), __hmax2(w2, w3));
+            float l = fminf(__low2float(l2), __high2float(l2)), h = fmaxf(__low2float(h2), __high2float(h2));
 #pragma unroll
             for (int m = 1; m < 8; m <<= 1) {
                 l = fminf(l, __shfl_xor_sync(0xffffffffu, l, m));
                 h = fmaxf(h, __shfl_xor_sync(0xffffffffu, h, m));
             }
-            v_lo = l;
-            v_sc = fmaxf(__fdiv_rn(__fsub_rn(h, l), levels), 1e-12f);
-            if ((tl & 7u) == 0) {
-                const uint32_t sidx = (t * hd + c0) / 64u;
-                scale[sidx] = v_sc;
-                lowp[sidx] = l;
-            }
-            const float r1 = __frcp_rn(v_sc);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) { lo[c] = l; inv[c] = r1; }
+            vl[p] = l;
+            vh[p] = h;
         }
+        const uint32_t j = tl & 7u;
+        float lj = vl[0], hj = vh[0];
+#pragma unroll
+        for (int p = 1; p < kPasses; ++p)
+            if (j == static_cast<uint32_t>(p)) { lj = vl[p]; hj = vh[p]; }
+        const float sj = fmaxf(__fdiv_rn(__fsub_rn(hj, lj), levels), 1e-12f);
+        const float ij = __frcp_rn(sj);
+        if (j < static_cast<uint32_t>(kPasses)) {
+            const uint32_t t = tg * 64u + j * kRowsPerPass + slot;
+            const uint32_t sidx = (t * hd + c0 - 8u * j) / 64u;   // group start channel = c0 - 8 j
+            scale[sidx] = sj;
+            lowp[sidx] = lj;
+        }
+        const uint32_t base_lane = (tid & 31u) & ~7u;
+#pragma unroll
+        for (int p = 0; p < kPasses; ++p) {
+            const float sp = __shfl_sync(0xffffffffu, sj, base_lane | p);
+            const float ip = __shfl_sync(0xffffffffu, ij, base_lane | p);
+            // stash per pass in the K arrays' slots (8 >= kPasses)
+            lo[p] = vl[p];
+            sc[p] = sp;
+            inv[p] = ip;
+        }
+    }
+    // One row slice: quantise, redo flagged elements exactly, pack, store.
+    auto row = [&](int p, auto low, auto scl, auto inv_of) {
+        const uint32_t t = tg * 64u + p * kRowsPerPass + slot;
+        uint32_t m[8];
+        const uint32_t near = quantise8_fast([&](int c) { return val(p, c); }, low, inv_of, m);
+        if (near) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                if (near & (1u << c)) m[c] = quantise_exact(val(p, c), low(c), scl(c));
+        }
+        const uint2 word = pack8<BITS>(m);
         const size_t e0 = static_cast<size_t>(t) * hd + c0;
-        bool near = false;
-        uint2 word = make_uint2(0u, 0u);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            const uint32_t q = quantise_fast(val(p, c), lo[c], inv[c], kLevels, near);
-            if (BITS == 8) {
-                if (c < 4) word.x |= q << (8 * c); else word.y |= q << (8 * (c - 4));
-            } else {
-                word.x |= q << (4 * c);
-            }
-        }
-        if (near) word = kind == 0 ? quantise_row_exact<BITS>(raw[p], lo, sc, 0.0f, 0.0f)
-                                   : quantise_row_exact<BITS>(raw[p], nullptr, nullptr, v_lo, v_sc);
         if (BITS == 8)
             *reinterpret_cast<uint2*>(pkt + e0) = word;
         else
             *reinterpret_cast<uint32_t*>(pkt + e0 / 2) = word.x;
+    };
+    if (kind == 0) {
+#pragma unroll
+        for (int p = 0; p < kPasses; ++p)
+            row(p, [&](int c) { return lo[c]; }, [&](int c) { return sc[c]; }, [&](int c) { return inv[c]; });
+    } else {
+#pragma unroll
+        for (int p = 0; p < kPasses; ++p)
+            row(p, [&](int) { return lo[p]; }, [&](int) { return sc[p]; }, [&](int) { return inv[p]; });
     }
     if (blockIdx.x == 0) {
         // int32 header {1, layer, kind, bits} then zero padding to width.
