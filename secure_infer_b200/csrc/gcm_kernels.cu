@@ -244,6 +244,9 @@ __device__ __forceinline__ void fill_aes_smem(uint32_t* te, uint32_t* rk, const 
 // [0, 64 KiB), pair (Te2, Te3) fills [64 KiB, 128 KiB); every lane reads its
 // own bank, so a warp's 32 lookups are one conflict-free wavefront.
 constexpr uint32_t kCtrThreads = 1024;
+// The layer keystream kernel uses half the register file (512 threads x 64),
+// so a quantise CTA of the writeback path can share the SM with it.
+constexpr uint32_t kLayerCtrThreads = 512;
 constexpr size_t kCtrTableBytes = 131072;
 constexpr size_t kCtrSmem = kCtrTableBytes + 256;
 
@@ -627,7 +630,7 @@ __device__ __forceinline__ void layer_iv(uint32_t iv0, uint64_t ticket, uint32_t
 
 // Keystream of every record plus E_K(J0) in the record's last 16 bytes.
 template <int kCap>
-__global__ void __launch_bounds__(kCtrThreads, 1) gcm_layer_ctr_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+__global__ void __launch_bounds__(kLayerCtrThreads, 1) gcm_layer_ctr_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     fill_aes4_smem(smem, L.h.sched);
@@ -1440,14 +1443,14 @@ int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream
     if (h.n == 0) return cudaSuccess;
     if (h.n > static_cast<uint32_t>(kLayerCapLarge)) return cudaErrorInvalidValue;
     const uint32_t blocks = static_cast<uint32_t>(((h.count + 15) / 16 + 1) * h.n);
-    const uint32_t items = (blocks + kCtrThreads - 1) / kCtrThreads;
+    const uint32_t items = (blocks + kLayerCtrThreads - 1) / kLayerCtrThreads;
     static bool set_small[64], set_large[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
-        return layer_launch<kLayerCapSmall>(kKernLayerCtr, gcm_layer_ctr_kernel<kLayerCapSmall>, h, rec, kCtrThreads, kCtrSmem, items,
+        return layer_launch<kLayerCapSmall>(kKernLayerCtr, gcm_layer_ctr_kernel<kLayerCapSmall>, h, rec, kLayerCtrThreads, kCtrSmem, items,
                                             set_small[dev & 63], stream);
-    return layer_launch<kLayerCapLarge>(kKernLayerCtr, gcm_layer_ctr_kernel<kLayerCapLarge>, h, rec, kCtrThreads, kCtrSmem, items,
+    return layer_launch<kLayerCapLarge>(kKernLayerCtr, gcm_layer_ctr_kernel<kLayerCapLarge>, h, rec, kLayerCtrThreads, kCtrSmem, items,
                                         set_large[dev & 63], stream);
 }
 

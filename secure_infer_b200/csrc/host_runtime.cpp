@@ -946,6 +946,19 @@ int writeback_device_locked(const void* const* srcs, void* const* host_dsts, uin
     }
     if (!CUDA_OK(cudaMemcpyAsync(slot.dev_aad, slot.host_aad, 64ull * n, cudaMemcpyHostToDevice, stream))) return -1;
     const uint32_t v_first = cp.kind == SECURE_INFER_KIND_KV ? n / 2 : (cp.kind == 1 ? 0u : n);
+    // The keystream needs only the tickets: it runs on the producer stream
+    // beside the quantiser (the two kernels share SMs: one is bound by the
+    // shared-memory pipe, the other by issue), and the encrypt kernel waits
+    // for both.  The producer first waits for this stream's earlier work, the
+    // slot's previous user.
+    if ((!slot.ks_ready && !CUDA_OK(cudaEventCreateWithFlags(&slot.ks_ready, cudaEventDisableTiming))) ||
+        (!slot.copied && !CUDA_OK(cudaEventCreateWithFlags(&slot.copied, cudaEventDisableTiming))))
+        return -1;
+    if (!CUDA_OK(cudaEventRecord(slot.copied, stream)) || !CUDA_OK(cudaStreamWaitEvent(g_s.producer, slot.copied, 0)))
+        return -1;
+    if (keystream_records_locked(tk.data(), n, count, slot.ks, g_s.producer) != 0 ||
+        !CUDA_OK(cudaEventRecord(slot.ks_ready, g_s.producer)))
+        return -1;
     if (cp.bits) {
         if (!CUDA_OK(cudaMemcpyAsync(slot.dev_ptrs, slot.host_ptrs, sizeof(void*) * n, cudaMemcpyHostToDevice, stream)))
             return -1;
@@ -959,7 +972,7 @@ int writeback_device_locked(const void* const* srcs, void* const* host_dsts, uin
         E.v_first = v_first;
         if (launch_encode(E, stream) != cudaSuccess) return -1;
     }
-    if (keystream_records_locked(tk.data(), n, count, slot.ks, stream) != 0) return -1;
+    if (!CUDA_OK(cudaStreamWaitEvent(stream, slot.ks_ready, 0))) return -1;
     std::vector<LayerRec> recs(std::min<uint32_t>(n, kLayerCapLarge));
     for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
         const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
@@ -1117,11 +1130,18 @@ void shutdown_locked()
         if (s.copied) cudaEventDestroy(s.copied);
         s.ks_ready = s.copied = nullptr;
     }
-    for (auto& s : g_s.d2h) free_stage(s);
+    for (auto& s : g_s.d2h) {
+        free_stage(s);
+        if (s.ks_ready) cudaEventDestroy(s.ks_ready);
+        if (s.copied) cudaEventDestroy(s.copied);
+        s.ks_ready = s.copied = nullptr;
+    }
     for (auto& s : g_s.wb) {
         free_stage(s);
         if (s.done) cudaEventDestroy(s.done);
-        s.done = nullptr;
+        if (s.ks_ready) cudaEventDestroy(s.ks_ready);
+        if (s.copied) cudaEventDestroy(s.copied);
+        s.done = s.ks_ready = s.copied = nullptr;
     }
     for (auto& s : g_s.launch) {
         cudaFreeHost(s.host_recs); cudaFreeHost(s.host_jobs);
