@@ -262,6 +262,43 @@ def test_reload_records_shared_keystream_across_streams(nl):
         assert torch.equal(dests[layer].cpu(), hosts[layer]), layer
 
 
+def test_kernel_profile_counts_reload_launches(nl):
+    """secure_infer_kernel_profile_*: one device-resident reload of a layer is
+    one keystream launch and one verify launch, each with a device time."""
+    heads, n = 2, 4
+    lib = nl._native.lib()
+    count = 128 * heads * 128 * 2
+    stride = nl.record_bytes(count)
+    host = bf16_random((n, 128, heads, 128), 901).pin_memory()
+    recs = torch.zeros((n, stride), dtype=torch.uint8).pin_memory()
+    tk = (ct.c_uint64 * n)()
+    assert lib.secure_infer_h2d_encrypt_records(nl._ptrs(host.data_ptr() + i * count for i in range(n)), count, n,
+                                                recs.data_ptr(), stride, tk) == 0
+    drecs = recs.cuda()
+    dest = torch.zeros((n, 128, heads, 128), dtype=torch.bfloat16, device="cuda")
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
+    status = torch.zeros(n, dtype=torch.int32, device="cuda")
+    kinds = 16
+    us, cnt = (ct.c_double * kinds)(), (ct.c_uint64 * kinds)()
+    torch.cuda.synchronize()
+    lib.secure_infer_kernel_profile_collect(us, cnt, kinds)           # drop anything recorded earlier
+    assert lib.secure_infer_kernel_profile_enable(1) == 0
+    try:
+        s = nl._stream()
+        assert lib.secure_infer_reload_records(3, drecs.data_ptr(), stride, count, n, tk,
+                                               nl._ptrs(dest.data_ptr() + i * count for i in range(n)),
+                                               ks.data_ptr(), status.data_ptr(), None, s, s) == 0
+        torch.cuda.synchronize()
+        assert lib.secure_infer_kernel_profile_collect(us, cnt, kinds) == 0
+    finally:
+        lib.secure_infer_kernel_profile_enable(0)
+    got = {lib.secure_infer_kernel_name(k).decode(): (cnt[k], us[k]) for k in range(kinds)
+           if lib.secure_infer_kernel_name(k) is not None and cnt[k]}
+    assert set(got) == {"gcm_layer_ctr_kernel", "gcm_layer_verify_kernel"}
+    assert all(c == 1 and t > 0 for c, t in got.values())
+    assert status.cpu().tolist() == [1] * n and torch.equal(dest.cpu(), host)
+
+
 def test_group_bracket_and_job_auth(nl):
     heads, blocks, layer = 1, 5, 11
     host = bf16_random((blocks, 128, heads, 128), 88).pin_memory()

@@ -27,3 +27,20 @@ def test_python_signatures_cover_declarations():
     from secure_infer_b200 import _native
     bound = set(_native.PLUGIN_SIGNATURES) | set(_native.HOST_SIGNATURES)
     assert declared_functions() <= bound
+
+
+def test_kernel_profile_names_and_empty_collect():
+    """The kernel profile entry points work without a GPU when nothing ran."""
+    import ctypes as ct
+    from secure_infer_b200 import _native
+    lib = _native.lib()
+    names = []
+    k = 0
+    while (name := lib.secure_infer_kernel_name(k)) is not None:
+        names.append(name.decode())
+        k += 1
+    assert {"gcm_layer_ctr_kernel", "gcm_layer_verify_kernel", "gcm_layer_encrypt", "kv_encode_kernel"} <= set(names)
+    us = (ct.c_double * len(names))()
+    cnt = (ct.c_uint64 * len(names))()
+    assert lib.secure_infer_kernel_profile_collect(us, cnt, len(names)) == 0
+    assert list(cnt) == [0] * len(names)
