@@ -62,10 +62,14 @@ CONFIGS = {
 # from the ncu capture summarised in profiles/ (scaled per launch); None until
 # captured for a config.
 NCU_TRAFFIC_BYTES = {
-    # one c2 layer (96 records x 256 KiB): ciphertext + keystream read, bf16 out mostly still in L2 at exit
-    ("c2", "gcm_layer_verify_kernel"): 50_543_360 + 1_207_808,
+    # one c2 layer (96 records x 256 KiB): ciphertext + keystream read; most of
+    # the bf16 output is still in L2 when the kernel ends
+    ("c2", "gcm_layer_verify_kernel"): 50_554_880 + 2_394_624,
     # one c5 layer (128 records x 10256 B, K+V in one launch)
     ("c5", "gcm_layer_verify_kernel"): 2_836_224,
+    # one c4 layer (128 blocks of 8 heads): bf16 read; packets stay in L2
+    ("c4", "kv_encode_kernel"): 33_612_800 + 768,
+    ("c4", "gcm_layer_encrypt"): 21_165_568,
 }
 
 # Shared-memory wavefronts per 16-byte block that the algorithm needs (the
