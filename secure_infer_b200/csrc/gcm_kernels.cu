@@ -698,17 +698,24 @@ __device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecPa
                                               const uint8_t* in, const uint8_t* ksp, uint8_t* out, uint32_t& key,
                                               float (&sc)[32], float (&lo)[32])
 {
+    // q -> fp32 without the conversion unit: a byte permute places q in the
+    // low mantissa byte of 2^23 (0x4B000000), and subtracting 2^23 is exact.
+    constexpr uint32_t kTwo23 = 0x4B000000u;
     const uint32_t w[4] = {p.x, p.y, p.z, p.w};
     float q[N];
     if constexpr (N == 16) {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) q[k] = static_cast<float>((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
+        for (int k = 0; k < 16; ++k)
+            q[k] = __fsub_rn(__uint_as_float(__byte_perm(w[k >> 2], kTwo23, 0x7650u | (k & 3))), 8388608.0f);
     } else {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const uint32_t byte = (w[k >> 2] >> (8 * (k & 3))) & 0xffu;
-            q[2 * k] = static_cast<float>(byte & 0xfu);
-            q[2 * k + 1] = static_cast<float>(byte >> 4);
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t lo4 = w[j] & 0x0f0f0f0fu, hi4 = (w[j] >> 4) & 0x0f0f0f0fu;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                q[8 * j + 2 * b] = __fsub_rn(__uint_as_float(__byte_perm(lo4, kTwo23, 0x7650u | b)), 8388608.0f);
+                q[8 * j + 2 * b + 1] = __fsub_rn(__uint_as_float(__byte_perm(hi4, kTwo23, 0x7650u | b)), 8388608.0f);
+            }
         }
     }
     const uint32_t e0 = static_cast<uint32_t>(c) * N;
@@ -745,12 +752,12 @@ __device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecPa
     }
 }
 
-enum : int { kLayerVerifyRaw = 0, kLayerVerifyCodec = 1, kLayerEncrypt = 2 };
+enum : int { kLayerVerifyRaw = 0, kLayerVerifyCodec8 = 1, kLayerEncrypt = 2, kLayerVerifyCodec4 = 3 };
 
 template <int kCap, int kMode>
 __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
-    constexpr bool kCodec = kMode == kLayerVerifyCodec;
+    constexpr bool kCodec = kMode == kLayerVerifyCodec8 || kMode == kLayerVerifyCodec4;
     constexpr bool kEncrypt = kMode == kLayerEncrypt;
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* gtab = reinterpret_cast<uint4*>(smem);
@@ -852,12 +859,9 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
             if (i >= a_blk && i < a_blk + n_blk) {
                 const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
                 if constexpr (kCodec) {
-                    if (off < cp.qb) {
-                        if (cp.bits == 8)
-                            layer_dequant<16>(xor4(x0, k0), off >> 4, cp, kind, in, ksp, out, pkey, psc, plo);
-                        else
-                            layer_dequant<32>(xor4(x0, k0), off >> 4, cp, kind, in, ksp, out, pkey, psc, plo);
-                    }
+                    if (off < cp.qb)
+                        layer_dequant<kMode == kLayerVerifyCodec8 ? 16 : 32>(xor4(x0, k0), off >> 4, cp, kind, in,
+                                                                           ksp, out, pkey, psc, plo);
                 } else if constexpr (kEncrypt) {
                     // C is zero past `count` (both loads are), so the whole
                     // block goes out: the record's padding must be zero.
@@ -1463,15 +1467,22 @@ int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t 
     int dev = 0;
     cudaGetDevice(&dev);
     // One CTA of 8 warps per SM (160 KiB of tables in shared memory).
-    static bool set_small_c[64], set_large_c[64];
+    static bool set_small_8[64], set_large_8[64], set_small_4[64], set_large_4[64];
     const uint32_t grid = (items + kLayerWarps - 1) / kLayerWarps;
     const bool small = h.n <= static_cast<uint32_t>(kLayerCapSmall);
-    if (h.codec.bits) {
+    if (h.codec.bits == 8) {
         if (small)
-            return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec>, h, rec,
-                                                kLayerThreads, kLayerSmem, grid, set_small_c[dev & 63], stream, 1);
-        return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec>, h, rec,
-                                            kLayerThreads, kLayerSmem, grid, set_large_c[dev & 63], stream, 1);
+            return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec8>,
+                                                h, rec, kLayerThreads, kLayerSmem, grid, set_small_8[dev & 63], stream, 1);
+        return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec8>,
+                                            h, rec, kLayerThreads, kLayerSmem, grid, set_large_8[dev & 63], stream, 1);
+    }
+    if (h.codec.bits == 4) {
+        if (small)
+            return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec4>,
+                                                h, rec, kLayerThreads, kLayerSmem, grid, set_small_4[dev & 63], stream, 1);
+        return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec4>,
+                                            h, rec, kLayerThreads, kLayerSmem, grid, set_large_4[dev & 63], stream, 1);
     }
     if (small)
         return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyRaw>, h, rec,

@@ -201,6 +201,53 @@ def test_tamper_precencrypted_is_fatal_and_zeroed(nl):
     assert lib.secure_infer_h2d_reload_layer(layer, rsrc, dsts, n, count, None, 1, tickets, nl._stream()) == -1
 
 
+@pytest.mark.parametrize("bits", [8, 4])
+def test_codec_tamper_fails_closed(nl, bits):
+    """A K+V codec reload where one record's quantised bytes, one record's
+    scale array and one record's tag were altered: exactly those records get
+    status 0 and their whole bf16 destination block zeroed, the rest decode."""
+    from oracle import gcm as orc
+    heads, layer = 2, 13
+    lib = nl._native.lib()
+    cache = bf16_random((8, 128, heads, 128), 700 + bits).cuda()
+    ids = [5, 1, 6, 2, 7, 0]
+    n = len(ids)
+    bb = 128 * heads * 128 * 2
+    count = nl.packet_bytes(heads, bits)
+    stride = nl.record_bytes(count)
+    aligned = orc.record_aligned_bytes(count)
+    qb = 128 * heads * 128 * bits // 8
+    records = torch.zeros((n, stride), dtype=torch.uint8, device="cuda")
+    tickets = (ct.c_uint64 * n)()
+    codec = nl._native.Codec(bits, nl._native.KIND_KV, heads, layer)
+    assert lib.secure_infer_writeback_records(nl._ptrs(cache.data_ptr() + i * bb for i in ids), None, n,
+                                              ct.byref(codec), records.data_ptr(), stride, tickets,
+                                              nl._stream()) == 0
+    torch.cuda.synchronize()
+    records[1, qb // 2] ^= 0x10          # K record: quantised byte
+    records[3, qb + 8] ^= 0x01           # V record: scale array
+    records[4, aligned + 5] ^= 0x80      # V record: tag
+    dest = torch.full((n, 128, heads, 128), 2.0, dtype=torch.bfloat16, device="cuda")
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
+    status = torch.full((n,), 7, dtype=torch.int32, device="cuda")
+    assert lib.secure_infer_reload_records(layer, records.data_ptr(), stride, count, n, tickets,
+                                           nl._ptrs(dest.data_ptr() + i * bb for i in range(n)), ks.data_ptr(),
+                                           status.data_ptr(), ct.byref(codec), nl._stream(), None) == 0
+    torch.cuda.synchronize()
+    assert status.cpu().tolist() == [1, 0, 1, 0, 0, 1]
+    got = u16(dest)
+    src = u16(cache)
+    for i in range(n):
+        if i in (1, 3, 4):
+            assert not got[i].any(), i
+        else:
+            kind = 0 if i < n // 2 else 1
+            pk, q_b, s_b = codec_oracle.encode(src, [ids[i]], bits, kind, layer)
+            exp = np.zeros((1, 128, heads, 128), np.uint16)
+            codec_oracle.decode_into(pk, exp, [0], bits, kind, q_b, s_b)
+            assert np.array_equal(got[i], exp[0]), i
+
+
 def test_reload_records_device_resident(nl):
     heads, n, layer = 4, 8, 2
     host = bf16_random((n, 128, heads, 128), 66).pin_memory()
