@@ -275,6 +275,37 @@ def test_reload_records_device_resident(nl):
         assert torch.equal(dest.cpu()[order], host)
 
 
+@pytest.mark.parametrize("count,n,dst_offset", [(1000, 7, 4), (48, 1500, 0), (16, 3, 2), (4097, 33, 0)])
+def test_reload_records_odd_sizes_and_chunks(nl, count, n, dst_offset):
+    """Device-resident reload of raw records whose size is not a multiple of
+    16, into unaligned destinations, and more records than one launch holds
+    (1024): every byte lands, nothing past `count` is written."""
+    lib = nl._native.lib()
+    stride = nl.record_bytes(count)
+    g = torch.Generator().manual_seed(count + n)
+    plain = torch.randint(0, 256, (n, count), dtype=torch.uint8, generator=g).pin_memory()
+    recs = torch.zeros((n, stride), dtype=torch.uint8).pin_memory()
+    tk = (ct.c_uint64 * n)()
+    assert lib.secure_infer_h2d_encrypt_records(nl._ptrs(plain.data_ptr() + i * count for i in range(n)), count, n,
+                                                recs.data_ptr(), stride, tk) == 0
+    drecs = recs.cuda()
+    pitch = count + 64
+    dest = torch.full((n, pitch), 0xA5, dtype=torch.uint8, device="cuda")
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
+    status = torch.zeros(n, dtype=torch.int32, device="cuda")
+    for keystream in (ks.data_ptr(), None):
+        dest.fill_(0xA5)
+        status.zero_()
+        assert lib.secure_infer_reload_records(1, drecs.data_ptr(), stride, count, n, tk,
+                                               nl._ptrs(dest.data_ptr() + i * pitch + dst_offset for i in range(n)),
+                                               keystream, status.data_ptr(), None, nl._stream(), None) == 0
+        torch.cuda.synchronize()
+        got = dest.cpu()
+        assert status.cpu().eq(1).all()
+        assert torch.equal(got[:, dst_offset:dst_offset + count], plain)
+        assert got[:, :dst_offset].eq(0xA5).all() and got[:, dst_offset + count:].eq(0xA5).all()
+
+
 def test_reload_records_shared_keystream_across_streams(nl):
     """Consecutive reloads that share one keystream buffer, with the keystream
     on the session's producer stream: each layer's output must be its own."""
@@ -462,6 +493,32 @@ def test_writeback_records_device_roundtrip(nl, bits, kind):
             assert np.array_equal(got[i], exp[0]), i
         else:
             assert np.array_equal(got[i], src[ids[i]]), i
+
+
+def test_writeback_records_more_than_one_launch(nl):
+    """1030 raw blocks (more than the 1024 records a launch holds) written back
+    on the device and reloaded: every block round-trips."""
+    heads, n, layer = 1, 1030, 14
+    lib = nl._native.lib()
+    bb = 128 * heads * 128 * 2
+    cache = bf16_random((n, 128, heads, 128), 4242).cuda()
+    stride = nl.record_bytes(bb)
+    records = torch.zeros((n, stride), dtype=torch.uint8, device="cuda")
+    tickets = (ct.c_uint64 * n)()
+    codec = nl._native.Codec(0, 0, heads, layer)
+    order = list(reversed(range(n)))
+    assert lib.secure_infer_writeback_records(nl._ptrs(cache.data_ptr() + i * bb for i in order), None, n,
+                                              ct.byref(codec), records.data_ptr(), stride, tickets,
+                                              nl._stream()) == 0
+    dest = torch.zeros_like(cache)
+    ks = torch.empty(n * (bb + 16), dtype=torch.uint8, device="cuda")
+    status = torch.zeros(n, dtype=torch.int32, device="cuda")
+    assert lib.secure_infer_reload_records(layer, records.data_ptr(), stride, bb, n, tickets,
+                                           nl._ptrs(dest.data_ptr() + i * bb for i in range(n)), ks.data_ptr(),
+                                           status.data_ptr(), None, nl._stream(), None) == 0
+    torch.cuda.synchronize()
+    assert status.cpu().eq(1).all()
+    assert torch.equal(dest.cpu(), cache.cpu()[order])
 
 
 def test_writeback_tamper_withheld(nl):
