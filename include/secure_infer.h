@@ -53,7 +53,9 @@ void secure_infer_register_host_range_ex(const void* base, size_t bytes, uint32_
 
 /* ------------------------------------------------------ record helpers */
 
-/* Next transfer ticket (secure_infer.cpp:262-272); never 0. */
+/* Next transfer ticket (secure_infer.cpp:262-272); never 0.  Tickets handed
+ * out here or by secure_infer_h2d_encrypt_records are redeemable once by a
+ * pre-encrypted reload; a replayed or never-issued ticket is rejected. */
 uint64_t secure_infer_new_transfer_ticket(void);
 
 /* IV = base[0..3] || BE64(session_nonce + ticket) || BE32(block_offset + 2)
