@@ -423,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
     uint32_t* aes_rk = aes_te + 256 * 32;
     float* codec_sl = reinterpret_cast<float*>(smem + kGhashSmem + (kInlineAes ? kAesSmem : 0));
     __shared__ uint4 red[kThreads];
+    __shared__ uint4 join_tab[512];     // H^(segment length), for the record's last CTA
     __shared__ uint32_t s_last, s_ok;
 
     const GcmSchedule* __restrict__ S = L.sched;
@@ -433,6 +434,9 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
     const GcmRecord* recs = L.recs ? L.recs : L.inl;
     const SmemAes aes{aes_te, aes_rk, lane};
     const CodecParams cp = L.codec;
+    // Segment length SB (256..4096 blocks) and its join table H^SB.
+    const int64_t SB = L.seg_blocks ? L.seg_blocks : kSegBlocks;
+    const uint4* join_src = S->tab[SB == 4096 ? kTabSeg : tab_pow_32k(static_cast<int>(SB / 32))];
 
     for (uint32_t w = blockIdx.x; w < L.total_segs; w += gridDim.x) {
         uint32_t lo = 0, hi = L.nrec - 1;
@@ -454,9 +458,9 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
         const int64_t n_blk = static_cast<int64_t>((count + 15) >> 4);
         const int64_t m = a_blk + n_blk + 1;
         const uint32_t k = w - R.seg_first;
-        const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * kSegBlocks;
-        const int64_t seg_end = len0 + static_cast<int64_t>(k) * kSegBlocks;
-        const int64_t seg_len = k == 0 ? len0 : kSegBlocks;
+        const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * SB;
+        const int64_t seg_end = len0 + static_cast<int64_t>(k) * SB;
+        const int64_t seg_len = k == 0 ? len0 : SB;
         const int J = static_cast<int>((seg_len + kThreads - 1) / kThreads);
         const int64_t base = seg_end - static_cast<int64_t>(J) * kThreads;
 
@@ -559,6 +563,10 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
         if (!s_last) continue;
 
         __threadfence();
+        if (nseg > 1 && op != kOpXorOnly) {
+            for (uint32_t e = tid; e < 512; e += kThreads) join_tab[e] = __ldg(&join_src[e]);
+            __syncthreads();
+        }
         if (warp == 0) {
             uint4 acc = zero4();
             if (op != kOpXorOnly) {
@@ -569,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
                         const uint4 p = make_uint4(
                             __shfl_sync(0xffffffffu, mine.x, kk), __shfl_sync(0xffffffffu, mine.y, kk),
                             __shfl_sync(0xffffffffu, mine.z, kk), __shfl_sync(0xffffffffu, mine.w, kk));
-                        acc = (k0 == 0 && kk == 0) ? p : xor4(gf_mul_warp<true>(acc, S->tab[kTabSeg], lane), p);
+                        acc = (k0 == 0 && kk == 0) ? p : xor4(gf_mul_warp<false>(acc, join_tab, lane), p);
                     }
                 }
             }
@@ -1321,11 +1329,24 @@ const char* kernel_kind_name(uint32_t kind)
 
 size_t schedule_bytes() { return sizeof(GcmSchedule); }
 
-uint32_t segments_for(uint64_t count, uint32_t aad_bytes)
+uint32_t segments_for(uint64_t count, uint32_t aad_bytes, uint32_t seg_blocks)
 {
     const uint64_t m = (aad_bytes + 15u) / 16u + (count + 15u) / 16u + 1u;
-    const uint64_t n = m / kSegBlocks;
+    const uint64_t n = m / (seg_blocks ? seg_blocks : kSegBlocks);
     return static_cast<uint32_t>(n ? n : 1u);
+}
+
+uint32_t segment_blocks_for(uint64_t total_blocks)
+{
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lock(g_dev_mu);
+        sms = device_info(dev).sms;
+    }
+    uint32_t sb = kSegBlocks;
+    while (sb > 256u && total_blocks / sb < 2u * static_cast<uint64_t>(sms)) sb >>= 1;
+    return sb;
 }
 
 int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream)

@@ -65,6 +65,7 @@ struct SegmentLaunch {
     uint4* partials;                    // [total_segs]
     uint32_t* counters;                 // [nrec], zero on entry, zero on exit
     CodecParams codec;
+    uint32_t seg_blocks;                // segment length: 256..4096 (power of two); 0 = 4096
 };
 
 // AES-CTR keystream / CTR XOR jobs.
@@ -169,7 +170,10 @@ int launch_auth_gate(uint8_t* data, const uint32_t* status, uint64_t bytes, cuda
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream);
 int launch_encode(const EncodeLaunch& args, cudaStream_t stream);
 size_t schedule_bytes();
-uint32_t segments_for(uint64_t count, uint32_t aad_bytes);
+uint32_t segments_for(uint64_t count, uint32_t aad_bytes, uint32_t seg_blocks = 4096);
+// Segment length for a segment-kernel launch covering `total_blocks` 16-byte
+// blocks: the longest of 4096 .. 256 that still gives every SM two segments.
+uint32_t segment_blocks_for(uint64_t total_blocks);
 
 
 }  // namespace sib

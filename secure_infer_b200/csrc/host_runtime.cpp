@@ -684,7 +684,9 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
         return 0;
     }
 
-    const uint32_t nseg = segments_for(count, kAadBytes);
+    const uint32_t seg_blocks = segment_blocks_for(
+        static_cast<uint64_t>(n) * ((kAadBytes + 15u) / 16u + (count + 15u) / 16u + 1u));
+    const uint32_t nseg = segments_for(count, kAadBytes, seg_blocks);
     LaunchSlot& slot = g_s.launch[g_s.launch_next];
     g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
     if (!ensure_launch_slot(slot, n, nseg * n)) return -1;
@@ -720,6 +722,7 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
     L.partials = slot.partials;
     L.counters = slot.counters;
     L.codec = cp;
+    L.seg_blocks = seg_blocks;
     if (launch_segments(L, keystream == nullptr, stream) != cudaSuccess) return -1;
     cudaEventRecord(slot.free_ev, stream);
     slot.used = true;

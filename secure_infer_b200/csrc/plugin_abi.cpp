@@ -99,12 +99,18 @@ int run_records(cudaStream_t stream, const void* key, const void* h, GcmRecord* 
     SegmentLaunch L{};
     uint32_t total = 0;
     bool inline_aes = false;
+    // A call carries one to four records: shorter segments keep the SMs busy
+    // when the payload is small (one 256 KiB record -> 16 segments).
+    uint64_t blocks = 0;
+    for (uint32_t i = 0; i < n; ++i)
+        blocks += (recs[i].aad_bytes + 15u) / 16u + (recs[i].count + 15u) / 16u + 1u;
+    L.seg_blocks = segment_blocks_for(blocks);
     for (uint32_t i = 0; i < n; ++i) {
         if (recs[i].aad_bytes > (1u << 20)) return -1;
         const bool needs_ks = recs[i].op == kOpDecrypt || recs[i].op == kOpEncrypt;
         inline_aes = inline_aes || (needs_ks && recs[i].ks == nullptr);
         recs[i].seg_first = total;
-        recs[i].nseg = segments_for(recs[i].count, recs[i].aad_bytes);
+        recs[i].nseg = segments_for(recs[i].count, recs[i].aad_bytes, L.seg_blocks);
         total += recs[i].nseg;
         L.inl[i] = recs[i];
     }
