@@ -1,12 +1,16 @@
 // gcm_kernels.cu -- sm_100a kernels of the authenticated KV transfer path.
 //
-//   gcm_schedule_kernel  per-key AES round keys + the 40 GHASH nibble tables
-//   gcm_ctr_kernel       AES-CTR keystream (optionally XORed with a payload)
-//   gcm_segment_kernel   segmented GHASH over AAD || payload || len, fused with
-//                        CTR XOR, the fail-closed gate, and (codec records) the
-//                        int8/int4 -> bf16 dequantisation + block-table scatter
-//   kv_encode_kernel     writeback quantisation of bf16 KV blocks into packets
-//   auth_gate_kernel     zero a buffer whose status is not 1
+//   gcm_schedule_kernel      per-key AES round keys + the GHASH nibble tables
+//   gcm_layer_ctr_kernel     keystream + tag masks of a layer's records
+//   gcm_layer_verify_kernel  warp-segmented GHASH fused with CTR XOR, the
+//                            fail-closed gate, int8/int4 -> bf16 dequantisation
+//                            and the block-table scatter; in encrypt mode the
+//                            writeback mirror (XOR, GHASH, tag, record layout)
+//   kv_encode_kernel         writeback quantisation of bf16 KV blocks into packets
+//   gcm_segment_kernel       plugin ABI: CTA-segmented GCM over up to four
+//                            descriptor records (decrypt/verify/encrypt/GHASH/XOR)
+//   gcm_ctr_kernel           plugin ABI: AES-CTR keystream or CTR XOR jobs
+//   auth_gate_kernel         zero a buffer whose status is not 1
 //
 // Semantics follow the reference AICPU kernels
 // (secure_infer/native/kernels/aicpu/ghash.aicpu): counter blocks :133-147,
@@ -343,85 +347,27 @@ __global__ void __launch_bounds__(kCtrThreads, 1) gcm_ctr_kernel(const __grid_co
 // ----------------------------------------------------------------------------
 // Work item = (record, segment).  The block sequence X = AAD || payload || len
 // (m blocks) is cut into segments aligned to its END: the last nseg-1 segments
-// hold kSegBlocks blocks, the first holds the remaining len0 blocks.  Thread t
+// hold SB blocks (256..4096, chosen per launch so small calls still spread over
+// the SMs), the first holds the remaining len0 blocks.  Thread t
 // of the CTA takes blocks base + t + 256 j (coalesced) and runs Horner with
 // H^256; the 256 partials are scaled to S_seg = sum_t Y_t H^(256-t) (see the
 // schedule comment).  Leading zero blocks (base < segment start) leave a
 // zero-started GHASH unchanged.  The last CTA of a record to finish joins the
-// segment partials with H^kSegBlocks, derives E_K(J0), checks/emits the tag
+// segment partials with H^SB (staged in shared memory), derives E_K(J0),
+// checks/emits the tag
 // and, on authentication failure, zeroes everything the record wrote
 // ("write then gate": nothing is released before the stream reaches the
 // layer event recorded after this kernel).
 constexpr int kBatch = 8;
 constexpr size_t kGhashSmem = 4096 * sizeof(uint4);          // H^256 table, 8 replicas
 constexpr size_t kAesSmem = 256 * 32 * sizeof(uint32_t) + 256; // T-table replicas + round keys
-constexpr uint32_t kMaxCodecParamBytes = 32768;               // staged scale+low
-
-template <int N>
-__device__ __forceinline__ void dequant_store(const float (&q)[N], uint32_t e0, const CodecParams& cp,
-                                              const float* scale, const float* low, uint8_t* out)
-{
-    float v[N];
-    if (cp.kind == 0) {
-        const uint32_t hd = cp.heads * 128u;
-        const uint32_t sidx0 = (e0 / (64u * hd)) * hd + (e0 % hd);
-#pragma unroll
-        for (int k = 0; k < N; k += 4) {
-            const float4 s4 = *reinterpret_cast<const float4*>(scale + sidx0 + k);
-            const float4 l4 = *reinterpret_cast<const float4*>(low + sidx0 + k);
-            v[k + 0] = __fadd_rn(__fmul_rn(q[k + 0], s4.x), l4.x);
-            v[k + 1] = __fadd_rn(__fmul_rn(q[k + 1], s4.y), l4.y);
-            v[k + 2] = __fadd_rn(__fmul_rn(q[k + 2], s4.z), l4.z);
-            v[k + 3] = __fadd_rn(__fmul_rn(q[k + 3], s4.w), l4.w);
-        }
-    } else {
-        const uint32_t sidx = e0 / 64u;
-        const float s = scale[sidx], l = low[sidx];
-#pragma unroll
-        for (int k = 0; k < N; ++k) v[k] = __fadd_rn(__fmul_rn(q[k], s), l);
-    }
-    uint4* dst = reinterpret_cast<uint4*>(out + 2u * static_cast<size_t>(e0));
-#pragma unroll
-    for (int k = 0; k < N; k += 8) {
-        uint4 o;
-        __nv_bfloat162 b;
-        b = __floats2bfloat162_rn(v[k + 0], v[k + 1]); o.x = *reinterpret_cast<uint32_t*>(&b);
-        b = __floats2bfloat162_rn(v[k + 2], v[k + 3]); o.y = *reinterpret_cast<uint32_t*>(&b);
-        b = __floats2bfloat162_rn(v[k + 4], v[k + 5]); o.z = *reinterpret_cast<uint32_t*>(&b);
-        b = __floats2bfloat162_rn(v[k + 6], v[k + 7]); o.w = *reinterpret_cast<uint32_t*>(&b);
-        dst[k / 8] = o;
-    }
-}
-
-__device__ __forceinline__ void dequant_block(uint4 p, uint64_t c, const CodecParams& cp, const float* scale,
-                                              const float* low, uint8_t* out)
-{
-    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
-    if (cp.bits == 8) {
-        float q[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) q[k] = static_cast<float>((w[k >> 2] >> (8 * (k & 3))) & 0xffu);
-        dequant_store<16>(q, static_cast<uint32_t>(c * 16u), cp, scale, low, out);
-    } else {
-        float q[32];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            const uint32_t byte = (w[k >> 2] >> (8 * (k & 3))) & 0xffu;
-            q[2 * k] = static_cast<float>(byte & 0xfu);
-            q[2 * k + 1] = static_cast<float>(byte >> 4);
-        }
-        dequant_store<32>(q, static_cast<uint32_t>(c * 32u), cp, scale, low, out);
-    }
-}
-
-template <bool kInlineAes, bool kCodec>
+template <bool kInlineAes>
 __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_constant__ SegmentLaunch L)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* gtab = reinterpret_cast<uint4*>(smem);
     uint32_t* aes_te = reinterpret_cast<uint32_t*>(smem + kGhashSmem);
     uint32_t* aes_rk = aes_te + 256 * 32;
-    float* codec_sl = reinterpret_cast<float*>(smem + kGhashSmem + (kInlineAes ? kAesSmem : 0));
     __shared__ uint4 red[kThreads];
     __shared__ uint4 join_tab[512];     // H^(segment length), for the record's last CTA
     __shared__ uint32_t s_last, s_ok;
@@ -433,7 +379,6 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
     __syncthreads();
     const GcmRecord* recs = L.recs ? L.recs : L.inl;
     const SmemAes aes{aes_te, aes_rk, lane};
-    const CodecParams cp = L.codec;
     // Segment length SB (256..4096 blocks) and its join table H^SB.
     const int64_t SB = L.seg_blocks ? L.seg_blocks : kSegBlocks;
     const uint4* join_src = S->tab[SB == 4096 ? kTabSeg : tab_pow_32k(static_cast<int>(SB / 32))];
@@ -463,22 +408,6 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
         const int64_t seg_len = k == 0 ? len0 : SB;
         const int J = static_cast<int>((seg_len + kThreads - 1) / kThreads);
         const int64_t base = seg_end - static_cast<int64_t>(J) * kThreads;
-
-        if constexpr (kCodec) {
-            // Stage the decrypted scale/low arrays when this segment holds
-            // quantised bytes (they sit after q in the packet).
-            const int64_t c_lo = (base > a_blk ? base : a_blk) - a_blk;
-            const bool needs = op == kOpDecrypt && c_lo < static_cast<int64_t>(cp.qb >> 4) && seg_end > a_blk;
-            __syncthreads();
-            if (needs) {
-                const uint32_t n16 = (2u * cp.sb) >> 4;
-                for (uint32_t i = tid; i < n16; i += kThreads) {
-                    const uint64_t off = cp.qb + 16ull * i;
-                    reinterpret_cast<uint4*>(codec_sl)[i] = xor4(ldg16(in + off), ldg16(ksp + off));
-                }
-            }
-            __syncthreads();
-        }
 
         uint4 Y = zero4();
         for (int jb = 0; jb < J; jb += kBatch) {
@@ -521,12 +450,7 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
                         if (!ksp) ks = aes.encrypt(ctr_block_le(R.iv, c));
                     }
                     if (op == kOpDecrypt) {
-                        const uint4 P = xor4(X, ks);
-                        if constexpr (kCodec) {
-                            if (off < cp.qb) dequant_block(P, c, cp, codec_sl, codec_sl + (cp.sb >> 2), out);
-                        } else {
-                            store_block(out + off, P, avail, aligned);
-                        }
+                        store_block(out + off, xor4(X, ks), avail, aligned);
                     } else if (op == kOpEncrypt) {
                         const uint4 C = mask_bytes(xor4(X, ks), avail);
                         store_block(out + off, C, avail, aligned);
@@ -608,9 +532,8 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
         __syncthreads();
         const bool gated = op == kOpDecrypt || (op == kOpGhash && (flags & kGhashXorOnSuccess));
         if (!s_ok && gated && out) {
-            const uint64_t bytes = kCodec ? 2ull * 128u * cp.heads * 128u : count;
-            for (uint64_t off = static_cast<uint64_t>(tid) * 16u; off < bytes; off += 16u * kThreads)
-                store_block(out + off, zero4(), bytes - off, aligned);
+            for (uint64_t off = static_cast<uint64_t>(tid) * 16u; off < count; off += 16u * kThreads)
+                store_block(out + off, zero4(), count - off, aligned);
         }
     }
 }
@@ -1257,7 +1180,7 @@ private:
     bool active_ = false;
 };
 
-template <bool A, bool C>
+template <bool A>
 int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cudaStream_t stream)
 {
     int dev = 0;
@@ -1267,11 +1190,11 @@ int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cud
         std::lock_guard<std::mutex> lock(g_dev_mu);
         DeviceInfo& d = device_info(dev);
         if (!d.attr_set[variant]) {
-            const size_t max_smem = kGhashSmem + kAesSmem + kMaxCodecParamBytes;
-            cudaError_t e = cudaFuncSetAttribute(gcm_segment_kernel<A, C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            const size_t max_smem = kGhashSmem + kAesSmem;
+            cudaError_t e = cudaFuncSetAttribute(gcm_segment_kernel<A>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  static_cast<int>(max_smem));
             if (e != cudaSuccess) return e;
-            e = cudaFuncSetAttribute(gcm_segment_kernel<A, C>, cudaFuncAttributePreferredSharedMemoryCarveout,
+            e = cudaFuncSetAttribute(gcm_segment_kernel<A>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                      cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
             d.attr_set[variant] = true;
@@ -1280,7 +1203,7 @@ int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cud
         per_sm = d.seg_blocks_per_sm[variant];
     }
     if (per_sm == 0) {
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gcm_segment_kernel<A, C>, kThreads, smem);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gcm_segment_kernel<A>, kThreads, smem);
         if (per_sm < 1) per_sm = 1;
         std::lock_guard<std::mutex> lock(g_dev_mu);
         device_info(dev).seg_blocks_per_sm[variant] = per_sm;
@@ -1288,7 +1211,7 @@ int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cud
     const uint32_t grid = static_cast<uint32_t>(
         args.total_segs < static_cast<uint32_t>(sms * per_sm) ? args.total_segs : sms * per_sm);
     ProfileScope prof(kKernSegment, stream);
-    gcm_segment_kernel<A, C><<<grid, kThreads, smem, stream>>>(args);
+    gcm_segment_kernel<A><<<grid, kThreads, smem, stream>>>(args);
     return cudaGetLastError();
 }
 
@@ -1531,12 +1454,9 @@ int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream)
 {
     if (args.total_segs == 0) return cudaSuccess;
-    const bool codec = args.codec.bits != 0;
-    if (codec && (inline_aes || 2u * args.codec.sb > kMaxCodecParamBytes)) return cudaErrorInvalidValue;
-    const size_t smem = kGhashSmem + (inline_aes ? kAesSmem : 0) + (codec ? 2u * args.codec.sb : 0);
-    if (inline_aes) return segment_launch_impl<true, false>(args, smem, 1, stream);
-    if (codec) return segment_launch_impl<false, true>(args, smem, 2, stream);
-    return segment_launch_impl<false, false>(args, smem, 0, stream);
+    const size_t smem = kGhashSmem + (inline_aes ? kAesSmem : 0);
+    if (inline_aes) return segment_launch_impl<true>(args, smem, 1, stream);
+    return segment_launch_impl<false>(args, smem, 0, stream);
 }
 
 int launch_encode(const EncodeLaunch& args, cudaStream_t stream)

@@ -23,7 +23,6 @@ enum : uint32_t {
     kGhashVerify = 1u << 1,
     kGhashXorOnSuccess = 1u << 2,
     kRecUnaligned = 1u << 8,   // some pointer is not 16-byte aligned
-    kRecCodec = 1u << 9,       // out is a bf16 KV block; payload is a codec packet
 };
 
 struct GcmRecord {
@@ -45,7 +44,7 @@ struct GcmRecord {
     uint32_t reserved;
 };
 
-// KV codec geometry for kRecCodec records (one layer/kind per launch).
+// KV codec geometry of a layer launch (one bit width per launch).
 struct CodecParams {
     uint32_t bits;    // 8 or 4
     uint32_t kind;    // 0 = K (64-token groups per channel), 1 = V (64-dim groups)
@@ -64,7 +63,6 @@ struct SegmentLaunch {
     uint32_t total_segs;
     uint4* partials;                    // [total_segs]
     uint32_t* counters;                 // [nrec], zero on entry, zero on exit
-    CodecParams codec;
     uint32_t seg_blocks;                // segment length: 256..4096 (power of two); 0 = 4096
 };
 

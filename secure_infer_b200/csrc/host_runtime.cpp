@@ -707,10 +707,6 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
         r.seg_first = i * nseg;
         r.nseg = nseg;
         if (rec_misaligned || misaligned(dsts[i]) || misaligned(r.ks)) r.flags |= kRecUnaligned;
-        if (cp.bits) {
-            if (r.flags & kRecUnaligned) return -1;
-            r.flags |= kRecCodec;
-        }
     }
     if (!CUDA_OK(cudaMemcpyAsync(slot.dev_recs, slot.host_recs, sizeof(GcmRecord) * n, cudaMemcpyHostToDevice, stream)))
         return -1;
@@ -721,7 +717,6 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
     L.total_segs = nseg * n;
     L.partials = slot.partials;
     L.counters = slot.counters;
-    L.codec = cp;
     L.seg_blocks = seg_blocks;
     if (launch_segments(L, keystream == nullptr, stream) != cudaSuccess) return -1;
     cudaEventRecord(slot.free_ev, stream);
