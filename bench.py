@@ -108,27 +108,59 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 200 ms during timing."""
+    """SM clock and clock-event reasons sampled during the timed region: every
+    5 ms through NVML (read only), or every 200 ms from nvidia-smi when NVML
+    cannot be used."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
         self.proc = None
+        self.samples = []
+        self.max_mhz = None
+        self.source = None
 
     def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            handle = pynvml.nvmlDeviceGetHandleByUUID(self.gpu_id)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+            self._stop = threading.Event()
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)),
+                                             int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+                    except pynvml.NVMLError:
+                        pass
+                    self._stop.wait(0.005)
+
+            self._thread = threading.Thread(target=poll, daemon=True)
+            self._thread.start()
+            self.source = "nvml, 5 ms"
+            return self
+        except Exception:
+            self.samples, self.source = [], None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                                           "-lms", "200", "-i", self.gpu_id], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvidia-smi, 200 ms"
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.source and self.source.startswith("nvml"):
+            self._stop.set()
+            self._thread.join()
+            return
         if self.proc is not None:
             time.sleep(0.25)
             self.proc.terminate()
@@ -137,25 +169,28 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            for ln in out.splitlines():
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm, self.max_mhz = float(f[1]), float(f[2])
+                except ValueError:
+                    continue
+                mask = 0
+                for (name, bit), val in zip(self.REASONS.items(), f[5:9]):
+                    if val.lower() == "active":
+                        mask |= bit
+                self.samples.append((sm, mask))
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, f[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [x for x, _ in self.samples]
+        mask = 0
+        for _, m in self.samples:
+            mask |= m
+        reasons = sorted(name for name, bit in self.REASONS.items() if mask & bit)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sm), "source": self.source}
 
 
 def kernel_profile(lib, torch, enqueue_step, layers):
