@@ -499,13 +499,27 @@ void free_stage(StageSlot& s)
     s.cap_recs = 0;
 }
 
-bool ensure_stage(StageSlot& s, uint64_t bytes, uint64_t ks_bytes, uint32_t recs, uint64_t pkt_bytes = 0)
+// H2D staging records are only written by the host and read by the copy
+// engine: write-combined pinned memory avoids the read-for-ownership of every
+// line the encryption writes (SECURE_INFER_WC_STAGING=0 turns it off).
+bool wc_staging()
+{
+    static const bool on = [] {
+        const char* v = std::getenv("SECURE_INFER_WC_STAGING");
+        return v == nullptr || std::atoi(v) != 0;
+    }();
+    return on;
+}
+
+bool ensure_stage(StageSlot& s, uint64_t bytes, uint64_t ks_bytes, uint32_t recs, uint64_t pkt_bytes = 0,
+                  bool host_write_only = false)
 {
     if (s.cap >= bytes && s.ks_cap >= ks_bytes && s.cap_recs >= recs && s.pkt_cap >= pkt_bytes) return true;
     if (s.done) cudaEventSynchronize(s.done);
     free_stage(s);
     const uint32_t r = std::max<uint32_t>(recs, 256);
-    if (!CUDA_OK(cudaHostAlloc(&s.host, bytes, cudaHostAllocDefault)) || !CUDA_OK(cudaMalloc(&s.dev, bytes)) ||
+    const unsigned host_flags = host_write_only && wc_staging() ? cudaHostAllocWriteCombined : cudaHostAllocDefault;
+    if (!CUDA_OK(cudaHostAlloc(&s.host, bytes, host_flags)) || !CUDA_OK(cudaMalloc(&s.dev, bytes)) ||
         (ks_bytes && !CUDA_OK(cudaMalloc(&s.ks, ks_bytes))) ||
         (pkt_bytes && !CUDA_OK(cudaMalloc(&s.pkt, pkt_bytes))) ||
         !CUDA_OK(cudaHostAlloc(&s.host_aad, 64ull * r, cudaHostAllocDefault)) ||
@@ -776,7 +790,7 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     StageSlot& slot = g_s.h2d[g_s.h2d_next];
     g_s.h2d_next = (g_s.h2d_next + 1) % g_s.h2d.size();
     if (slot.owner) harvest(*slot.owner);   // statuses leave the slot before reuse
-    if (!ensure_stage(slot, stride * n, layer_ks_stride(count) * n, n)) return nullptr;
+    if (!ensure_stage(slot, stride * n, layer_ks_stride(count) * n, n, 0, true)) return nullptr;
     if (slot.done) cudaEventSynchronize(slot.done);
 
     std::vector<uint64_t> tickets(n);
