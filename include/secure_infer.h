@@ -38,6 +38,18 @@ extern "C" {
  * are exactly this key and salt.  Resets tickets and the replay set. */
 int secure_infer_session_init(int device, const uint8_t* key16, const uint8_t* iv_salt4);
 
+/* Experimental session setup by key agreement (secure_infer.cpp:449-521,
+ * secure_infer_experimental_device_session): the host draws an X25519 secret
+ * and a 32-byte challenge (OpenSSL RAND_bytes), the device kernel
+ * (secure_infer_aicpu_key_agreement_do) returns its public value and a proof,
+ * the host derives key = BLAKE2b-16(key = shared, "SecureInfer X25519 BLAKE2b
+ * test v1" || host public || device public || challenge), checks the proof
+ * BLAKE2b-32(key = key, challenge) in constant time and derives the salt
+ * BLAKE2b-4(key = shared, "SecureInfer IV salt v1").  The device key schedule
+ * is built from the device's own copy of the key.  Returns 0, or -1 with no
+ * session when any step or the proof check fails. */
+int secure_infer_session_init_key_agreement(int device);
+
 /* Tear down the session (waits for in-flight work, frees staging). */
 int secure_infer_session_shutdown(void);
 

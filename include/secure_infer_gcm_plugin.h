@@ -51,6 +51,15 @@ int secure_infer_aicpu_ghash_do(void* stream, void* input, void* hash_subkey, vo
 /* Zero `data` unless *status == 1.  launcher.asc:116-132 / ghash.aicpu:1051-1068. */
 int secure_infer_aicpu_auth_gate_do(void* stream, void* data, void* status, uint64_t bytes);
 
+/* Device half of the experimental X25519 + BLAKE2b session key agreement
+ * (launcher.asc:23-33 / key_agreement.aicpu): from the host's 32-byte X25519
+ * public value and 32-byte challenge, writes the device public value (32 B),
+ * the 16-byte session key (it stays in device memory) and the 32-byte proof
+ * BLAKE2b(key = session key, challenge); *status (int32) = 0 when done.  The
+ * device secret is hashed from on-chip timers (B200 has no entropy source). */
+int secure_infer_aicpu_key_agreement_do(void* stream, void* host_public, void* challenge, void* device_key,
+                                        void* device_public, void* proof, void* status);
+
 /* AES-128-CTR XOR of `bytes` bytes.  launcher.asc:134-155 / ghash.aicpu:517-535. */
 int secure_infer_aicpu_aes_ctr_do(void* stream, void* input, void* key, void* output, uint64_t bytes,
                                   uint32_t iv_word0, uint32_t iv_word1, uint32_t iv_word2, uint32_t iv_word3);

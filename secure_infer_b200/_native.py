@@ -24,6 +24,7 @@ class NativeLibraryMissing(RuntimeError):
 PLUGIN_SIGNATURES = {
     "secure_infer_aicpu_ghash_do": ([P] * 10 + [U64, U64, U32], I32),
     "secure_infer_aicpu_auth_gate_do": ([P, P, P, U64], I32),
+    "secure_infer_aicpu_key_agreement_do": ([P] * 7, I32),
     "secure_infer_aicpu_aes_ctr_do": ([P, P, P, P, U64] + [U32] * 4, I32),
     "secure_infer_aicpu_keystream_do": ([P, P, P, U64] + [U32] * 4, I32),
     "secure_infer_aicpu_keystream_batch_do": ([P, P, PP, U32P, U64, U32], I32),
@@ -42,6 +43,7 @@ PLUGIN_SIGNATURES = {
 CHARP = ct.c_char_p
 HOST_SIGNATURES: dict[str, tuple[list, object]] = {
     "secure_infer_session_init": ([I32, P, P], I32),
+    "secure_infer_session_init_key_agreement": ([I32], I32),
     "secure_infer_session_shutdown": ([], I32),
     "secure_infer_register_host_range": ([P, SZ], None),
     "secure_infer_register_host_range_ex": ([P, SZ, U32, U32, SZ], None),

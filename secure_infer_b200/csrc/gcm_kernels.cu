@@ -20,6 +20,7 @@
 // (secure_infer/kv_offload/transport_codec.py:22-42, optimized_decode.py:5-27).
 #include "gcm_device.cuh"
 #include "gcm_kernels.cuh"
+#include "kx.cuh"
 
 #include <cuda_bf16.h>
 
@@ -1102,6 +1103,62 @@ __global__ void __launch_bounds__(256, 2) kv_encode_kernel(const __grid_constant
             pkt[hdr + i] = b;
         }
     }
+}
+
+// Device side of the session key agreement (key_agreement.aicpu): a device
+// X25519 key pair, the shared secret with the host's public value, the
+// session key and the proof the host checks.  B200 has no entropy source, so
+// the device secret is a BLAKE2b-512 hash of %globaltimer and clock64 readings
+// that 32 threads take around contended shared-memory atomics: far weaker
+// than the AICPU's /dev/urandom, so callers that can supply a host-agreed key
+// (secure_infer_session_init) should.
+__global__ void __launch_bounds__(32) key_agreement_kernel(const uint8_t* host_public, const uint8_t* challenge,
+                                                           uint8_t* device_key, uint8_t* device_public,
+                                                           uint8_t* proof, int32_t* status)
+{
+    __shared__ unsigned long long samples[32][8];
+    __shared__ uint32_t contended;
+    const uint32_t lane = threadIdx.x;
+    if (lane == 0) {
+        contended = 0;
+        *status = 1;
+    }
+    __syncwarp();
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t spins = 64u + (lane * 7u + static_cast<uint32_t>(i)) % 13u;
+        for (uint32_t j = 0; j < spins; ++j) atomicAdd(&contended, lane ^ j);
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        samples[lane][i] = t ^ (static_cast<unsigned long long>(clock64()) << 17) ^ contended;
+    }
+    __syncwarp();
+    if (lane != 0) return;
+    uint8_t secret[64], shared[32];
+    kx::blake2b(secret, 64, nullptr, 0, reinterpret_cast<const uint8_t*>(samples), sizeof(samples));
+    *status = 2;
+    kx::x25519_public(device_public, secret);
+    kx::x25519(shared, secret, host_public);
+    uint32_t nonzero = 0;
+    for (int i = 0; i < 32; ++i) nonzero |= shared[i];
+    if (nonzero) {
+        *status = 3;
+        kx::derive_key(device_key, shared, host_public, device_public, challenge);
+        kx::derive_proof(proof, device_key, challenge);
+        *status = 0;
+    }
+    for (int i = 0; i < 64; ++i) secret[i] = 0;
+    for (int i = 0; i < 32; ++i) shared[i] = 0;
+}
+
+int launch_key_agreement(const void* host_public, const void* challenge, void* device_key, void* device_public,
+                         void* proof, int32_t* status, cudaStream_t stream)
+{
+    key_agreement_kernel<<<1, 32, 0, stream>>>(static_cast<const uint8_t*>(host_public),
+                                               static_cast<const uint8_t*>(challenge),
+                                               static_cast<uint8_t*>(device_key),
+                                               static_cast<uint8_t*>(device_public), static_cast<uint8_t*>(proof),
+                                               status);
+    return cudaGetLastError();
 }
 
 __global__ void auth_gate_kernel(uint8_t* data, const uint32_t* status, uint64_t bytes)

@@ -165,6 +165,10 @@ int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool nee
 int launch_ctr(const CtrLaunch& args, cudaStream_t stream);
 int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStream_t stream);
 int launch_auth_gate(uint8_t* data, const uint32_t* status, uint64_t bytes, cudaStream_t stream);
+// Device half of the X25519/BLAKE2b session key agreement (32-byte publics,
+// challenge and proof; 16-byte key; status 0 = done).
+int launch_key_agreement(const void* host_public, const void* challenge, void* device_key, void* device_public,
+                         void* proof, int32_t* status, cudaStream_t stream);
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream);
 int launch_encode(const EncodeLaunch& args, cudaStream_t stream);
 size_t schedule_bytes();

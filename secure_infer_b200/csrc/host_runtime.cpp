@@ -24,9 +24,12 @@
 //            verify + decrypt every record with OpenSSL into the host pool
 //            (:2470-2547); a failed record is zeroed and reported.
 #include "gcm_kernels.cuh"
+#include "kx.cuh"
 #include "../../include/secure_infer.h"
 
 #include <openssl/evp.h>
+#include <openssl/rand.h>
+#include <openssl/crypto.h>
 
 #include <algorithm>
 #include <atomic>
@@ -1192,10 +1195,73 @@ using sib::launch_schedule;
 
 #define SI_EXPORT extern "C" __attribute__((visibility("default")))
 
+namespace {
+// Session setup shared by the two entry points.  device_key: the key already
+// in device memory (key agreement), or null to copy key16 to the device.
+int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt4, const void* device_key);
+}  // namespace
+
 SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const uint8_t* iv_salt4)
 {
     if (key16 == nullptr || iv_salt4 == nullptr) return -1;
     std::lock_guard<std::recursive_mutex> lock(g_mu);
+    return session_init_locked(device, key16, iv_salt4, nullptr);
+}
+
+SI_EXPORT int secure_infer_session_init_key_agreement(int device)
+{
+    if (device < 0) return -1;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    shutdown_locked();
+    if (!CUDA_OK(cudaSetDevice(device))) return -1;
+    // Host half (secure_infer.cpp:449-521): fresh X25519 secret and challenge.
+    uint8_t secret[32], challenge[32], host_public[32], device_public[32], proof[32], shared[32];
+    uint8_t key[16], expected[32], salt[4];
+    int32_t status = -1;
+    if (RAND_bytes(secret, sizeof(secret)) != 1 || RAND_bytes(challenge, sizeof(challenge)) != 1) return -1;
+    kx::x25519_public(host_public, secret);
+    uint8_t* d = nullptr;   // [0,32) host public, [32,64) challenge, [64,96) device public, [96,128) proof,
+                            // [128,144) key, [160,164) status
+    cudaStream_t setup = nullptr;
+    bool ok = CUDA_OK(cudaMalloc(&d, 192)) && CUDA_OK(cudaStreamCreateWithFlags(&setup, cudaStreamNonBlocking)) &&
+              CUDA_OK(cudaMemcpyAsync(d, host_public, 32, cudaMemcpyHostToDevice, setup)) &&
+              CUDA_OK(cudaMemcpyAsync(d + 32, challenge, 32, cudaMemcpyHostToDevice, setup)) &&
+              sib::launch_key_agreement(d, d + 32, d + 128, d + 64, d + 96, reinterpret_cast<int32_t*>(d + 160),
+                                        setup) == cudaSuccess &&
+              CUDA_OK(cudaMemcpyAsync(device_public, d + 64, 32, cudaMemcpyDeviceToHost, setup)) &&
+              CUDA_OK(cudaMemcpyAsync(proof, d + 96, 32, cudaMemcpyDeviceToHost, setup)) &&
+              CUDA_OK(cudaMemcpyAsync(&status, d + 160, 4, cudaMemcpyDeviceToHost, setup)) &&
+              CUDA_OK(cudaStreamSynchronize(setup)) && status == 0;
+    if (ok) {
+        kx::x25519(shared, secret, device_public);
+        uint8_t nonzero = 0;
+        for (uint8_t b : shared) nonzero |= b;
+        kx::derive_key(key, shared, host_public, device_public, challenge);
+        kx::derive_proof(expected, key, challenge);
+        kx::derive_salt(salt, shared);
+        uint8_t diff = 0;
+        for (int i = 0; i < 32; ++i) diff |= static_cast<uint8_t>(expected[i] ^ proof[i]);
+        ok = nonzero != 0 && diff == 0;
+    }
+    // The device builds its schedule from its own copy of the key, which then
+    // is wiped with the rest of the handshake buffer.
+    if (ok) ok = session_init_locked(device, key, salt, d + 128) == 0;
+    if (d) {
+        cudaMemset(d, 0, 192);
+        cudaDeviceSynchronize();
+        cudaFree(d);
+    }
+    if (setup) cudaStreamDestroy(setup);
+    OPENSSL_cleanse(secret, sizeof(secret));
+    OPENSSL_cleanse(shared, sizeof(shared));
+    OPENSSL_cleanse(key, sizeof(key));
+    OPENSSL_cleanse(salt, sizeof(salt));
+    return ok ? 0 : -1;
+}
+
+namespace {
+int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt4, const void* device_key)
+{
     shutdown_locked();
     host_only_session = false;
     g_s.device = device;
@@ -1218,7 +1284,8 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
     uint8_t* dkey = nullptr;
     if (!CUDA_OK(cudaMalloc(&g_s.sched, sib::schedule_bytes())) ||
         !CUDA_OK(cudaMemset(g_s.sched, 0, sib::schedule_bytes())) || !CUDA_OK(cudaMalloc(&dkey, 16)) ||
-        !CUDA_OK(cudaMemcpy(dkey, key16, 16, cudaMemcpyHostToDevice)) ||
+        !CUDA_OK(device_key ? cudaMemcpy(dkey, device_key, 16, cudaMemcpyDeviceToDevice)
+                            : cudaMemcpy(dkey, key16, 16, cudaMemcpyHostToDevice)) ||
         !CUDA_OK(cudaStreamCreateWithFlags(&g_s.producer, cudaStreamNonBlocking)) ||
         !CUDA_OK(cudaStreamCreateWithFlags(&g_s.copier, cudaStreamNonBlocking)) ||
         !CUDA_OK(cudaEventCreateWithFlags(&g_s.consumed_ev, cudaEventDisableTiming)) ||
@@ -1244,6 +1311,7 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
     g_s.ready = true;
     return 0;
 }
+}  // namespace
 
 SI_EXPORT int secure_infer_session_shutdown(void)
 {

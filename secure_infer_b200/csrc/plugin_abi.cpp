@@ -177,6 +177,18 @@ SI_EXPORT int secure_infer_aicpu_auth_gate_do(void* stream, void* data, void* st
                             static_cast<cudaStream_t>(stream)) == cudaSuccess ? 0 : -1;
 }
 
+SI_EXPORT int secure_infer_aicpu_key_agreement_do(void* stream, void* host_public, void* challenge, void* device_key,
+                                                  void* device_public, void* proof, void* status)
+{
+    if (host_public == nullptr || challenge == nullptr || device_key == nullptr || device_public == nullptr ||
+        proof == nullptr || status == nullptr)
+        return -1;
+    return launch_key_agreement(host_public, challenge, device_key, device_public, proof,
+                                static_cast<int32_t*>(status), static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? 0
+               : -1;
+}
+
 SI_EXPORT int secure_infer_aicpu_aes_ctr_do(void* stream, void* input, void* key, void* output, uint64_t bytes,
                                             uint32_t iv_word0, uint32_t iv_word1, uint32_t iv_word2,
                                             uint32_t iv_word3)

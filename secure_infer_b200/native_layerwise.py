@@ -82,6 +82,18 @@ class Session:
         if self.lib.secure_infer_session_init(device, self._key, self._salt) != 0:
             raise RuntimeError("secure_infer_session_init failed")
 
+    @classmethod
+    def key_agreement(cls, device: int) -> "Session":
+        """Session whose key and salt come from the X25519 + BLAKE2b handshake
+        with the device (secure_infer.cpp:449-521); the key never reaches
+        Python."""
+        self = cls.__new__(cls)
+        self.lib = _native.lib()
+        self.device = device
+        if self.lib.secure_infer_session_init_key_agreement(device) != 0:
+            raise RuntimeError("secure_infer_session_init_key_agreement failed")
+        return self
+
     def close(self):
         self.lib.secure_infer_session_shutdown()
 
