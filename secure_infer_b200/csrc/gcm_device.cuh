@@ -262,6 +262,37 @@ __device__ __forceinline__ uint4 gf_mul_table(uint4 z, const uint4* __restrict__
     return xor4(acc0, acc1);
 }
 
+// Z * M using M's byte tables: entry (b, v) = v placed at byte b of a block,
+// times M, stored at tab[((b >> 3) * 256 + v) * 8 + (b & 7)] (64 KiB, one
+// copy).  At step s lane rep (= lane & 7) reads byte position s ^ rep, so the
+// eight lanes of a shared-memory phase read eight distinct 16-byte bank groups:
+// 16 conflict-free LDS.128 per product, half the shared-memory traffic of the
+// nibble tables and no replication.
+__device__ __forceinline__ uint4 gf_mul_byte8(uint4 z, const uint4* __restrict__ tab, uint32_t rep)
+{
+    // zp byte s = z byte (s ^ rep): swap word pairs for rep bit 2, then permute
+    // bytes within each word for rep bits 0-1.
+    const bool sw = (rep & 4u) != 0;
+    const uint32_t sel = 0x3210u ^ (0x1111u * (rep & 3u));
+    const uint32_t w[4] = {__byte_perm(sw ? z.y : z.x, 0u, sel), __byte_perm(sw ? z.x : z.y, 0u, sel),
+                           __byte_perm(sw ? z.w : z.z, 0u, sel), __byte_perm(sw ? z.z : z.w, 0u, sel)};
+    const char* base = reinterpret_cast<const char*>(tab);
+    uint4 acc0 = zero4(), acc1 = zero4();
+#pragma unroll
+    for (int s = 0; s < 16; s += 2) {
+        const uint32_t k0 = s & 3, k1 = (s + 1) & 3;
+        const uint32_t v0 = k0 == 0 ? (w[s >> 2] << 7) : (w[s >> 2] >> (8 * k0 - 7));
+        const uint32_t v1 = w[(s + 1) >> 2] >> (8 * k1 - 7);
+        const uint32_t o0 = (v0 & 0x7f80u) | ((((s & 7) ^ rep)) << 4);
+        const uint32_t o1 = (v1 & 0x7f80u) | (((((s + 1) & 7) ^ rep)) << 4);
+        const uint4 e0 = *reinterpret_cast<const uint4*>(base + (s >> 3) * 32768 + o0);
+        const uint4 e1 = *reinterpret_cast<const uint4*>(base + ((s + 1) >> 3) * 32768 + o1);
+        acc0 = xor4(acc0, e0);
+        acc1 = xor4(acc1, e1);
+    }
+    return xor4(acc0, acc1);
+}
+
 // Build the 32x16 nibble table of M (given in BE layout) cooperatively in one
 // warp: lane p produces the 16 entries of nibble position p,
 // T_p[v] = sum over bits of v of M * x^(4p + j) (bit 3 of v <-> j = 0).
@@ -302,8 +333,9 @@ __device__ inline void build_nibble_table_warp(uint4 m_be, uint4* dst, int lane)
 //   tab[e - 1]         H^e,      e = 1..32
 //   tab[30 + k]        H^(32 k), k = 2..64  (tab[38] = H^256, the CTA stride)
 //   tab[95]            H^4096 (CTA segment join)
-// rep32 / lane8 hold shared-memory-ready copies: H^32 replicated 8x, and the
-// eight tables H^(8 - r) interleaved by r, both in the (p, v, r) layout.
+// byte32 / lane8 hold shared-memory-ready copies: H^32 as byte tables (see
+// gf_mul_byte8), and the eight nibble tables H^(8 - r) interleaved by r in
+// the (p, v, r) layout.
 constexpr int kGhashTables = 96;
 constexpr int kThreads = 256;                       // threads per segment CTA
 constexpr int kSegBlocks = 4096;                    // 16-byte blocks per segment
@@ -323,7 +355,7 @@ struct __align__(16) GcmSchedule {
     uint32_t reserved[2];
     uint4 h_le;               // hash subkey H (memory bytes, LE words)
     uint4 tab[kGhashTables][32 * 16];
-    uint4 rep32[32 * 16 * 8]; // H^32, entry (p, v) replicated: [(p * 16 + v) * 8 + r]
+    uint4 byte32[2 * 256 * 8]; // H^32, byte position b, value v at [((b >> 3) * 256 + v) * 8 + (b & 7)]
     uint4 lane8[32 * 16 * 8]; // H^(8 - r) at [(p * 16 + v) * 8 + r], r = 0..7
 };
 

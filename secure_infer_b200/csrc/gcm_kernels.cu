@@ -39,6 +39,12 @@ __device__ __forceinline__ uint4 shfl_xor4(uint4 v, int m)
                       __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
 }
 
+__device__ __forceinline__ uint4 shfl_up4(uint4 v, uint32_t d)
+{
+    return make_uint4(__shfl_up_sync(0xffffffffu, v.x, d), __shfl_up_sync(0xffffffffu, v.y, d),
+                      __shfl_up_sync(0xffffffffu, v.z, d), __shfl_up_sync(0xffffffffu, v.w, d));
+}
+
 __device__ __forceinline__ uint4 warp_xor_reduce(uint4 v)
 {
 #pragma unroll
@@ -97,6 +103,15 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 __device__ __forceinline__ void cp_async_wait_all()
 {
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Wait until at most N of this thread's committed copy groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // mbarrier + bulk (TMA, non-multicast) global -> shared copy of this GPU's
@@ -219,14 +234,36 @@ __global__ void __launch_bounds__(256) gcm_schedule_kernel(const uint8_t* key, c
     // Shared-memory-ready layouts for the layer kernel.
     for (int i = tid; i < 32 * 16 * 8; i += 256) {
         const int e = i >> 3, r = i & 7;
-        S->rep32[i] = S->tab[tab_pow_small(32)][e];
         S->lane8[i] = S->tab[tab_pow_small(8 - r)][e];
+        // byte32 entry i: position b = (i >> 11) * 8 + (i & 7), value v = (i >> 3) & 255;
+        // byte b holds nibbles 2b (high) and 2b + 1 (low).
+        const int b = (i >> 11) * 8 + (i & 7), v = (i >> 3) & 255;
+        const uint4* t32 = S->tab[tab_pow_small(32)];
+        S->byte32[i] = xor4(t32[(2 * b) * 16 + (v >> 4)], t32[(2 * b + 1) * 16 + (v & 15)]);
     }
     __syncthreads();
     if (tid == 0) {
         __threadfence();
         S->reserved[0] = 1u;
         S->valid = 1u;
+    }
+}
+
+// Segment join tables for the layer kernels: for every segment length
+// L = 32 s blocks (s = 1..kMaxWarpSegSteps), the nibble tables of
+// H^(L 2^b), b = 1..5, at out[((s - 1) * 5 + b - 1) * 512].  One warp per s,
+// by repeated squaring from H^(32 s).  Built once per session key.
+__global__ void __launch_bounds__(32) gcm_join_tables_kernel(const GcmSchedule* S, uint4* out)
+{
+    const int s = blockIdx.x + 1, lane = threadIdx.x;
+    const uint4* tab = S->tab[tab_pow_32k(s)];
+    uint4 v = tab[8];                 // entry (0, 8) = the multiplier itself, LE layout
+    for (int b = 1; b <= 5; ++b) {
+        v = gf_mul_warp<false>(v, tab, lane);
+        uint4* dst = out + ((s - 1) * 5 + b - 1) * 512;
+        build_nibble_table_warp(bswap4(v), dst, lane);
+        __syncwarp();
+        tab = dst;
     }
 }
 
@@ -599,9 +636,17 @@ __global__ void __launch_bounds__(kLayerCtrThreads, 1) gcm_layer_ctr_kernel(cons
 // last warp of a record joins the partials with H^(32 k), XORs the tag mask
 // the keystream kernel left behind, compares, writes the status and zeroes
 // the record's output on a mismatch ("write then gate").
-constexpr uint32_t kLayerThreads = 256;
-constexpr uint32_t kLayerWarps = kLayerThreads / 32;
-constexpr size_t kLayerSmem = 2 * kGhashSmem + 4 * 512 * sizeof(uint4);   // rep32, lane8, H^8/16/24, join
+enum : int { kLayerVerifyRaw = 0, kLayerVerifyCodec8 = 1, kLayerEncrypt = 2, kLayerVerifyCodec4 = 3 };
+// Threads per verify/encrypt CTA: one CTA per SM shares the tables.  Raw
+// verify and encrypt fit 128 registers, so 16 warps cover load and ALU
+// latency; the codec modes need more registers and run 8 warps.
+__host__ __device__ constexpr uint32_t layer_threads(int mode)
+{
+    return mode == kLayerVerifyRaw || mode == kLayerEncrypt ? 512u : 256u;
+}
+// byte32 (64 KiB), lane8 (64 KiB), H^8/16/24 (24 KiB), the segment join
+// tables H^(32 S 2^b) for b = 0..4 (40 KiB).
+constexpr size_t kLayerSmem = 2 * kGhashSmem + 8 * 512 * sizeof(uint4);
 constexpr int kLayerPrefetch = 4;
 
 // Decrypted fp32 parameters (scale or low) of a codec packet: N consecutive
@@ -684,10 +729,8 @@ __device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecPa
     }
 }
 
-enum : int { kLayerVerifyRaw = 0, kLayerVerifyCodec8 = 1, kLayerEncrypt = 2, kLayerVerifyCodec4 = 3 };
-
 template <int kCap, int kMode>
-__global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+__global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
     constexpr bool kCodec = kMode == kLayerVerifyCodec8 || kMode == kLayerVerifyCodec4;
     constexpr bool kEncrypt = kMode == kLayerEncrypt;
@@ -695,27 +738,25 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
     uint4* gtab = reinterpret_cast<uint4*>(smem);
     uint4* ltab = reinterpret_cast<uint4*>(smem + kGhashSmem);
     uint4* qtab = reinterpret_cast<uint4*>(smem + 2 * kGhashSmem);   // [3][512]: H^8, H^16, H^24
-    uint4* jtab = qtab + 3 * 512;
+    uint4* jtab = qtab + 3 * 512;                                    // [5][512]: H^(32 S 2^b), b = 0..4
     const GcmSchedule* __restrict__ S = L.h.sched;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u, quarter = lane >> 3;
     const uint32_t seg_steps = L.h.seg_steps;
     __shared__ __align__(8) uint64_t tables_bar;
     // Tables used only after a warp's main loop (lane, quarter and join
-    // tables, 96 KiB) stream in by bulk copy while the main loop runs.
+    // tables, 128 KiB) stream in by bulk copy while the main loop runs.
     if (tid == 0) {
-        mbar_init_expect(&tables_bar, 65536u + 4u * 8192u);
+        mbar_init_expect(&tables_bar, 65536u + 8u * 8192u);
         bulk_g2s(ltab, S->lane8, 65536u, &tables_bar);
         bulk_g2s(qtab, S->tab[tab_pow_small(8)], 8192u, &tables_bar);
         bulk_g2s(qtab + 512, S->tab[tab_pow_small(16)], 8192u, &tables_bar);
         bulk_g2s(qtab + 1024, S->tab[tab_pow_small(24)], 8192u, &tables_bar);
         bulk_g2s(jtab, S->tab[tab_pow_32k(seg_steps)], 8192u, &tables_bar);
+        bulk_g2s(jtab + 512, L.h.join_pow, 4u * 8192u, &tables_bar);
     }
-    // The Horner table H^32 is replicated 8x from its 8 KiB original.
-    for (uint32_t e = tid; e < 512; e += kLayerThreads) {
-        const uint4 v = __ldg(&S->tab[tab_pow_small(32)][e]);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) gtab[e * 8 + r] = v;
-    }
+    // The Horner multiplier H^32 as byte tables (64 KiB).
+    constexpr uint32_t kLayerThreads = layer_threads(kMode), kLayerWarps = kLayerThreads / 32;
+    for (uint32_t e = tid; e < 4096; e += kLayerThreads) gtab[e] = __ldg(&S->byte32[e]);
     __syncthreads();
     // Records, keystream and destinations are touched only after the
     // previous grid (the keystream kernel) has completed.
@@ -753,7 +794,22 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
         const int J = static_cast<int>((seg_len + 31) / 32);
         const int64_t base = seg_end - static_cast<int64_t>(J) * 32;
 
+        // Interior steps [j_lo, j_hi): every lane holds a full 16-byte
+        // payload block of an aligned record, at byte offset off0 + 512 j.
+        // They skip the per-lane AAD / length-block / tail checks.
+        const int64_t n_full = aligned ? static_cast<int64_t>(count >> 4) : 0;
+        const int64_t lo_num = a_blk - base, hi_num = a_blk + n_full - 32 - base;
+        const int j_lo = lo_num <= 0 ? 0 : static_cast<int>((lo_num + 31) / 32);
+        const int j_hi = hi_num < 0 ? 0 : (hi_num / 32 + 1 < J ? static_cast<int>(hi_num / 32 + 1) : J);
+        const int64_t off0 = (base + lane - a_blk) * 16;
+        auto interior = [&](int j) { return j >= j_lo && j < j_hi; };
         auto load = [&](int j, uint4& x, uint4& ks) {
+            if (interior(j)) {
+                const uint64_t off = static_cast<uint64_t>(off0 + 512ll * j);
+                x = ldg16(in + off);
+                ks = ldg16(ksp + off);
+                return;
+            }
             x = zero4();
             ks = zero4();
             const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
@@ -774,19 +830,13 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
                 x = len_blk;
             }
         };
-        uint4 xq[kLayerPrefetch], kq[kLayerPrefetch];
-#pragma unroll
-        for (int u = 0; u < kLayerPrefetch; ++u) load(u, xq[u], kq[u]);
-        uint4 Y = zero4();
+        uint4 Y = zero4();            // Horner accumulator; 0 * H^32 = 0 starts it
         uint32_t pkey = ~0u;          // codec: index of the cached K parameters
         float psc[32], plo[32];
         const uint32_t kind = r >= L.h.v_first ? 1u : 0u;
-#pragma unroll 1
-        for (int j = 0; j < J; ++j) {
-            const uint4 x0 = xq[0], k0 = kq[0];
-#pragma unroll
-            for (int u = 0; u + 1 < kLayerPrefetch; ++u) { xq[u] = xq[u + 1]; kq[u] = kq[u + 1]; }
-            load(j + kLayerPrefetch, xq[kLayerPrefetch - 1], kq[kLayerPrefetch - 1]);
+        // Any step through the general path: AAD, payload, partial and
+        // length blocks in any mix.
+        auto consume = [&](int j, uint4 x0, uint4 k0) {
             const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
             if (i >= a_blk && i < a_blk + n_blk) {
                 const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
@@ -803,8 +853,69 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
                 }
             }
             // GHASH runs over the ciphertext: loaded (verify) or just formed (encrypt).
-            const uint4 h0 = kEncrypt ? xor4(x0, k0) : x0;
-            Y = j == 0 ? h0 : xor4(gf_mul_table<8, false>(Y, gtab, rep), h0);
+            Y = xor4(gf_mul_byte8(Y, gtab, rep), kEncrypt ? xor4(x0, k0) : x0);
+        };
+        // Slot u of a prefetch ring holds step j0 + u and is refilled in
+        // place with step j0 + u + kLayerPrefetch once consumed.  The inner
+        // loops are unrolled so every slot keeps its own registers: moving a
+        // register whose load is still in flight would wait for that load.
+        uint4 xq[kLayerPrefetch], kq[kLayerPrefetch];
+        if constexpr (kCodec) {
+#pragma unroll
+            for (int u = 0; u < kLayerPrefetch; ++u) load(u, xq[u], kq[u]);
+#pragma unroll 1
+            for (int j0 = 0; j0 < J; j0 += kLayerPrefetch) {
+#pragma unroll
+                for (int u = 0; u < kLayerPrefetch; ++u) {
+                    const int j = j0 + u;
+                    if (j >= J) break;
+                    const uint4 x0 = xq[u], k0 = kq[u];
+                    load(j + kLayerPrefetch, xq[u], kq[u]);
+                    consume(j, x0, k0);
+                }
+            }
+        } else {
+            // General head (AAD side), tight interior, general tail (length
+            // block, partial last block).  Interior segments are all interior.
+            const int lo = j_lo < J ? j_lo : J;
+            const int hi = j_hi > lo ? j_hi : lo;
+#pragma unroll 1
+            for (int j = 0; j < lo; ++j) {
+                uint4 x0, k0;
+                load(j, x0, k0);
+                consume(j, x0, k0);
+            }
+#pragma unroll
+            for (int u = 0; u < kLayerPrefetch; ++u) {
+                if (lo + u < hi) {
+                    const uint64_t off = static_cast<uint64_t>(off0 + 512ll * (lo + u));
+                    xq[u] = ldg16(in + off);
+                    kq[u] = ldg16(ksp + off);
+                }
+            }
+#pragma unroll 1
+            for (int j0 = lo; j0 < hi; j0 += kLayerPrefetch) {
+#pragma unroll
+                for (int u = 0; u < kLayerPrefetch; ++u) {
+                    const int j = j0 + u;
+                    if (j >= hi) break;
+                    const uint4 x0 = xq[u], k0 = kq[u];
+                    if (j + kLayerPrefetch < hi) {
+                        const uint64_t nxt = static_cast<uint64_t>(off0 + 512ll * (j + kLayerPrefetch));
+                        xq[u] = ldg16(in + nxt);
+                        kq[u] = ldg16(ksp + nxt);
+                    }
+                    const uint4 c = xor4(x0, k0);
+                    *reinterpret_cast<uint4*>(out + static_cast<uint64_t>(off0 + 512ll * j)) = c;
+                    Y = xor4(gf_mul_byte8(Y, gtab, rep), kEncrypt ? c : x0);
+                }
+            }
+#pragma unroll 1
+            for (int j = hi; j < J; ++j) {
+                uint4 x0, k0;
+                load(j, x0, k0);
+                consume(j, x0, k0);
+            }
         }
         // Two-stage lane combine in shared memory.  If the table copy never
         // completes the partial is poisoned, so the record fails closed
@@ -830,17 +941,27 @@ __global__ void __launch_bounds__(kLayerThreads, 1) gcm_layer_verify_kernel(cons
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
-        // Join the record's partials: lanes load 32 at a time in parallel, then
-        // Horner with H^(32 k) from registers (shuffle broadcast).
+        // Join the record's partials, S = sum_k p_k H^(L (nseg - 1 - k)) with
+        // L = 32 seg_steps blocks per segment: chunks of 32 partials (the
+        // first chunk takes the remainder), each reduced by a tree over the
+        // lanes (level b combines pairs of 2^b-partial groups with H^(L 2^b)),
+        // chunks joined by Horner with H^(32 L).
         uint4 acc = zero4();
-        for (uint32_t k0 = 0; k0 < nseg; k0 += 32) {
-            const uint32_t cnt = nseg - k0 < 32 ? nseg - k0 : 32;
-            const uint4 mine = lane < cnt ? __ldcg(&L.h.partials[r * nseg + k0 + lane]) : zero4();
-            for (uint32_t kk = 0; kk < cnt; ++kk) {
-                const uint4 p = make_uint4(__shfl_sync(0xffffffffu, mine.x, kk), __shfl_sync(0xffffffffu, mine.y, kk),
-                                           __shfl_sync(0xffffffffu, mine.z, kk), __shfl_sync(0xffffffffu, mine.w, kk));
-                acc = (k0 == 0 && kk == 0) ? p : xor4(gf_mul_warp<false>(acc, jtab, lane), p);
+        const uint32_t first = nseg - (nseg - 1) / 32 * 32;
+        for (uint32_t k0 = 0; k0 < nseg;) {
+            const uint32_t cnt = k0 == 0 ? first : 32;
+            const uint32_t pad = 32 - cnt;     // zero partials in front keep the powers aligned
+            uint4 v = lane >= pad ? __ldcg(&L.h.partials[r * nseg + k0 + lane - pad]) : zero4();
+#pragma unroll
+            for (int b = 0; b < 5; ++b) {
+                const uint4 left = shfl_up4(v, 1u << b);
+                const uint32_t grp = (2u << b) - 1u;
+                if ((lane & grp) == grp) v = xor4(gf_mul_table<1, false>(left, jtab + 512 * b, 0), v);
             }
+            v = make_uint4(__shfl_sync(0xffffffffu, v.x, 31), __shfl_sync(0xffffffffu, v.y, 31),
+                           __shfl_sync(0xffffffffu, v.z, 31), __shfl_sync(0xffffffffu, v.w, 31));
+            acc = k0 == 0 ? v : xor4(gf_mul_warp<true>(acc, L.h.join_pow + 4 * 512, lane), v);
+            k0 += cnt;
         }
         const uint4 mask = *reinterpret_cast<const uint4*>(ksp + (L.h.ks_stride - 16));
         if constexpr (kEncrypt) {
@@ -1329,6 +1450,12 @@ uint32_t segment_blocks_for(uint64_t total_blocks)
     return sb;
 }
 
+int launch_join_tables(const GcmSchedule* sched, void* out, cudaStream_t stream)
+{
+    gcm_join_tables_kernel<<<kMaxWarpSegSteps, 32, 0, stream>>>(sched, static_cast<uint4*>(out));
+    return cudaGetLastError();
+}
+
 int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream)
 {
     ProfileScope prof(kKernSchedule, stream);
@@ -1379,11 +1506,12 @@ int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStrea
     return cudaGetLastError();
 }
 
-void layer_segments_for(uint64_t count, uint32_t n, uint32_t* seg_steps, uint32_t* nseg)
+void layer_segments_for(uint64_t count, uint32_t n, uint32_t codec_bits, uint32_t* seg_steps, uint32_t* nseg)
 {
-    // Pick the segment length (32 k blocks, k <= 16) so that n * nseg fills
-    // the resident warps once (2 CTAs x 16 warps per SM); long layers fall
-    // back to the longest segment.
+    // Pick the segment length (32 k blocks, k <= 64) so that n * nseg fills
+    // the resident warps once (one CTA per SM); long layers fall back to the
+    // longest segment.
+    const uint32_t kLayerWarps = layer_threads(codec_bits ? kLayerVerifyCodec8 : kLayerVerifyRaw) / 32;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     {
@@ -1462,50 +1590,56 @@ int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream
 int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
 {
     if (h.n == 0) return cudaSuccess;
-    if (h.n > static_cast<uint32_t>(kLayerCapLarge)) return cudaErrorInvalidValue;
+    if (h.n > static_cast<uint32_t>(kLayerCapLarge) || h.join_pow == nullptr || h.seg_steps < 1 ||
+        h.seg_steps > static_cast<uint32_t>(kMaxWarpSegSteps))
+        return cudaErrorInvalidValue;
     const uint32_t items = h.nseg * h.n;
     static bool set_small[64], set_large[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    // One CTA of 8 warps per SM (160 KiB of tables in shared memory).
+    // One CTA per SM (160 KiB of tables in shared memory).
     static bool set_small_8[64], set_large_8[64], set_small_4[64], set_large_4[64];
-    const uint32_t grid = (items + kLayerWarps - 1) / kLayerWarps;
+    const uint32_t warps = layer_threads(h.codec.bits ? kLayerVerifyCodec8 : kLayerVerifyRaw) / 32;
+    const uint32_t grid = (items + warps - 1) / warps;
     const bool small = h.n <= static_cast<uint32_t>(kLayerCapSmall);
     if (h.codec.bits == 8) {
         if (small)
             return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec8>,
-                                                h, rec, kLayerThreads, kLayerSmem, grid, set_small_8[dev & 63], stream, 1);
+                                                h, rec, layer_threads(kLayerVerifyCodec8), kLayerSmem, grid, set_small_8[dev & 63], stream, 1);
         return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec8>,
-                                            h, rec, kLayerThreads, kLayerSmem, grid, set_large_8[dev & 63], stream, 1);
+                                            h, rec, layer_threads(kLayerVerifyCodec8), kLayerSmem, grid, set_large_8[dev & 63], stream, 1);
     }
     if (h.codec.bits == 4) {
         if (small)
             return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyCodec4>,
-                                                h, rec, kLayerThreads, kLayerSmem, grid, set_small_4[dev & 63], stream, 1);
+                                                h, rec, layer_threads(kLayerVerifyCodec4), kLayerSmem, grid, set_small_4[dev & 63], stream, 1);
         return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec4>,
-                                            h, rec, kLayerThreads, kLayerSmem, grid, set_large_4[dev & 63], stream, 1);
+                                            h, rec, layer_threads(kLayerVerifyCodec4), kLayerSmem, grid, set_large_4[dev & 63], stream, 1);
     }
     if (small)
         return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyRaw>, h, rec,
-                                            kLayerThreads, kLayerSmem, grid, set_small[dev & 63], stream, 1);
+                                            layer_threads(kLayerVerifyRaw), kLayerSmem, grid, set_small[dev & 63], stream, 1);
     return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyRaw>, h, rec,
-                                        kLayerThreads, kLayerSmem, grid, set_large[dev & 63], stream, 1);
+                                        layer_threads(kLayerVerifyRaw), kLayerSmem, grid, set_large[dev & 63], stream, 1);
 }
 
 int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
 {
     if (h.n == 0) return cudaSuccess;
-    if (h.n > static_cast<uint32_t>(kLayerCapLarge) || h.aad == nullptr) return cudaErrorInvalidValue;
+    if (h.n > static_cast<uint32_t>(kLayerCapLarge) || h.aad == nullptr || h.join_pow == nullptr ||
+        h.seg_steps < 1 || h.seg_steps > static_cast<uint32_t>(kMaxWarpSegSteps))
+        return cudaErrorInvalidValue;
     const uint32_t items = h.nseg * h.n;
     static bool set_small[64], set_large[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    const uint32_t grid = (items + kLayerWarps - 1) / kLayerWarps;
+    const uint32_t warps = layer_threads(kLayerEncrypt) / 32;
+    const uint32_t grid = (items + warps - 1) / warps;
     if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
         return layer_launch<kLayerCapSmall>(kKernLayerEncrypt, gcm_layer_verify_kernel<kLayerCapSmall, kLayerEncrypt>, h, rec,
-                                            kLayerThreads, kLayerSmem, grid, set_small[dev & 63], stream, 1);
+                                            layer_threads(kLayerEncrypt), kLayerSmem, grid, set_small[dev & 63], stream, 1);
     return layer_launch<kLayerCapLarge>(kKernLayerEncrypt, gcm_layer_verify_kernel<kLayerCapLarge, kLayerEncrypt>, h, rec,
-                                        kLayerThreads, kLayerSmem, grid, set_large[dev & 63], stream, 1);
+                                        layer_threads(kLayerEncrypt), kLayerSmem, grid, set_large[dev & 63], stream, 1);
 }
 
 int launch_segments(const SegmentLaunch& args, bool inline_aes, cudaStream_t stream)

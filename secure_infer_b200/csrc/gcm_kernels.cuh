@@ -125,6 +125,7 @@ struct LayerHeader {
     CodecParams codec;      // bits 0: raw payload; 8/4: codec packets dequantised into bf16 blocks
     uint32_t v_first;       // codec: records r >= v_first decode as V packets, the rest as K
     const uint8_t* aad;     // encrypt: AAD of record r at aad + 64 r (records are the output)
+    const uint4* join_pow;  // H^(32 seg_steps 2^b) nibble tables, b = 1..5 (join_tables_for)
 };
 
 template <int kCap>
@@ -138,7 +139,7 @@ constexpr int kLayerCapLarge = 1024;
 
 inline uint64_t layer_ks_stride(uint64_t count) { return ((count + 15) & ~uint64_t(15)) + 16; }
 // Segment length (seg_steps) and count (nseg) per record for a launch of n records.
-void layer_segments_for(uint64_t count, uint32_t n, uint32_t* seg_steps, uint32_t* nseg);
+void layer_segments_for(uint64_t count, uint32_t n, uint32_t codec_bits, uint32_t* seg_steps, uint32_t* nseg);
 
 // Keystream (+ tag masks) and fused verify/XOR/scatter for up to
 // kLayerCapLarge records; rec points at n LayerRec entries.  The encrypt
@@ -162,6 +163,16 @@ const char* kernel_kind_name(uint32_t kind);
 // Host-side launchers (gcm_kernels.cu).  Return a cudaError_t value.
 // key may be null (GHASH-only requests); h null -> H = E_K(0^128) on device.
 int launch_schedule(GcmSchedule* sched, const void* key, const void* h, bool need_tables, cudaStream_t stream);
+
+// Segment join tables of the layer kernels for a session schedule: 64 segment
+// lengths x 5 powers x 8 KiB (join_tables_bytes()).  LayerHeader::join_pow for
+// a launch with seg_steps s is join_tables_for(tables, s).
+constexpr size_t join_tables_bytes() { return 64u * 5u * 512u * 16u; }
+inline const uint4* join_tables_for(const void* tables, uint32_t seg_steps)
+{
+    return static_cast<const uint4*>(tables) + (seg_steps - 1u) * 5u * 512u;
+}
+int launch_join_tables(const GcmSchedule* sched, void* out, cudaStream_t stream);
 int launch_ctr(const CtrLaunch& args, cudaStream_t stream);
 int launch_ctr_uniform(const CtrLaunch& args, uint64_t uniform_blocks, cudaStream_t stream);
 int launch_auth_gate(uint8_t* data, const uint32_t* status, uint64_t bytes, cudaStream_t stream);

@@ -400,6 +400,7 @@ struct Session {
     uint8_t key[16] = {};
     uint8_t salt[4] = {};
     GcmSchedule* sched = nullptr;
+    void* join_tabs = nullptr;        // segment join tables of the layer kernels
     cudaStream_t producer = nullptr;
     cudaStream_t copier = nullptr;    // staged H2D record copies
     // Cross-stream fences of reload_records when the keystream is produced on
@@ -662,7 +663,7 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
         for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
             const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
             uint32_t seg_steps = 0, nseg = 0;
-            layer_segments_for(count, m, &seg_steps, &nseg);
+            layer_segments_for(count, m, cp.bits, &seg_steps, &nseg);
             LaunchSlot& slot = g_s.launch[g_s.launch_next];
             g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
             if (!ensure_launch_slot(slot, m, nseg * m)) return -1;
@@ -680,6 +681,7 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
             h.n = m;
             h.nseg = nseg;
             h.seg_steps = seg_steps;
+            h.join_pow = sib::join_tables_for(g_s.join_tabs, seg_steps);
             h.codec = cp;
             // Records of this chunk from index v_first on are V packets.
             const uint32_t v_global = cp.kind == SECURE_INFER_KIND_KV ? n / 2 : (cp.kind == 1 ? 0u : n);
@@ -999,7 +1001,7 @@ int writeback_device_locked(const void* const* srcs, void* const* host_dsts, uin
     for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
         const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
         uint32_t seg_steps = 0, nseg = 0;
-        layer_segments_for(count, m, &seg_steps, &nseg);
+        layer_segments_for(count, m, 0, &seg_steps, &nseg);
         LaunchSlot& ls = g_s.launch[g_s.launch_next];
         g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
         if (!ensure_launch_slot(ls, m, nseg * m)) return -1;
@@ -1017,6 +1019,7 @@ int writeback_device_locked(const void* const* srcs, void* const* host_dsts, uin
         h.n = m;
         h.nseg = nseg;
         h.seg_steps = seg_steps;
+        h.join_pow = sib::join_tables_for(g_s.join_tabs, seg_steps);
         h.aad = slot.dev_aad + 64ull * first;
         h.unaligned = unaligned ? 1u : 0u;
         for (uint32_t i = 0; i < m; ++i) {
@@ -1176,6 +1179,8 @@ void shutdown_locked()
     g_s.wb.clear();
     cudaFree(g_s.sched);
     g_s.sched = nullptr;
+    cudaFree(g_s.join_tabs);
+    g_s.join_tabs = nullptr;
     if (g_s.producer) cudaStreamDestroy(g_s.producer);
     g_s.producer = nullptr;
     if (g_s.copier) cudaStreamDestroy(g_s.copier);
@@ -1283,7 +1288,8 @@ int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt
     if (!CUDA_OK(cudaSetDevice(device))) return -1;
     uint8_t* dkey = nullptr;
     if (!CUDA_OK(cudaMalloc(&g_s.sched, sib::schedule_bytes())) ||
-        !CUDA_OK(cudaMemset(g_s.sched, 0, sib::schedule_bytes())) || !CUDA_OK(cudaMalloc(&dkey, 16)) ||
+        !CUDA_OK(cudaMemset(g_s.sched, 0, sib::schedule_bytes())) ||
+        !CUDA_OK(cudaMalloc(&g_s.join_tabs, sib::join_tables_bytes())) || !CUDA_OK(cudaMalloc(&dkey, 16)) ||
         !CUDA_OK(device_key ? cudaMemcpy(dkey, device_key, 16, cudaMemcpyDeviceToDevice)
                             : cudaMemcpy(dkey, key16, 16, cudaMemcpyHostToDevice)) ||
         !CUDA_OK(cudaStreamCreateWithFlags(&g_s.producer, cudaStreamNonBlocking)) ||
@@ -1297,6 +1303,7 @@ int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt
     // copy used for the derivation is wiped and freed right after.
     const bool ok = launch_schedule(g_s.sched, dkey, nullptr, true, g_s.producer) == cudaSuccess &&
                     CUDA_OK(cudaMemsetAsync(dkey, 0, 16, g_s.producer)) &&
+                    sib::launch_join_tables(g_s.sched, g_s.join_tabs, g_s.producer) == cudaSuccess &&
                     CUDA_OK(cudaStreamSynchronize(g_s.producer));
     cudaFree(dkey);
     if (!ok) return -1;

@@ -275,7 +275,8 @@ def test_reload_records_device_resident(nl):
         assert torch.equal(dest.cpu()[order], host)
 
 
-@pytest.mark.parametrize("count,n,dst_offset", [(1000, 7, 4), (48, 1500, 0), (16, 3, 2), (4097, 33, 0)])
+@pytest.mark.parametrize("count,n,dst_offset", [(1000, 7, 4), (48, 1500, 0), (16, 3, 2), (4097, 33, 0),
+                                                 (1 << 20, 1, 0), (300000, 2, 0), (262144, 3, 0)])
 def test_reload_records_odd_sizes_and_chunks(nl, count, n, dst_offset):
     """Device-resident reload of raw records whose size is not a multiple of
     16, into unaligned destinations, and more records than one launch holds
