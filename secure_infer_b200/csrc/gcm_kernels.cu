@@ -129,6 +129,13 @@ __device__ __forceinline__ void mbar_init_expect(uint64_t* bar, uint32_t tx_byte
                  : "memory");
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, bytes a multiple of
+// 16): no completion to wait for, no registers or shared memory held.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -647,7 +654,7 @@ __host__ __device__ constexpr uint32_t layer_threads(int mode)
 // byte32 (64 KiB), lane8 (64 KiB), H^8/16/24 (24 KiB), the segment join
 // tables H^(32 S 2^b) for b = 0..4 (40 KiB).
 constexpr size_t kLayerSmem = 2 * kGhashSmem + 8 * 512 * sizeof(uint4);
-constexpr int kLayerPrefetch = 4;
+constexpr int kLayerPrefetch = 2;
 
 // Decrypted fp32 parameters (scale or low) of a codec packet: N consecutive
 // words at byte `off`, each C ^ KS (16-byte aligned).
@@ -742,10 +749,14 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
     const GcmSchedule* __restrict__ S = L.h.sched;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u, quarter = lane >> 3;
     const uint32_t seg_steps = L.h.seg_steps;
-    __shared__ __align__(8) uint64_t tables_bar;
+    __shared__ __align__(8) uint64_t tables_bar, gtab_bar;
     // Tables used only after a warp's main loop (lane, quarter and join
     // tables, 128 KiB) stream in by bulk copy while the main loop runs.
     if (tid == 0) {
+        // The Horner multiplier H^32 as byte tables (64 KiB), needed from the
+        // first step on; waited for after each warp has issued its first loads.
+        mbar_init_expect(&gtab_bar, 65536u);
+        bulk_g2s(gtab, S->byte32, 65536u, &gtab_bar);
         mbar_init_expect(&tables_bar, 65536u + 8u * 8192u);
         bulk_g2s(ltab, S->lane8, 65536u, &tables_bar);
         bulk_g2s(qtab, S->tab[tab_pow_small(8)], 8192u, &tables_bar);
@@ -754,15 +765,13 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
         bulk_g2s(jtab, S->tab[tab_pow_32k(seg_steps)], 8192u, &tables_bar);
         bulk_g2s(jtab + 512, L.h.join_pow, 4u * 8192u, &tables_bar);
     }
-    // The Horner multiplier H^32 as byte tables (64 KiB).
     constexpr uint32_t kLayerThreads = layer_threads(kMode), kLayerWarps = kLayerThreads / 32;
-    for (uint32_t e = tid; e < 4096; e += kLayerThreads) gtab[e] = __ldg(&S->byte32[e]);
     __syncthreads();
     // Records, keystream and destinations are touched only after the
     // previous grid (the keystream kernel) has completed.
     allow_dependent_launch();
     grid_dependency_wait();
-    bool tables_ready = false;
+    bool tables_ready = false, gtab_ready = false;
 
     const uint64_t count = L.h.count;
     const bool aligned = L.h.unaligned == 0;
@@ -863,6 +872,7 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
         if constexpr (kCodec) {
 #pragma unroll
             for (int u = 0; u < kLayerPrefetch; ++u) load(u, xq[u], kq[u]);
+            if (!gtab_ready) gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
 #pragma unroll 1
             for (int j0 = 0; j0 < J; j0 += kLayerPrefetch) {
 #pragma unroll
@@ -879,11 +889,13 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
             // block, partial last block).  Interior segments are all interior.
             const int lo = j_lo < J ? j_lo : J;
             const int hi = j_hi > lo ? j_hi : lo;
-#pragma unroll 1
-            for (int j = 0; j < lo; ++j) {
-                uint4 x0, k0;
-                load(j, x0, k0);
-                consume(j, x0, k0);
+            // The warp's interior is one contiguous range of the input and of
+            // the keystream: stream both into L2 ahead of the loads below.
+            if (lane == 0 && hi > lo) {
+                const uint64_t off = static_cast<uint64_t>((base - a_blk) * 16 + 512ll * lo);
+                const uint32_t bytes = static_cast<uint32_t>(hi - lo) * 512u;
+                l2_prefetch_bulk(in + off, bytes);
+                l2_prefetch_bulk(ksp + off, bytes);
             }
 #pragma unroll
             for (int u = 0; u < kLayerPrefetch; ++u) {
@@ -892,6 +904,13 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
                     xq[u] = ldg16(in + off);
                     kq[u] = ldg16(ksp + off);
                 }
+            }
+            if (!gtab_ready) gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
+#pragma unroll 1
+            for (int j = 0; j < lo; ++j) {
+                uint4 x0, k0;
+                load(j, x0, k0);
+                consume(j, x0, k0);
             }
 #pragma unroll 1
             for (int j0 = lo; j0 < hi; j0 += kLayerPrefetch) {
@@ -921,7 +940,7 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
         // completes the partial is poisoned, so the record fails closed
         // (status 0, output zeroed) instead of waiting forever.
         if (!tables_ready) tables_ready = mbar_wait_bounded(&tables_bar, 0);
-        if (!tables_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
+        if (!tables_ready || !gtab_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
         Y = gf_mul_table<8, false>(Y, ltab, rep);                       // * H^(8 - r)
         Y = xor4(Y, shfl_xor4(Y, 1));
         Y = xor4(Y, shfl_xor4(Y, 2));
