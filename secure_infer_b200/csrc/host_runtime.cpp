@@ -420,6 +420,16 @@ struct Session {
     size_t launch_next = 0;
     std::vector<StageSlot> h2d;       // ring
     size_t h2d_next = 0;
+    // Host side of the staged H2D path: chunks of records are encrypted into
+    // a small ring of cached pinned buffers and each chunk is copied as soon
+    // as it is complete (see encrypt_ring_locked).
+    struct RingChunk {
+        uint8_t* host = nullptr;
+        uint64_t cap = 0;
+        cudaEvent_t ev = nullptr;     // recorded after the chunk's copy
+    };
+    std::vector<RingChunk> ring;
+    uint32_t ring_next = 0;
     std::vector<StageSlot> d2h;       // ring
     size_t d2h_next = 0;
     std::vector<StageSlot> wb;        // ring: scratch of device-resident writebacks
@@ -506,6 +516,41 @@ void free_stage(StageSlot& s)
 // H2D staging records are only written by the host and read by the copy
 // engine: write-combined pinned memory avoids the read-for-ownership of every
 // line the encryption writes (SECURE_INFER_WC_STAGING=0 turns it off).
+// H2D record staging: by default a whole layer is encrypted into one staging
+// buffer and copied once.  SECURE_INFER_H2D_RING=1 sends records through the
+// chunk ring instead: SECURE_INFER_H2D_RING_SLOTS buffers (default 8) of about
+// SECURE_INFER_H2D_RING_CHUNK bytes (default 8 MiB), which bounds pinned
+// staging memory independently of the layer size.  On a 16-core host the two
+// reach the same end-to-end rate with 8 MiB chunks; smaller chunks are slower.
+bool h2d_ring()
+{
+    static const bool on = [] {
+        const char* v = std::getenv("SECURE_INFER_H2D_RING");
+        return v != nullptr && std::atoi(v) != 0;
+    }();
+    return on;
+}
+
+uint32_t ring_slots()
+{
+    static const uint32_t n = [] {
+        const char* v = std::getenv("SECURE_INFER_H2D_RING_SLOTS");
+        const long x = v ? std::atol(v) : 8;
+        return static_cast<uint32_t>(std::min<long>(std::max<long>(x, 2), 64));
+    }();
+    return n;
+}
+
+uint64_t ring_chunk_bytes()
+{
+    static const uint64_t n = [] {
+        const char* v = std::getenv("SECURE_INFER_H2D_RING_CHUNK");
+        const long long x = v ? std::atoll(v) : (8ll << 20);
+        return static_cast<uint64_t>(std::min<long long>(std::max<long long>(x, 64ll << 10), 256ll << 20));
+    }();
+    return n;
+}
+
 bool wc_staging()
 {
     static const bool on = [] {
@@ -781,6 +826,93 @@ void maybe_tamper_h2d(uint8_t* rec, uint64_t count)
     }
 }
 
+// Encrypts n records (tickets given) into the chunk ring and copies every
+// chunk to dev (record i at dev + i * stride) on the copy stream as soon as
+// its last record is encrypted, so the copy engine reads freshly written
+// lines and the ring's few megabytes are reused instead of a whole layer of
+// staging.  Records are taken in increasing order by the pool; a worker that
+// needs a ring buffer first waits until the chunk that used it R chunks
+// earlier has been copied.  Every record of that chunk was taken before, so
+// the wait always ends.  Caller holds g_mu.
+bool encrypt_ring_locked(const uint64_t* tickets, const void* const* srcs, uint32_t n, uint64_t count, uint64_t stride,
+                         uint8_t* dev)
+{
+    const uint32_t R = ring_slots();
+    const uint64_t per = std::max<uint64_t>(1, ring_chunk_bytes() / stride);
+    const uint32_t C = static_cast<uint32_t>(std::min<uint64_t>(per, n));
+    const uint32_t chunks = (n + C - 1) / C;
+    if (g_s.ring.size() != R) g_s.ring.resize(R);
+    for (auto& rc : g_s.ring) {
+        if (!rc.ev && !CUDA_OK(cudaEventCreateWithFlags(&rc.ev, cudaEventDisableTiming))) return false;
+        if (rc.cap < C * stride) {
+            cudaEventSynchronize(rc.ev);
+            if (rc.host) cudaFreeHost(rc.host);
+            rc.host = nullptr;
+            rc.cap = 0;
+            if (!CUDA_OK(cudaHostAlloc(&rc.host, C * stride,
+                                       wc_staging() ? cudaHostAllocWriteCombined : cudaHostAllocDefault)))
+                return false;
+            rc.cap = C * stride;
+        }
+    }
+    const uint32_t base = g_s.ring_next;
+    std::unique_ptr<std::atomic<uint32_t>[]> left(new std::atomic<uint32_t>[chunks]);
+    std::unique_ptr<std::atomic<bool>[]> issued(new std::atomic<bool>[chunks]);
+    // Per chunk: 0 = buffer not yet claimed, 1 = one worker is waiting for
+    // the buffer's previous copy, 2 = buffer free.  One driver wait per
+    // chunk: concurrent event waits from every worker serialise in the driver.
+    std::unique_ptr<std::atomic<int>[]> state(new std::atomic<int>[chunks]);
+    for (uint32_t k = 0; k < chunks; ++k) {
+        left[k] = std::min<uint32_t>(C, n - k * C);
+        issued[k] = false;
+        state[k] = 0;
+    }
+    std::mutex mu;
+    std::condition_variable cv;
+    std::atomic<bool> ok{true};
+    const uint8_t* key = g_s.key;
+    pool().parallel_for(n, [&](size_t i) {
+        const uint32_t k = static_cast<uint32_t>(i / C);
+        Session::RingChunk& rc = g_s.ring[(base + k) % R];
+        int expect = 0;
+        if (state[k].compare_exchange_strong(expect, 1)) {
+            if (k >= R) {
+                std::unique_lock<std::mutex> lock(mu);
+                cv.wait(lock, [&] { return issued[k - R].load(); });
+            }
+            cudaEventSynchronize(rc.ev);
+            {
+                std::lock_guard<std::mutex> lock(mu);
+                state[k] = 2;
+            }
+            cv.notify_all();
+        } else if (state[k].load() != 2) {
+            std::unique_lock<std::mutex> lock(mu);
+            cv.wait(lock, [&] { return state[k].load() == 2; });
+        }
+        uint8_t* rec = rc.host + (i - static_cast<size_t>(k) * C) * stride;
+        uint8_t iv[16], aad[64];
+        iv_for(tickets[i], iv);
+        build_aad(srcs[i], count, SECURE_INFER_DIRECTION_H2D, tickets[i], 0, 0, aad);
+        if (!encrypt_record(key, iv, aad, static_cast<const uint8_t*>(srcs[i]), count, rec)) ok = false;
+        maybe_tamper_h2d(rec, count);
+        if (left[k].fetch_sub(1) == 1) {
+            const uint32_t first = k * C, cnt = std::min<uint32_t>(C, n - first);
+            if (!CUDA_OK(cudaMemcpyAsync(dev + first * stride, rc.host, cnt * stride, cudaMemcpyHostToDevice,
+                                         g_s.copier)) ||
+                !CUDA_OK(cudaEventRecord(rc.ev, g_s.copier)))
+                ok = false;
+            {
+                std::lock_guard<std::mutex> lock(mu);
+                issued[k] = true;
+            }
+            cv.notify_all();
+        }
+    });
+    g_s.ring_next = (base + chunks) % R;
+    return ok;
+}
+
 // Encrypt + stage + device reload.  Returns the batch (not yet registered).
 std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* const* srcs, void* const* dsts, uint32_t n,
                                                 uint64_t count, const secure_infer_codec* codec, bool encrypted,
@@ -816,7 +948,10 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     if (keystream_records_locked(tickets.data(), n, count, slot.ks, g_s.producer) != 0 ||
         !CUDA_OK(cudaEventRecord(slot.ks_ready, g_s.producer)))
         return nullptr;
-    if (!encrypted) {
+    const bool ring = !encrypted && h2d_ring();
+    if (ring) {
+        if (!encrypt_ring_locked(tickets.data(), srcs, n, count, stride, slot.dev)) return nullptr;
+    } else if (!encrypted) {
         std::atomic<bool> ok{true};
         const uint8_t* key = g_s.key;
         pool().parallel_for(n, [&](size_t i) {
@@ -847,7 +982,7 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     // does not queue behind this layer's kernel; the caller's stream waits
     // for the records and the keystream, then runs the fused kernel.
     const void* host_src = encrypted ? srcs[0] : slot.host;
-    if (!CUDA_OK(cudaMemcpyAsync(slot.dev, host_src, stride * n, cudaMemcpyHostToDevice, g_s.copier)) ||
+    if ((!ring && !CUDA_OK(cudaMemcpyAsync(slot.dev, host_src, stride * n, cudaMemcpyHostToDevice, g_s.copier))) ||
         !CUDA_OK(cudaEventRecord(slot.copied, g_s.copier)) ||
         !CUDA_OK(cudaStreamWaitEvent(stream, slot.copied, 0)) ||
         !CUDA_OK(cudaStreamWaitEvent(stream, slot.ks_ready, 0)))
@@ -1175,6 +1310,13 @@ void shutdown_locked()
     }
     g_s.launch.clear();
     g_s.h2d.clear();
+    for (auto& rc : g_s.ring) {
+        if (rc.ev) cudaEventSynchronize(rc.ev);
+        if (rc.host) cudaFreeHost(rc.host);
+        if (rc.ev) cudaEventDestroy(rc.ev);
+    }
+    g_s.ring.clear();
+    g_s.ring_next = 0;
     g_s.d2h.clear();
     g_s.wb.clear();
     cudaFree(g_s.sched);
