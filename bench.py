@@ -64,18 +64,19 @@ CONFIGS = {
 NCU_TRAFFIC_BYTES = {
     # one c2 layer (96 records x 256 KiB): ciphertext + keystream read; most of
     # the bf16 output is still in L2 when the kernel ends
-    ("c2", "gcm_layer_verify_kernel"): 50_554_880 + 2_394_624,
+    ("c2", "gcm_layer_verify_kernel"): 50_825_728 + 1_944_320,
     # one c5 layer (128 records x 10256 B, K+V in one launch)
     ("c5", "gcm_layer_verify_kernel"): 2_836_224,
     # one c4 layer (128 blocks of 8 heads): bf16 read; packets stay in L2
     ("c4", "kv_encode_kernel"): 33_612_800 + 768,
-    ("c4", "gcm_layer_encrypt"): 21_165_568,
+    ("c4", "gcm_layer_encrypt"): 21_253_120,
 }
 
 # Shared-memory wavefronts per 16-byte block that the algorithm needs (the
-# binding pipe): GHASH = 32 LDS.128 per lane per block = 4 wavefronts;
-# AES-128 = 160 T-table LDS.32 + 16 final-round = 176 per 32 blocks = 5.5.
-SMEM_WAVEFRONTS_PER_BLOCK = {"gcm_layer_verify_kernel": 4.0, "gcm_layer_ctr_kernel": 5.5}
+# binding pipe): GHASH with byte tables = 16 conflict-free LDS.128 per lane per
+# block = 2 wavefronts; AES-128 = 160 T-table LDS.32 + 16 final-round = 176 per
+# 32 blocks = 5.5.
+SMEM_WAVEFRONTS_PER_BLOCK = {"gcm_layer_verify_kernel": 2.0, "gcm_layer_ctr_kernel": 5.5}
 
 
 def layer_bits(mode, layer, layers):
@@ -492,8 +493,8 @@ def run_gpu(args, cfg):
                          "smem_pipe_frac": smem,
                          "note": "achieved = per-layer algorithmic bytes (ciphertext in + bf16 out) / dominant "
                                  "kernel time; peak = measured HBM copy bandwidth (of measured). The binding "
-                                 "resource is the shared-memory pipe (AES T-tables, GHASH nibble tables): "
-                                 "smem_pipe_frac = algorithmic wavefronts (GHASH 4, AES 5.5 per 16-byte block) / "
+                                 "resource is the shared-memory pipe (AES T-tables, GHASH byte tables): "
+                                 "smem_pipe_frac = algorithmic wavefronts (GHASH 2, AES 5.5 per 16-byte block) / "
                                  "(kernel time x SMs x sampled SM clock), 1 wavefront per SM per clock peak."},
             "clocks": clocks.summary(),
         }
