@@ -230,15 +230,34 @@ const char* secure_infer_kernel_name(uint32_t kind);
 
 /* ------------------------------------------------- prediction scope */
 
-/* secure_infer.cpp:1102-1146.  Keystreams here are derived from tickets at
- * submission time, so there are no speculative reservations to drop; these
- * bump the generation counter reported by the stats. */
+/* Announce a future secure_infer_h2d_reload_layer(layer, srcs, ..., n, count,
+ * codec, 0, ...) so its records are encrypted ahead of time: the host side of
+ * the reference's CPU ciphertext pool (secure_infer.cpp:3264-3710, scheduled
+ * by its history predictor through secure_infer_gcm_schedule_cpu_ciphertext,
+ * :3526-3597).  Tickets, IVs and AADs are fixed now; a background thread
+ * encrypts the records on the worker pool into a pinned buffer of a bounded
+ * pool (SECURE_INFER_PREPARE_POOL_BYTES, default 256 MiB; ready entries are
+ * evicted oldest first).  A later reload call with the same layer, source
+ * pointers (in the same order), count and codec takes the entry, waiting for
+ * it if it is still being encrypted, and copies it instead of encrypting;
+ * any other reload encrypts inline as before.  The sources must not change
+ * between the two calls.  Returns 0 when scheduled, 1 when not (the same
+ * announcement is pending, or the pool is full), -1 on bad arguments or no
+ * session. */
+int secure_infer_h2d_prepare_layer(uint32_t layer, const void* const* srcs, uint32_t n, uint64_t count,
+                                   const secure_infer_codec* codec);
+
+/* secure_infer.cpp:1102-1146: end the current prediction scope.  Entries
+ * announced before the call are dropped (one being encrypted is dropped when
+ * it finishes); their tickets are never used. */
 void secure_infer_invalidate_transfer_prefetches(void);
 void secure_infer_retire_transfer_prefetches(void);
 
 /* ------------------------------------------------------------ stats */
 
-/* secure_infer.cpp:821-835 */
+/* secure_infer.cpp:821-835: records reloaded from announced entries, reloads
+ * that had to wait for their entry, reloads that found announced entries
+ * outstanding but none matching. */
 void secure_infer_get_transfer_prefetch_stats(uint64_t* ready, uint64_t* busy_fallback, uint64_t* missing_fallback);
 /* secure_infer.cpp:5038-5053: scheduled, ready, hit, miss, retired, stale, failed */
 void secure_infer_get_gcm_keystream_stats(uint64_t* scheduled, uint64_t* ready, uint64_t* hit, uint64_t* miss,

@@ -57,6 +57,7 @@ HOST_SIGNATURES: dict[str, tuple[list, object]] = {
     "secure_infer_keystream_records": ([U64P, U32, U64, P, P], I32),
     "secure_infer_verify_records": ([U32, P, U64, U64, U32, U64P, PP, P, P, P, P], I32),
     "secure_infer_h2d_reload_layer": ([U32, PP, PP, U32, U64, P, I32, U64P, P], I32),
+    "secure_infer_h2d_prepare_layer": ([U32, PP, U32, U64, P], I32),
     "secure_infer_layer_ready_wait": ([U32, P], I32),
     "secure_infer_h2d_layer_group_begin": ([SZ], I32),
     "secure_infer_h2d_layer_group_end": ([], I32),

@@ -355,6 +355,7 @@ struct StageSlot {
     cudaEvent_t done = nullptr;
     cudaEvent_t ks_ready = nullptr, copied = nullptr;   // staged reload: keystream / records landed
     std::shared_ptr<LayerBatch> owner;
+    std::shared_ptr<struct Prepared> hold;   // pre-encrypted records the slot's copy reads
 };
 
 struct RetryInfo {
@@ -466,6 +467,10 @@ Session g_s;
 
 std::atomic<uint64_t> g_verified{0}, g_rejected{0}, g_retried{0};
 std::atomic<uint64_t> g_ks_scheduled{0}, g_ks_hit{0}, g_ks_launches{0}, g_generation{0};
+// Pre-encryption lookahead (secure_infer_h2d_prepare_layer): records taken
+// from a ready entry, reloads that waited for their entry, and reloads that
+// found prepared entries outstanding but none of them matching.
+std::atomic<uint64_t> g_prep_ready{0}, g_prep_busy{0}, g_prep_missing{0};
 std::atomic<uint64_t> g_tamper_h2d_nth{0}, g_tamper_d2h_nth{0};
 std::atomic<uint32_t> g_tamper_h2d_target{0};
 
@@ -913,6 +918,195 @@ bool encrypt_ring_locked(const uint64_t* tickets, const void* const* srcs, uint3
     return ok;
 }
 
+// ------------------------------------------------------------ lookahead
+// Host pre-encryption of a reload the caller announces ahead of time (the
+// reference's CPU ciphertext pool, secure_infer.cpp:3264-3710, fed by its
+// history predictor; here the caller names the transfer).  Tickets, IVs and
+// AADs are fixed when the reload is announced; a background thread encrypts
+// the records on the worker pool into a pinned buffer of the prepared pool;
+// the matching reload copies that buffer instead of encrypting.
+struct Prepared {
+    uint32_t layer = 0;
+    std::vector<const void*> srcs;
+    uint64_t count = 0, stride = 0, generation = 0;
+    bool has_codec = false;
+    secure_infer_codec codec{};
+    std::vector<uint64_t> tickets;
+    std::vector<uint8_t> ivs, aads;   // [n][16], [n][64]
+    uint8_t key[16] = {};
+    uint8_t* host = nullptr;          // pinned [n][stride], from the prepared pool
+    uint64_t bytes = 0;
+    int state = 0;                    // 0 queued, 1 encrypting, 2 ready, 3 failed (guarded by g_prep.mu)
+};
+
+struct PrepPool {
+    std::mutex mu;
+    std::condition_variable cv;
+    std::deque<std::shared_ptr<Prepared>> queue;     // waiting for the encrypt thread
+    std::vector<std::shared_ptr<Prepared>> entries;  // announced, not yet taken by a reload
+    std::multimap<uint64_t, uint8_t*> free_bufs;      // pinned buffers by size
+    uint64_t held = 0;                                // bytes of all pinned buffers
+    std::thread worker;
+    bool stop = false;
+} g_prep;
+
+uint64_t prep_pool_cap()
+{
+    static const uint64_t cap = [] {
+        const char* v = std::getenv("SECURE_INFER_PREPARE_POOL_BYTES");
+        const long long x = v ? std::atoll(v) : (256ll << 20);
+        return static_cast<uint64_t>(std::max<long long>(x, 0));
+    }();
+    return cap;
+}
+
+// Caller holds g_prep.mu.
+void prep_release_locked(Prepared& e)
+{
+    if (e.host) g_prep.free_bufs.emplace(e.bytes, e.host);
+    e.host = nullptr;
+}
+
+// A pinned buffer of at least `bytes` from the pool, evicting ready entries
+// (oldest first) when the cap would be exceeded.  Caller holds g_prep.mu.
+uint8_t* prep_buffer_locked(uint64_t bytes, uint64_t* got)
+{
+    for (;;) {
+        auto it = g_prep.free_bufs.lower_bound(bytes);
+        if (it != g_prep.free_bufs.end()) {
+            uint8_t* p = it->second;
+            *got = it->first;
+            g_prep.free_bufs.erase(it);
+            return p;
+        }
+        if (g_prep.held + bytes <= prep_pool_cap()) {
+            uint8_t* p = nullptr;
+            if (!CUDA_OK(cudaHostAlloc(&p, bytes, wc_staging() ? cudaHostAllocWriteCombined : cudaHostAllocDefault)))
+                return nullptr;
+            g_prep.held += bytes;
+            *got = bytes;
+            return p;
+        }
+        if (!g_prep.free_bufs.empty()) {          // too small: give one back and retry
+            auto f = g_prep.free_bufs.begin();
+            cudaFreeHost(f->second);
+            g_prep.held -= f->first;
+            g_prep.free_bufs.erase(f);
+            continue;
+        }
+        auto victim = std::find_if(g_prep.entries.begin(), g_prep.entries.end(),
+                                   [](const std::shared_ptr<Prepared>& e) { return e->state >= 2; });
+        if (victim == g_prep.entries.end()) return nullptr;
+        prep_release_locked(**victim);
+        g_prep.entries.erase(victim);
+    }
+}
+
+void prep_worker()
+{
+    for (;;) {
+        std::shared_ptr<Prepared> e;
+        {
+            std::unique_lock<std::mutex> lock(g_prep.mu);
+            g_prep.cv.wait(lock, [] { return g_prep.stop || !g_prep.queue.empty(); });
+            if (g_prep.stop) return;
+            e = g_prep.queue.front();
+            g_prep.queue.pop_front();
+            if (e->generation != g_generation.load() || e->host == nullptr) {
+                e->state = 3;
+                g_prep.cv.notify_all();
+                continue;
+            }
+            e->state = 1;
+        }
+        std::atomic<bool> ok{true};
+        const uint32_t n = static_cast<uint32_t>(e->srcs.size());
+        pool().parallel_for(n, [&](size_t i) {
+            if (!encrypt_record(e->key, &e->ivs[16 * i], &e->aads[64 * i], static_cast<const uint8_t*>(e->srcs[i]),
+                                e->count, e->host + i * e->stride))
+                ok = false;
+        });
+        {
+            std::lock_guard<std::mutex> lock(g_prep.mu);
+            e->state = ok ? 2 : 3;
+        }
+        g_prep.cv.notify_all();
+    }
+}
+
+bool same_codec(const Prepared& e, const secure_infer_codec* codec)
+{
+    if (!codec) return !e.has_codec;
+    return e.has_codec && std::memcmp(&e.codec, codec, sizeof(secure_infer_codec)) == 0;
+}
+
+// The announced entry for this reload, removed from the pool and complete
+// (ready or failed), or null.  Caller holds g_mu.
+std::shared_ptr<Prepared> take_prepared(uint32_t layer, const void* const* srcs, uint32_t n, uint64_t count,
+                                        const secure_infer_codec* codec)
+{
+    std::unique_lock<std::mutex> lock(g_prep.mu);
+    if (g_prep.entries.empty()) return nullptr;
+    const uint64_t gen = g_generation.load();
+    auto it = std::find_if(g_prep.entries.begin(), g_prep.entries.end(), [&](const std::shared_ptr<Prepared>& e) {
+        return e->layer == layer && e->count == count && e->srcs.size() == n && e->generation == gen &&
+               same_codec(*e, codec) && std::equal(e->srcs.begin(), e->srcs.end(), srcs);
+    });
+    if (it == g_prep.entries.end()) {
+        ++g_prep_missing;
+        return nullptr;
+    }
+    std::shared_ptr<Prepared> e = *it;
+    g_prep.entries.erase(it);
+    if (e->state < 2) {
+        ++g_prep_busy;
+        g_prep.cv.wait(lock, [&] { return e->state >= 2; });
+    }
+    if (e->state != 2) {
+        prep_release_locked(*e);
+        return nullptr;
+    }
+    return e;
+}
+
+// Drops every entry that is not being encrypted right now (those are dropped
+// when taken or when the thread finds them stale).
+void prep_drop_stale()
+{
+    std::lock_guard<std::mutex> lock(g_prep.mu);
+    const uint64_t gen = g_generation.load();
+    for (auto it = g_prep.entries.begin(); it != g_prep.entries.end();) {
+        if ((*it)->generation != gen && (*it)->state != 1) {
+            if ((*it)->state == 0) (*it)->state = 3;
+            prep_release_locked(**it);
+            it = g_prep.entries.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    g_prep.cv.notify_all();
+}
+
+// Stops the encrypt thread (after its current entry) and frees the pool.
+void prep_shutdown()
+{
+    {
+        std::lock_guard<std::mutex> lock(g_prep.mu);
+        g_prep.stop = true;
+    }
+    g_prep.cv.notify_all();
+    if (g_prep.worker.joinable()) g_prep.worker.join();
+    std::lock_guard<std::mutex> lock(g_prep.mu);
+    for (auto& e : g_prep.entries) prep_release_locked(*e);
+    for (auto& e : g_prep.queue) prep_release_locked(*e);
+    g_prep.entries.clear();
+    g_prep.queue.clear();
+    for (auto& f : g_prep.free_bufs) cudaFreeHost(f.second);
+    g_prep.free_bufs.clear();
+    g_prep.held = 0;
+    g_prep.stop = false;
+}
+
 // Encrypt + stage + device reload.  Returns the batch (not yet registered).
 std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* const* srcs, void* const* dsts, uint32_t n,
                                                 uint64_t count, const secure_infer_codec* codec, bool encrypted,
@@ -929,9 +1123,20 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     if (slot.owner) harvest(*slot.owner);   // statuses leave the slot before reuse
     if (!ensure_stage(slot, stride * n, layer_ks_stride(count) * n, n, 0, true)) return nullptr;
     if (slot.done) cudaEventSynchronize(slot.done);
+    if (slot.hold) {                        // its copy has completed: the buffer goes back to the pool
+        std::lock_guard<std::mutex> lock(g_prep.mu);
+        prep_release_locked(*slot.hold);
+        slot.hold.reset();
+    }
+    // A pre-encrypted entry for exactly this reload replaces the inline
+    // encryption; its tickets were reserved when it was announced.
+    std::shared_ptr<Prepared> pre = encrypted ? nullptr : take_prepared(layer, srcs, n, count, codec);
 
     std::vector<uint64_t> tickets(n);
-    if (encrypted) {
+    if (pre) {
+        tickets = pre->tickets;
+        g_prep_ready += n;
+    } else if (encrypted) {
         if (given_tickets == nullptr) return nullptr;
         for (uint32_t i = 0; i < n; ++i)
             if (!reserve_given_ticket(given_tickets[i])) return nullptr;
@@ -948,8 +1153,10 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     if (keystream_records_locked(tickets.data(), n, count, slot.ks, g_s.producer) != 0 ||
         !CUDA_OK(cudaEventRecord(slot.ks_ready, g_s.producer)))
         return nullptr;
-    const bool ring = !encrypted && h2d_ring();
-    if (ring) {
+    const bool ring = !encrypted && !pre && h2d_ring();
+    if (pre) {
+        for (uint32_t i = 0; i < n; ++i) maybe_tamper_h2d(pre->host + i * stride, count);
+    } else if (ring) {
         if (!encrypt_ring_locked(tickets.data(), srcs, n, count, stride, slot.dev)) return nullptr;
     } else if (!encrypted) {
         std::atomic<bool> ok{true};
@@ -981,7 +1188,7 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     // Records cross the link on the copy stream, so the next layer's copy
     // does not queue behind this layer's kernel; the caller's stream waits
     // for the records and the keystream, then runs the fused kernel.
-    const void* host_src = encrypted ? srcs[0] : slot.host;
+    const void* host_src = encrypted ? srcs[0] : pre ? pre->host : slot.host;
     if ((!ring && !CUDA_OK(cudaMemcpyAsync(slot.dev, host_src, stride * n, cudaMemcpyHostToDevice, g_s.copier))) ||
         !CUDA_OK(cudaEventRecord(slot.copied, g_s.copier)) ||
         !CUDA_OK(cudaStreamWaitEvent(stream, slot.copied, 0)) ||
@@ -994,6 +1201,7 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     cudaEventRecord(batch->done, stream);
     slot.done = batch->done;
     slot.owner = batch;
+    slot.hold = pre;
     return batch;
 }
 
@@ -1268,6 +1476,7 @@ void shutdown_locked()
 {
     host_only_session = false;
     if (!g_s.ready) return;
+    prep_shutdown();
     cudaDeviceSynchronize();
     {
         std::lock_guard<std::mutex> dl(g_d2h_mu);
@@ -1597,6 +1806,61 @@ SI_EXPORT int secure_infer_h2d_reload_layer(uint32_t layer, const void* const* s
     return 0;
 }
 
+SI_EXPORT int secure_infer_h2d_prepare_layer(uint32_t layer, const void* const* srcs, uint32_t n, uint64_t count,
+                                             const secure_infer_codec* codec)
+{
+    if (srcs == nullptr || n == 0 || count == 0) return -1;
+    for (uint32_t i = 0; i < n; ++i)
+        if (srcs[i] == nullptr) return -1;
+    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    if (!g_s.ready) return -1;
+    sib::CodecParams cp;
+    uint64_t packet = 0;
+    if (!codec_geometry(codec, &cp, &packet, true)) return -1;
+    if (cp.bits && (count != packet || (cp.kind == SECURE_INFER_KIND_KV && (n & 1u)))) return -1;
+    auto e = std::make_shared<Prepared>();
+    e->layer = layer;
+    e->srcs.assign(srcs, srcs + n);
+    e->count = count;
+    e->stride = record_bytes(count);
+    e->generation = g_generation.load();
+    if (codec) {
+        e->has_codec = true;
+        e->codec = *codec;
+    }
+    {
+        std::lock_guard<std::mutex> pl(g_prep.mu);
+        for (const auto& x : g_prep.entries)   // the same announcement is already pending
+            if (x->layer == layer && x->count == count && x->generation == e->generation && x->srcs == e->srcs &&
+                same_codec(*x, codec))
+                return 1;
+        uint64_t got = 0;
+        e->host = prep_buffer_locked(e->stride * n, &got);
+        if (e->host == nullptr) return 1;
+        e->bytes = got;
+    }
+    std::memcpy(e->key, g_s.key, 16);
+    e->tickets.resize(n);
+    e->ivs.resize(16ull * n);
+    e->aads.resize(64ull * n);
+    reserve_tickets(n, e->tickets.data());
+    for (uint32_t i = 0; i < n; ++i) {
+        iv_for(e->tickets[i], &e->ivs[16ull * i]);
+        build_aad(srcs[i], count, SECURE_INFER_DIRECTION_H2D, e->tickets[i], 0, 0, &e->aads[64ull * i]);
+    }
+    {
+        std::lock_guard<std::mutex> pl(g_prep.mu);
+        if (!g_prep.worker.joinable()) {
+            g_prep.stop = false;
+            g_prep.worker = std::thread(prep_worker);
+        }
+        g_prep.entries.push_back(e);
+        g_prep.queue.push_back(e);
+    }
+    g_prep.cv.notify_all();
+    return 0;
+}
+
 SI_EXPORT int secure_infer_layer_ready_wait(uint32_t layer, void* stream)
 {
     std::lock_guard<std::recursive_mutex> lock(g_mu);
@@ -1795,15 +2059,24 @@ SI_EXPORT int secure_infer_writeback_records(const void* const* srcs, void* cons
     return CUDA_OK(cudaEventRecord(slot.done, s)) ? 0 : -1;
 }
 
-SI_EXPORT void secure_infer_invalidate_transfer_prefetches(void) { ++g_generation; }
-SI_EXPORT void secure_infer_retire_transfer_prefetches(void) { ++g_generation; }
+SI_EXPORT void secure_infer_invalidate_transfer_prefetches(void)
+{
+    ++g_generation;
+    prep_drop_stale();
+}
+
+SI_EXPORT void secure_infer_retire_transfer_prefetches(void)
+{
+    ++g_generation;
+    prep_drop_stale();
+}
 
 SI_EXPORT void secure_infer_get_transfer_prefetch_stats(uint64_t* ready, uint64_t* busy_fallback,
                                                         uint64_t* missing_fallback)
 {
-    if (ready) *ready = g_ks_hit.load();
-    if (busy_fallback) *busy_fallback = 0;
-    if (missing_fallback) *missing_fallback = 0;
+    if (ready) *ready = g_prep_ready.load();
+    if (busy_fallback) *busy_fallback = g_prep_busy.load();
+    if (missing_fallback) *missing_fallback = g_prep_missing.load();
 }
 
 SI_EXPORT void secure_infer_get_gcm_keystream_stats(uint64_t* scheduled, uint64_t* ready, uint64_t* hit,

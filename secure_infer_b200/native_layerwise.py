@@ -101,6 +101,14 @@ class Session:
         return auth_stats()
 
 
+def prefetch_stats() -> dict:
+    """Records reloaded from announced entries, reloads that waited for their
+    entry, reloads that found announced entries but none matching."""
+    r, b, m = ct.c_uint64(), ct.c_uint64(), ct.c_uint64()
+    _native.lib().secure_infer_get_transfer_prefetch_stats(ct.byref(r), ct.byref(b), ct.byref(m))
+    return dict(ready=r.value, busy=b.value, missing=m.value)
+
+
 def auth_stats() -> dict:
     """Records verified / rejected / retried since the session started."""
     v, r, t = ct.c_uint64(), ct.c_uint64(), ct.c_uint64()
@@ -138,15 +146,10 @@ class NativeTransfer:
         self.heads = heads
         self.layer = 0
 
-    def single_layer_kv_transfer(self, payload, destination, stream=None):
-        """K and V of the layer go out as one reload of 2n records (K records
-        first), so both kinds share one staged copy and one fused kernel."""
-        host, mapping = payload
-        layer = self.layer
+    def _sources(self, host, mapping, heads: int, layer: int):
+        """(source pointers, record bytes, codec) of one layer's reload: K
+        records first, then V, in mapping order."""
         src_idx = mapping[:, 0].tolist()
-        dst_idx = mapping[:, 1].tolist()
-        n = len(src_idx)
-        heads = destination[0].shape[2]
         if self.mode == "none":
             codec = None
             counts = {src[0].numel() * src.element_size() for src in host}
@@ -160,17 +163,42 @@ class NativeTransfer:
             for src in host:
                 if src.shape[1] != count:
                     raise ValueError(f"packet width {src.shape[1]} != {count}")
-        srcs, dsts = [], []
-        for src, dst in zip(host, destination):
+        srcs = []
+        for src in host:
             stride = src.stride(0) * src.element_size()
-            dstride = dst.stride(0) * dst.element_size()
             srcs += [src.data_ptr() + i * stride for i in src_idx]
+        return srcs, count, codec
+
+    def single_layer_kv_transfer(self, payload, destination, stream=None):
+        """K and V of the layer go out as one reload of 2n records (K records
+        first), so both kinds share one staged copy and one fused kernel."""
+        host, mapping = payload
+        layer = self.layer
+        srcs, count, codec = self._sources(host, mapping, destination[0].shape[2], layer)
+        dst_idx = mapping[:, 1].tolist()
+        dsts = []
+        for dst in destination:
+            dstride = dst.stride(0) * dst.element_size()
             dsts += [dst.data_ptr() + i * dstride for i in dst_idx]
-        rc = self.lib.secure_infer_h2d_reload_layer(layer, _ptrs(srcs), _ptrs(dsts), 2 * n, count,
+        rc = self.lib.secure_infer_h2d_reload_layer(layer, _ptrs(srcs), _ptrs(dsts), len(srcs), count,
                                                     ct.byref(codec) if codec else None, 0, None, _stream(stream))
         if rc != 0:
             raise RuntimeError(f"secure_infer_h2d_reload_layer failed for layer {layer}")
         self.layer += 1
+
+    def prepare_layer(self, payload, heads: int, layer: int | None = None) -> bool:
+        """Announce the reload of ``payload`` for ``layer`` (default: the next
+        layer this object transfers) so its records are encrypted ahead of
+        time (secure_infer_h2d_prepare_layer).  Returns whether it was
+        scheduled."""
+        host, mapping = payload
+        layer = self.layer if layer is None else layer
+        srcs, count, codec = self._sources(host, mapping, heads, layer)
+        rc = self.lib.secure_infer_h2d_prepare_layer(layer, _ptrs(srcs), len(srcs), count,
+                                                     ct.byref(codec) if codec else None)
+        if rc < 0:
+            raise RuntimeError(f"secure_infer_h2d_prepare_layer failed for layer {layer}")
+        return rc == 0
 
     def wait_for_layer_load(self, layer: int):
         if self.lib.secure_infer_recovery_wait_layer_authentication(layer) != 0:
