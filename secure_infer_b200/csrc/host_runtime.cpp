@@ -1908,6 +1908,10 @@ SI_EXPORT int secure_infer_recovery_wait_layer_authentication(uint32_t layer)
     }
     bool ok = true;
     for (auto& b : batches) {
+        // Wait for the batch without the session lock, so other threads keep
+        // submitting meanwhile (the batch owns its event; a slot reused in the
+        // meantime has harvested its owner under the lock first).
+        if (b->done) cudaEventSynchronize(b->done);
         std::lock_guard<std::recursive_mutex> lock(g_mu);
         harvest(*b);
         std::vector<const void*> srcs;
@@ -1956,6 +1960,8 @@ SI_EXPORT int secure_infer_recovery_wait_job_authentication(uint64_t job_id)
     }
     if (batches.empty()) return -1;
     bool valid = true;
+    for (auto& b : batches)
+        if (b->done) cudaEventSynchronize(b->done);
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     for (auto& b : batches) {
         harvest(*b);
