@@ -6,6 +6,7 @@ missing, ``lib()`` raises ``NativeLibraryMissing`` with the build command.
 from __future__ import annotations
 
 import ctypes as ct
+import os
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "_build" / "libsecure_infer.so"
@@ -102,14 +103,28 @@ KIND_KV = 2
 _lib: ct.CDLL | None = None
 
 
+def _preloaded() -> ct.CDLL | None:
+    """The process namespace, when libsecure_infer.so is already in it (for
+    example LD_PRELOADed, as the reference's run.sh:66 does): the symbols are
+    then bound through ``ctypes.CDLL(None)`` like the reference's Python side
+    (npu_predict.py:158-254).  SECURE_INFER_USE_PRELOADED=0 disables this."""
+    if os.environ.get("SECURE_INFER_USE_PRELOADED", "1") == "0":
+        return None
+    proc = ct.CDLL(None)
+    needed = ("secure_infer_session_init", "secure_infer_h2d_reload_layer", "secure_infer_aicpu_ghash_do")
+    return proc if all(hasattr(proc, name) for name in needed) else None
+
+
 def lib() -> ct.CDLL:
     """Load (once) and return the native library with typed entry points."""
     global _lib
     if _lib is None:
-        if not LIB_PATH.exists():
-            raise NativeLibraryMissing(
-                f"{LIB_PATH} is missing; build it with `python -m secure_infer_b200.build`")
-        handle = ct.CDLL(str(LIB_PATH))
+        handle = _preloaded()
+        if handle is None:
+            if not LIB_PATH.exists():
+                raise NativeLibraryMissing(
+                    f"{LIB_PATH} is missing; build it with `python -m secure_infer_b200.build`")
+            handle = ct.CDLL(str(LIB_PATH))
         for table in (PLUGIN_SIGNATURES, HOST_SIGNATURES):
             for name, (args, res) in table.items():
                 fn = getattr(handle, name, None)

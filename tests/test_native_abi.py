@@ -44,3 +44,18 @@ def test_kernel_profile_names_and_empty_collect():
     cnt = (ct.c_uint64 * len(names))()
     assert lib.secure_infer_kernel_profile_collect(us, cnt, len(names)) == 0
     assert list(cnt) == [0] * len(names)
+
+
+def test_preloaded_library_binds_through_process_namespace():
+    """With the library LD_PRELOADed (the reference's deployment, run.sh:66),
+    the Python side binds its symbols through ctypes.CDLL(None)."""
+    import os
+    import subprocess
+    import sys
+    from secure_infer_b200 import _native
+    code = ("import sys; sys.path.insert(0, sys.argv[1]); from secure_infer_b200 import _native; "
+            "h = _native.lib(); print(h._name, h.secure_infer_record_bytes(100))")
+    env = dict(os.environ, LD_PRELOAD=str(_native.LIB_PATH))
+    out = subprocess.run([sys.executable, "-c", code, str(ROOT)], env=env, capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert out.stdout.split() == ["None", str(_native.lib().secure_infer_record_bytes(100))]
