@@ -65,6 +65,9 @@ NCU_TRAFFIC_BYTES = {
     # one c2 layer (96 records x 256 KiB): ciphertext + keystream read; most of
     # the bf16 output is still in L2 when the kernel ends
     ("c2", "gcm_layer_verify_kernel"): 50_825_728 + 1_944_320,
+    # one c2 layer of keystream: written into L2 and read from there by the
+    # verify kernel, so almost nothing reaches DRAM
+    ("c2", "gcm_layer_ctr_kernel"): 22_784 + 4_096,
     # one c5 layer (128 records x 10256 B, K+V in one launch)
     ("c5", "gcm_layer_verify_kernel"): 2_836_224,
     # one c4 layer (128 blocks of 8 heads): bf16 read; packets stay in L2
