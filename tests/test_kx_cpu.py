@@ -100,3 +100,31 @@ def test_handshake_derivations_match_oracle(driver):
         assert kxo.host_side(host_secret, challenge, dev_public, bad) is None
         assert kxo.host_side(host_secret, rnd(800 + i, 32), dev_public, proof) is None
     assert kxo.host_side(rnd(1, 32), rnd(2, 32), le(0), bytes(32)) is None
+
+
+def test_golden_vectors_from_reference_monocypher(driver):
+    """tests/golden/kx_vectors.json holds outputs of the reference's own
+    Monocypher (make_kx_golden.py): the oracle and the host build of kx.cuh
+    must reproduce every one of them."""
+    import json
+    g = json.loads((ROOT / "tests" / "golden" / "kx_vectors.json").read_text())
+    fx = bytes.fromhex
+    for c in g["x25519"]:
+        assert kxo.x25519(fx(c["scalar"]), fx(c["u"])).hex() == c["out"]
+    assert driver([f"x {c['scalar']} {c['u']}" for c in g["x25519"]]) == [c["out"] for c in g["x25519"]]
+    for c in g["public"]:
+        assert kxo.x25519_public(fx(c["scalar"])).hex() == c["out"]
+    assert driver([f"p {c['scalar']}" for c in g["public"]]) == [c["out"] for c in g["public"]]
+    for c in g["blake2b"]:
+        assert kxo.blake2b(fx(c["msg"]), c["size"], fx(c["key"])).hex() == c["out"]
+    assert driver([f"b {c['size']} {c['key'] or '-'} {c['msg'] or '-'}" for c in g["blake2b"]]) == \
+        [c["out"] for c in g["blake2b"]]
+    for h in g["handshakes"]:
+        shared = fx(h["shared"])
+        assert kxo.x25519_public(fx(h["host_secret"])).hex() == h["host_public"]
+        assert kxo.x25519(fx(h["host_secret"]), fx(h["device_public"])) == shared
+        assert kxo.derive_key(shared, fx(h["host_public"]), fx(h["device_public"]), fx(h["challenge"])).hex() == h["key"]
+        got = driver([f"d {h['shared']} {h['host_public']} {h['device_public']} {h['challenge']}"])[0].split()
+        assert got == [h["key"], h["proof"], h["salt"]]
+        assert kxo.host_side(fx(h["host_secret"]), fx(h["challenge"]), fx(h["device_public"]), fx(h["proof"])) == \
+            (fx(h["key"]), fx(h["salt"]))
