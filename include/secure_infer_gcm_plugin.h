@@ -135,7 +135,7 @@ int secure_infer_aicpu_gcm_xor_only_do(void* stream, void* ciphertext, void* key
  * (code inside an allocator or memory budget it does not own, or a path that
  * must never pay for a device allocation): the entry points above allocate a
  * per-stream scratch area on first use, this one keeps its scratch (key
- * schedule, segment partials, arrival counter; about 0.9 MiB, held by every
+ * schedule, segment partials, arrival counter; about 1 MiB, held by every
  * GPU that loads the library until exit) in a fixed device array.  Same
  * arguments, meaning and results; returns -2 with a message on stderr when
  * bytes > 16 MiB or aad_bytes > 4096.  The first call on a device looks up the

@@ -357,6 +357,14 @@ struct __align__(16) GcmSchedule {
     uint4 tab[kGhashTables][32 * 16];
     uint4 byte32[2 * 256 * 8]; // H^32, byte position b, value v at [((b >> 3) * 256 + v) * 8 + (b & 7)]
     uint4 lane8[32 * 16 * 8]; // H^(8 - r) at [(p * 16 + v) * 8 + r], r = 0..7
+    uint4 pow2hi[5][32 * 16]; // H^(2^e), e = 13..17 (segment joins of the plugin kernel)
+    uint4 byte256[2 * 256 * 8]; // H^256 byte tables, layout of byte32 (Horner table of the plugin kernel)
 };
+
+// Nibble table of H^(2^e), 8 <= e <= 17.
+__device__ __forceinline__ const uint4* tab_pow2(const GcmSchedule* S, int e)
+{
+    return e <= 11 ? S->tab[tab_pow_32k(1 << (e - 5))] : e == 12 ? S->tab[kTabSeg] : S->pow2hi[e - 13];
+}
 
 }  // namespace sib

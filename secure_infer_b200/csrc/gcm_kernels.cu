@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(256) gcm_schedule_kernel(const uint8_t* key, c
 {
     __shared__ uint4 tab_s[32 * 16];
     __shared__ uint4 pow_le[kGhashTables];
+    __shared__ uint4 pow_hi[5];               // H^(2^13) .. H^(2^17)
     __shared__ int s_skip;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
@@ -234,9 +235,18 @@ __global__ void __launch_bounds__(256) gcm_schedule_kernel(const uint8_t* key, c
         __syncwarp();
         cur = gf_mul_warp<false>(cur, tab_s, lane);
         if (lane == 0) pow_le[kTabSeg] = cur;
+        // H^(2^13) .. H^(2^17) by squaring, for the plugin kernel's segment joins.
+        for (int e = 0; e < 5; ++e) {
+            __syncwarp();
+            build_nibble_table_warp(bswap4(cur), tab_s, lane);
+            __syncwarp();
+            cur = gf_mul_warp<false>(cur, tab_s, lane);
+            if (lane == 0) pow_hi[e] = cur;
+        }
     }
     __syncthreads();
     for (int t = warp; t < kGhashTables; t += 8) build_nibble_table_warp(bswap4(pow_le[t]), S->tab[t], lane);
+    if (warp < 5) build_nibble_table_warp(bswap4(pow_hi[warp]), S->pow2hi[warp], lane);
     __syncthreads();
     // Shared-memory-ready layouts for the layer kernel.
     for (int i = tid; i < 32 * 16 * 8; i += 256) {
@@ -247,6 +257,8 @@ __global__ void __launch_bounds__(256) gcm_schedule_kernel(const uint8_t* key, c
         const int b = (i >> 11) * 8 + (i & 7), v = (i >> 3) & 255;
         const uint4* t32 = S->tab[tab_pow_small(32)];
         S->byte32[i] = xor4(t32[(2 * b) * 16 + (v >> 4)], t32[(2 * b + 1) * 16 + (v & 15)]);
+        const uint4* t256 = S->tab[kTabStride];
+        S->byte256[i] = xor4(t256[(2 * b) * 16 + (v >> 4)], t256[(2 * b + 1) * 16 + (v & 15)]);
     }
     __syncthreads();
     if (tid == 0) {
@@ -404,7 +416,7 @@ __global__ void __launch_bounds__(kCtrThreads, 1) gcm_ctr_kernel(const __grid_co
 // ("write then gate": nothing is released before the stream reaches the
 // layer event recorded after this kernel).
 constexpr int kBatch = 8;
-constexpr size_t kGhashSmem = 4096 * sizeof(uint4);          // H^256 table, 8 replicas
+constexpr size_t kGhashSmem = 4096 * sizeof(uint4);          // H^256 (plugin) or H^32 (layer) byte tables
 constexpr size_t kAesSmem = 256 * 32 * sizeof(uint32_t) + 256; // T-table replicas + round keys
 template <bool kInlineAes>
 __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_constant__ SegmentLaunch L)
@@ -414,19 +426,26 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
     uint32_t* aes_te = reinterpret_cast<uint32_t*>(smem + kGhashSmem);
     uint32_t* aes_rk = aes_te + 256 * 32;
     __shared__ uint4 red[kThreads];
-    __shared__ uint4 join_tab[512];     // H^(segment length), for the record's last CTA
     __shared__ uint32_t s_last, s_ok;
 
     const GcmSchedule* __restrict__ S = L.sched;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5, rep = lane & 7u;
-    for (uint32_t i = tid; i < 4096; i += kThreads) gtab[i] = __ldg(&S->tab[kTabStride][i >> 3]);
+    // The Horner multiplier H^256 as byte tables (64 KiB) by one bulk copy,
+    // overlapping the AES table fill; waited for (bounded) before the first
+    // GHASH step.  A copy that never lands poisons the partials, so records
+    // fail closed.
+    __shared__ __align__(8) uint64_t gtab_bar;
+    if (tid == 0) {
+        mbar_init_expect(&gtab_bar, 65536u);
+        bulk_g2s(gtab, S->byte256, 65536u, &gtab_bar);
+    }
     if constexpr (kInlineAes) fill_aes_smem(aes_te, aes_rk, S);
     __syncthreads();
+    const bool gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
     const GcmRecord* recs = L.recs ? L.recs : L.inl;
     const SmemAes aes{aes_te, aes_rk, lane};
     // Segment length SB (256..4096 blocks) and its join table H^SB.
     const int64_t SB = L.seg_blocks ? L.seg_blocks : kSegBlocks;
-    const uint4* join_src = S->tab[SB == 4096 ? kTabSeg : tab_pow_32k(static_cast<int>(SB / 32))];
 
     for (uint32_t w = blockIdx.x; w < L.total_segs; w += gridDim.x) {
         uint32_t lo = 0, hi = L.nrec - 1;
@@ -504,11 +523,12 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
                         store_block(out + off, xor4(X, ks), avail, aligned);
                     }
                 }
-                if (op != kOpXorOnly) Y = j == 0 ? X : xor4(gf_mul_table<8, false>(Y, gtab, rep), X);
+                if (op != kOpXorOnly) Y = j == 0 ? X : xor4(gf_mul_byte8(Y, gtab, rep), X);
             }
         }
 
         if (op != kOpXorOnly) {
+            if (!gtab_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
             if (warp != 7) Y = gf_mul_table<1, true>(Y, S->tab[tab_pow_32k(7 - warp)], 0);
             red[tid] = Y;
             __syncthreads();
@@ -532,24 +552,48 @@ __global__ void __launch_bounds__(kThreads, 2) gcm_segment_kernel(const __grid_c
         if (!s_last) continue;
 
         __threadfence();
-        if (nseg > 1 && op != kOpXorOnly) {
-            for (uint32_t e = tid; e < 512; e += kThreads) join_tab[e] = __ldg(&join_src[e]);
+        // Join the record's partials, S = sum_k p_k H^(SB (nseg - 1 - k)).  SB
+        // is a power of two 2^e0, so every power needed is some H^(2^e).  The
+        // five tables H^(SB 2^b), b = 0..4, go into the Horner table's shared
+        // memory (this CTA's main loop is done); chunks of 32 partials (the
+        // first takes the remainder) are reduced by a lane tree, up to eight
+        // chunks at a time on the eight warps, and warp 0 joins the chunk
+        // values with H^(32 SB).
+        uint4 acc = zero4();
+        if (op != kOpXorOnly && nseg == 1) {
+            acc = __ldcg(&L.partials[R.seg_first]);
+        } else if (op != kOpXorOnly) {
+            const int e0 = 31 - __clz(static_cast<uint32_t>(SB));
+            for (uint32_t e = tid; e < 5u * 512u; e += kThreads) gtab[e] = __ldg(&tab_pow2(S, e0 + static_cast<int>(e >> 9))[e & 511u]);
             __syncthreads();
+            const uint32_t nchunk = (nseg + 31) / 32, first = nseg - (nchunk - 1) * 32;
+            for (uint32_t c0 = 0; c0 < nchunk; c0 += kThreads) {
+                const uint32_t round = nchunk - c0 < kThreads ? nchunk - c0 : kThreads;
+                for (uint32_t c = c0 + warp; c < c0 + round; c += 8) {
+                    const uint32_t cnt = c == 0 ? first : 32, start = c == 0 ? 0 : first + (c - 1) * 32;
+                    const uint32_t pad = 32 - cnt;
+                    uint4 v = lane >= pad ? __ldcg(&L.partials[R.seg_first + start + lane - pad]) : zero4();
+#pragma unroll
+                    for (int b = 0; b < 5; ++b) {
+                        const uint4 left = shfl_up4(v, 1u << b);
+                        const uint32_t grp = (2u << b) - 1u;
+                        if ((lane & grp) == grp) v = xor4(gf_mul_table<1, false>(left, gtab + 512 * b, 0), v);
+                    }
+                    if (lane == 31) red[c - c0] = v;
+                }
+                __syncthreads();
+                if (warp == 0) {
+                    for (uint32_t c = 0; c < round; ++c)
+                        acc = (c0 == 0 && c == 0) ? red[0] : xor4(gf_mul_warp<true>(acc, tab_pow2(S, e0 + 5), lane), red[c]);
+                }
+                __syncthreads();
+            }
+            if (w + gridDim.x < L.total_segs) {   // more segments for this CTA: restore the Horner table
+                for (uint32_t i = tid; i < 4096; i += kThreads) gtab[i] = __ldg(&S->byte256[i]);
+                __syncthreads();
+            }
         }
         if (warp == 0) {
-            uint4 acc = zero4();
-            if (op != kOpXorOnly) {
-                for (uint32_t k0 = 0; k0 < nseg; k0 += 32) {
-                    const uint32_t cnt = nseg - k0 < 32 ? nseg - k0 : 32;
-                    const uint4 mine = lane < cnt ? __ldcg(&L.partials[R.seg_first + k0 + lane]) : zero4();
-                    for (uint32_t kk = 0; kk < cnt; ++kk) {
-                        const uint4 p = make_uint4(
-                            __shfl_sync(0xffffffffu, mine.x, kk), __shfl_sync(0xffffffffu, mine.y, kk),
-                            __shfl_sync(0xffffffffu, mine.z, kk), __shfl_sync(0xffffffffu, mine.w, kk));
-                        acc = (k0 == 0 && kk == 0) ? p : xor4(gf_mul_warp<false>(acc, join_tab, lane), p);
-                    }
-                }
-            }
             if (lane == 0) {
                 uint32_t ok = 1u;
                 if (op == kOpDecrypt || op == kOpVerify || op == kOpEncrypt) {
@@ -1725,7 +1769,7 @@ struct NoAllocScratch {
 }  // namespace
 }  // namespace sib
 
-// The scratch itself: about 0.9 MiB, held by every GPU that loads this library
+// The scratch itself: about 1 MiB, held by every GPU that loads this library
 // until the process exits.  Static device memory starts zeroed.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[sizeof(sib::NoAllocScratch)];
 
