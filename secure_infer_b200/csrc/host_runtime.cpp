@@ -1087,7 +1087,9 @@ void prep_drop_stale()
     g_prep.cv.notify_all();
 }
 
-// Stops the encrypt thread (after its current entry) and frees the pool.
+// Stops the encrypt thread (after its current entry) and frees the pool,
+// including the buffers staging slots still hold.  Call after the device is
+// idle: a held buffer may be the source of a copy until then.
 void prep_shutdown()
 {
     {
@@ -1097,6 +1099,10 @@ void prep_shutdown()
     g_prep.cv.notify_all();
     if (g_prep.worker.joinable()) g_prep.worker.join();
     std::lock_guard<std::mutex> lock(g_prep.mu);
+    for (auto& slot : g_s.h2d) {
+        if (slot.hold) prep_release_locked(*slot.hold);
+        slot.hold.reset();
+    }
     for (auto& e : g_prep.entries) prep_release_locked(*e);
     for (auto& e : g_prep.queue) prep_release_locked(*e);
     g_prep.entries.clear();
@@ -1476,8 +1482,8 @@ void shutdown_locked()
 {
     host_only_session = false;
     if (!g_s.ready) return;
-    prep_shutdown();
     cudaDeviceSynchronize();
+    prep_shutdown();
     {
         std::lock_guard<std::mutex> dl(g_d2h_mu);
         g_s.d2h_stop = true;
