@@ -69,7 +69,7 @@ NCU_TRAFFIC_BYTES = {
     # verify kernel, so almost nothing reaches DRAM
     ("c2", "gcm_layer_ctr_kernel"): 22_784 + 4_096,
     # one c5 layer (128 records x 10256 B, K+V in one launch)
-    ("c5", "gcm_layer_verify_kernel"): 2_836_224,
+    ("c5", "gcm_layer_verify_kernel"): 2_939_392,
     # one c4 layer (128 blocks of 8 heads): bf16 read; packets stay in L2
     ("c4", "kv_encode_kernel"): 33_612_800 + 768,
     ("c4", "gcm_layer_encrypt"): 21_253_120,
