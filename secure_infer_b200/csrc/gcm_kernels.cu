@@ -914,19 +914,25 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
         // register whose load is still in flight would wait for that load.
         uint4 xq[kLayerPrefetch], kq[kLayerPrefetch];
         if constexpr (kCodec) {
-#pragma unroll
-            for (int u = 0; u < kLayerPrefetch; ++u) load(u, xq[u], kq[u]);
+            // Codec packets: the warp's payload blocks (packets, scales and
+            // lows) and their keystream stream into L2 first; the loop then
+            // loads one step ahead and is not unrolled, so the large
+            // dequantising body is emitted once.
+            const int64_t i0 = base > a_blk ? base : a_blk;
+            const int64_t i1 = seg_end < a_blk + n_blk ? seg_end : a_blk + n_blk;
+            if (lane == 0 && i1 > i0) {
+                const uint64_t off = static_cast<uint64_t>(i0 - a_blk) * 16u;
+                l2_prefetch_bulk(in + off, static_cast<uint32_t>(i1 - i0) * 16u);
+                l2_prefetch_bulk(ksp + off, static_cast<uint32_t>(i1 - i0) * 16u);
+            }
+            uint4 xc, kc;
+            load(0, xc, kc);
             if (!gtab_ready) gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
 #pragma unroll 1
-            for (int j0 = 0; j0 < J; j0 += kLayerPrefetch) {
-#pragma unroll
-                for (int u = 0; u < kLayerPrefetch; ++u) {
-                    const int j = j0 + u;
-                    if (j >= J) break;
-                    const uint4 x0 = xq[u], k0 = kq[u];
-                    load(j + kLayerPrefetch, xq[u], kq[u]);
-                    consume(j, x0, k0);
-                }
+            for (int j = 0; j < J; ++j) {
+                const uint4 x0 = xc, k0 = kc;
+                load(j + 1, xc, kc);
+                consume(j, x0, k0);
             }
         } else {
             // General head (AAD side), tight interior, general tail (length
