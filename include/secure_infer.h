@@ -35,7 +35,10 @@ extern "C" {
 /* Install the session key (16 bytes, AES-128) and the 4-byte IV salt on
  * `device`, derive H = E_K(0^128) and the key schedule on the device.  Stands
  * in for the device key agreement (secure_infer.cpp:449-521), whose outputs
- * are exactly this key and salt.  Resets tickets and the replay set. */
+ * are exactly this key and salt.  This is the recommended session path.
+ * Clears the replay set.  Tickets come from one counter per process that no
+ * init resets (as the reference's, secure_infer.cpp:126, :264), so a second
+ * session with the same key and salt never repeats a GCM nonce. */
 int secure_infer_session_init(int device, const uint8_t* key16, const uint8_t* iv_salt4);
 
 /* Experimental session setup by key agreement (secure_infer.cpp:449-521,
@@ -47,7 +50,14 @@ int secure_infer_session_init(int device, const uint8_t* key16, const uint8_t* i
  * BLAKE2b-32(key = key, challenge) in constant time and derives the salt
  * BLAKE2b-4(key = shared, "SecureInfer IV salt v1").  The device key schedule
  * is built from the device's own copy of the key.  Returns 0, or -1 with no
- * session when any step or the proof check fails. */
+ * session when any step or the proof check fails.
+ *
+ * WEAK DEVICE ENTROPY: the reference's AICPU reads its X25519 secret from
+ * /dev/urandom; a GPU has no entropy source, so the device secret here is a
+ * BLAKE2b hash of %globaltimer / clock64 samples and an atomic counter.  Those
+ * inputs are partly predictable and hold little entropy, and a guessed device
+ * secret reveals the session key.  Use secure_infer_session_init with a key
+ * from a real key exchange for anything but experiments. */
 int secure_infer_session_init_key_agreement(int device);
 
 /* Tear down the session (waits for in-flight work, frees staging). */

@@ -138,8 +138,10 @@ int secure_infer_aicpu_gcm_xor_only_do(void* stream, void* ciphertext, void* key
  * schedule, segment partials, arrival counter; about 1 MiB, held by every
  * GPU that loads the library until exit) in a fixed device array.  Same
  * arguments, meaning and results; returns -2 with a message on stderr when
- * bytes > 16 MiB or aad_bytes > 4096.  The first call on a device looks up the
- * array's address, so make it before any stream capture.  Every call shares
+ * bytes > 16 MiB or aad_bytes > 4096.  Every call looks up the array's
+ * address on the current device (so it stays valid after cudaDeviceReset);
+ * the first call on a device may load the module, so make it before any
+ * stream capture.  Every call shares
  * the array: calls whose work overlaps on the GPU race and must be serialised
  * by the caller. */
 int secure_infer_aicpu_gcm_decrypt_verify_aad_noalloc_do(void* stream, void* ciphertext, void* key,

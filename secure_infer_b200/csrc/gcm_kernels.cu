@@ -1784,23 +1784,16 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[sizeof(sib::NoAllocSc
 namespace sib {
 namespace {
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
-
 // Device address of g_noalloc_scratch on the current device.  In host code the
 // array's name is only a host-side stand-in; the address comes from the
-// runtime, once per device, with that device current.
+// runtime with the device current.  It is looked up on every call rather than
+// cached: after cudaDeviceReset the module is loaded again and the array may
+// move, and the lookup costs a few microseconds of host time.
 NoAllocScratch* noalloc_scratch()
 {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
-        g_noalloc_ptr[dev] = p;
-    }
-    return static_cast<NoAllocScratch*>(g_noalloc_ptr[dev]);
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return nullptr;
+    return static_cast<NoAllocScratch*>(p);
 }
 
 }  // namespace
@@ -1808,8 +1801,9 @@ NoAllocScratch* noalloc_scratch()
 
 // Same arguments, meaning and results as
 // secure_infer_aicpu_gcm_decrypt_verify_aad_do; returns -2 (with a message on
-// stderr) when bytes exceed 16 MiB or aad_bytes exceed 4096.  The first call on
-// a device looks up the scratch address, so make it before any stream capture.
+// stderr) when bytes exceed 16 MiB or aad_bytes exceed 4096.  Every call looks
+// up the scratch address of the current device; the first call on a device may
+// load the module, so make it before any stream capture.
 // All calls share the one scratch array: calls whose work overlaps on the GPU
 // (for example on two streams at once) race and must be serialised by the
 // caller.

@@ -55,16 +55,23 @@ def test_aad_from_registered_range(host_session, golden_records):
     assert lib.secure_infer_build_gcm_aad(buf.ctypes.data, 64, 3, 9, 0, out) == -1
 
 
-def test_encrypt_records_match_golden_layout(host_session, golden_records):
-    lib = host_session
-    row = golden_records["rows"][1]
+def _golden_record_sha(row, key_hex, salt_hex):
+    """Encrypts the golden record in this (fresh) process: the ticket counter
+    is process-wide and starts at 1, so it reaches the golden ticket only in a
+    process that has issued no more tickets than that."""
+    import sys
+    from conftest import ROOT
+    sys.path.insert(0, str(ROOT))
+    from secure_infer_b200 import _native
+    lib = _native.lib()
+    assert lib.secure_infer_session_init(-1, (ct.c_uint8 * 16)(*bytes.fromhex(key_hex)),
+                                         (ct.c_uint8 * 4)(*bytes.fromhex(salt_hex))) == 0
     count = row["count"]
     pool = np.zeros((row["block"] + 1) * count, np.uint8)
     plain = det_bytes(row["plain_seed"], count)
     pool[row["block"] * count:(row["block"] + 1) * count] = np.frombuffer(plain, np.uint8)
     lib.secure_infer_register_host_range_ex(pool.ctypes.data, pool.nbytes, row["layer"], row["kind"], count)
     stride = lib.secure_infer_record_bytes(count)
-    assert stride == row["record_len"]
     # Advance the ticket counter so the record gets the golden ticket.
     for _ in range(row["ticket"] - 1):
         lib.secure_infer_new_transfer_ticket()
@@ -72,8 +79,48 @@ def test_encrypt_records_match_golden_layout(host_session, golden_records):
     srcs = (ct.c_void_p * 1)(pool.ctypes.data + row["block"] * count)
     tickets = (ct.c_uint64 * 1)()
     assert lib.secure_infer_h2d_encrypt_records(srcs, count, 1, rec.ctypes.data, stride, tickets) == 0
-    assert tickets[0] == row["ticket"]
-    assert hashlib.sha256(rec.tobytes()).hexdigest() == row["record_sha256"]
+    lib.secure_infer_session_shutdown()
+    return stride, int(tickets[0]), hashlib.sha256(rec.tobytes()).hexdigest()
+
+
+def test_encrypt_records_match_golden_layout(golden_records):
+    import multiprocessing as mp
+    row = golden_records["rows"][1]
+    with mp.get_context("spawn").Pool(1) as p:
+        stride, ticket, sha = p.apply(_golden_record_sha, (row, golden_records["key"], golden_records["salt"]))
+    assert stride == row["record_len"]
+    assert ticket == row["ticket"]
+    assert sha == row["record_sha256"]
+
+
+def test_reinit_same_key_never_repeats_a_nonce(golden_records):
+    """A second session with the same key and salt continues the ticket
+    counter: no (key, IV) pair is used twice, so the same plaintext encrypts
+    to different records."""
+    from secure_infer_b200 import _native
+    lib = _native.lib()
+    key = (ct.c_uint8 * 16)(*bytes.fromhex(golden_records["key"]))
+    salt = (ct.c_uint8 * 4)(*bytes.fromhex(golden_records["salt"]))
+    count, n = 4096, 4
+    data = np.frombuffer(det_bytes("reinit", count * n), np.uint8).reshape(n, count).copy()
+    stride = lib.secure_infer_record_bytes(count)
+    srcs = (ct.c_void_p * n)(*[data.ctypes.data + i * count for i in range(n)])
+    seen_tickets, seen_ivs, seen_ct = set(), set(), set()
+    for _ in range(2):
+        assert lib.secure_infer_session_init(-1, key, salt) == 0
+        lib.secure_infer_register_host_range_ex(data.ctypes.data, data.nbytes, 2, 0, count)
+        recs = np.zeros((n, stride), np.uint8)
+        tickets = (ct.c_uint64 * n)()
+        assert lib.secure_infer_h2d_encrypt_records(srcs, count, n, recs.ctypes.data, stride, tickets) == 0
+        lib.secure_infer_session_shutdown()
+        for i in range(n):
+            iv = orc.derive_transfer_iv(bytes(salt), tickets[i])
+            assert tickets[i] not in seen_tickets and iv not in seen_ivs
+            seen_tickets.add(tickets[i])
+            seen_ivs.add(iv)
+            c = recs[i, :count].tobytes()
+            assert c not in seen_ct
+            seen_ct.add(c)
 
 
 def test_encrypt_many_records_threads(host_session):

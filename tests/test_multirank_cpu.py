@@ -3,8 +3,8 @@
 Each rank (one TP shard) runs its own host-only session with the key and salt
 bench.py gives it, encrypts records for its own KV heads, and the ranks
 exchange what they produced: a rank's records authenticate under its own
-session and under no other, tickets restart per session, and the job time is
-the maximum over ranks.
+session and under no other, each rank process numbers its tickets from 1,
+and the job time is the maximum over ranks.
 """
 from __future__ import annotations
 
@@ -47,7 +47,7 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str):
     tickets = (ct.c_uint64 * N)()
     srcs = (ct.c_void_p * N)(*[kv.ctypes.data + i * COUNT for i in range(N)])
     assert lib.secure_infer_h2d_encrypt_records(srcs, COUNT, N, recs.ctypes.data, stride, tickets) == 0
-    assert list(tickets) == list(range(1, N + 1))      # ticket space is per session
+    assert list(tickets) == list(range(1, N + 1))      # each rank process has its own ticket counter
 
     mine = torch.from_numpy(recs.copy())
     gathered = [torch.zeros_like(mine) for _ in range(world)]
