@@ -11,7 +11,15 @@ dataset for this path):
       48 blocks of 128 tokens, KV_CODEC=none, TP=1          (default at N=1)
   c3  Qwen2.5-7B: 28 layers, 4 KV heads, 48 blocks, KV_CODEC=int8, values
       N(0,1) with 1% outliers at 8 sigma
-  c5  Llama-3-70B TP=8: 80 layers, 1 KV head per GPU, 64 blocks, KV_CODEC=int4
+  c5  Llama-3-70B at TP=8: 80 layers, 8 KV heads (1 per GPU), 64 blocks,
+      KV_CODEC=int4 (--tp 2/4 for 4/2 heads per GPU)
+
+Multi-GPU (--gpus N under torchrun): the path's TP partition.  Each rank owns
+kv_heads / TP heads of every layer (TP = --tp, else the config's own TP, else
+N) with its own session, streams and host pool share; there is no collective
+on the path (NCCL carries only the barrier and the max-over-ranks timing).
+Ranks sharing a host split its CPUs into disjoint slices for their OpenSSL
+workers.
 
 Reported:
   value  whole-job GB/s with the encrypted records resident in HBM (inputs
@@ -48,15 +56,37 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# The CPUs this process may use at start, before a rank pins itself to its slice.
+START_CPUS = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else None
 
 CONFIGS = {
+    # heads = KV heads of the whole model; each rank of a TP=T job owns heads / T
+    # of them (T = --tp, else the config's "tp", else the number of GPUs).
     "c2": dict(model="Llama-3-8B", layers=32, heads=8, blocks=48, codec="none", outliers=False),
     "c3": dict(model="Qwen2.5-7B", layers=28, heads=4, blocks=48, codec="int8", outliers=True),
-    "c5": dict(model="Llama-3-70B-TP8", layers=80, heads=1, blocks=64, codec="int4", outliers=False),
+    "c5": dict(model="Llama-3-70B", layers=80, heads=8, blocks=64, codec="int4", outliers=False, tp=8),
     # writeback direction (gather + quantise + encrypt + tag; e2e adds D2H + host verify)
     "c4": dict(model="Llama-3-8B", layers=32, heads=8, blocks=64, codec="int4", outliers=False, direction="d2h"),
     "c4m": dict(model="Llama-3-8B", layers=32, heads=8, blocks=64, codec="mixed", outliers=False, direction="d2h"),
 }
+
+
+def shard_config(cfg: dict, world: int, tp: int | None) -> dict:
+    """The per-rank share of a TP-sharded job (the path's partition: every GPU
+    owns heads / TP KV heads of every layer with its own session, and no data
+    crosses between ranks).  TP is --tp, else the config's own TP (c5: the
+    70B model at TP=8, one KV head per GPU), else the number of GPUs, capped at
+    the model's KV heads; a job with more GPUs than TP shards runs the shards
+    as replicas (weak scaling)."""
+    total = cfg["heads"]
+    t = tp or cfg.get("tp") or world
+    t = min(t, total)
+    if total % t:
+        raise SystemExit(f"--tp {t} does not divide the {total} KV heads of {cfg['model']}")
+    out = dict(cfg)
+    out.update(heads=total // t, heads_total=total, tp=t)
+    return out
+
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the fused kernel,
 # from the ncu capture summarised in profiles/ (scaled per launch); None until
@@ -64,16 +94,17 @@ CONFIGS = {
 NCU_TRAFFIC_BYTES = {
     # one c2 layer (96 records x 256 KiB): ciphertext + keystream read; most of
     # the bf16 output is still in L2 when the kernel ends
-    ("c2", "gcm_layer_verify_kernel"): 50_825_728 + 1_944_320,
+    ("c2", 8, "gcm_layer_verify_kernel"): 50_825_728 + 1_944_320,
     # one c2 layer of keystream: written into L2 and read from there by the
     # verify kernel, so almost nothing reaches DRAM
-    ("c2", "gcm_layer_ctr_kernel"): 22_784 + 4_096,
+    ("c2", 8, "gcm_layer_ctr_kernel"): 22_784 + 4_096,
     # one c5 layer (128 records x 10256 B, K+V in one launch)
-    ("c5", "gcm_layer_verify_kernel"): 2_939_392,
+    ("c5", 1, "gcm_layer_verify_kernel"): 2_939_392,
     # one c4 layer (128 blocks of 8 heads): bf16 read; packets stay in L2
-    ("c4", "kv_encode_kernel"): 33_612_800 + 768,
-    ("c4", "gcm_layer_encrypt"): 21_253_120,
+    ("c4", 8, "kv_encode_kernel"): 33_612_800 + 768,
+    ("c4", 8, "gcm_layer_encrypt"): 21_253_120,
 }
+
 
 # Shared-memory wavefronts per 16-byte block that the algorithm needs (the
 # binding pipe): GHASH with byte tables = 16 conflict-free LDS.128 per lane per
@@ -260,6 +291,72 @@ def link_gbs(torch, stream, direction="h2d", nbytes=256 << 20, reps=5, write_com
     return best
 
 
+def host_copy_gbs(torch, nbytes: int = 1 << 30, reps: int = 3) -> tuple[float, int]:
+    """Host memory copy bandwidth, (read + write bytes) / s, best of `reps`
+    copies of `nbytes` with torch's CPU copy on every CPU this process may use
+    (the host's own bound on encrypting records into staging while the copy
+    engines read them out).  Returns (GB/s, threads)."""
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    a = torch.ones(nbytes, dtype=torch.uint8)
+    b = torch.zeros(nbytes, dtype=torch.uint8)
+    best = 0.0
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        b.copy_(a)
+        best = max(best, 2 * nbytes / (time.perf_counter() - t0) / 1e9)
+    torch.set_num_threads(prev)
+    del a, b
+    return best, threads
+
+
+def rank_host_pool(world: int) -> dict:
+    """The library's host pool for this rank (OpenSSL workers pinned to the
+    rank's slice of the host's CPUs when ranks share the host); the rank's
+    own Python thread moves onto the same slice."""
+    from secure_infer_b200 import _native
+    info = _native.host_pool_info()
+    if world > 1 and info["pinned"] and info["cpus"] and hasattr(os, "sched_setaffinity"):
+        os.sched_setaffinity(0, info["cpus"])
+    return {"threads_per_rank": info["threads"] + 1, "cpus_per_rank": len(info["cpus"]),
+            "pinned": info["pinned"], "note": "OpenSSL workers + the submitting thread, per rank"}
+
+
+def measure_host_bound(torch, dist, rank: int) -> dict | None:
+    """Rank 0 measures the host's copy bandwidth while every other rank waits
+    at a barrier (all ranks take the same collective steps)."""
+    if dist is not None:
+        dist.barrier()
+    out = None
+    if rank == 0:
+        saved = os.sched_getaffinity(0) if hasattr(os, "sched_getaffinity") else None
+        if saved is not None and START_CPUS:
+            os.sched_setaffinity(0, START_CPUS)
+        gbs, threads = host_copy_gbs(torch)
+        if saved is not None and hasattr(os, "sched_setaffinity"):
+            os.sched_setaffinity(0, saved)
+        out = {"gbs": round(gbs, 1), "threads": threads}
+    if dist is not None:
+        dist.barrier()
+    return out
+
+
+def host_bound(host_mem: dict | None, algo: int, link_bytes: int, world: int) -> dict | None:
+    """The host's memory bound on e2e: every record crosses host memory three
+    times per step (plaintext read and ciphertext written by OpenSSL, then read
+    by the copy engine; or, for writeback, written by the copy engine, read by
+    OpenSSL and the plaintext written), on every rank."""
+    if not host_mem:
+        return None
+    host_bytes = 3 * link_bytes * world
+    return {"host_copy_gbs": host_mem["gbs"], "copy_threads": host_mem["threads"],
+            "host_bytes_per_step_all_ranks": host_bytes,
+            "e2e_bound_gbs": round(host_mem["gbs"] * algo * world / host_bytes, 1),
+            "note": "host copy bandwidth = (read + write) bytes/s of a 1 GiB torch CPU copy on all host CPUs; "
+                    "e2e_bound = that bandwidth spread over 3 host-memory passes per record byte"}
+
+
 def build_workload(cfg, rank, torch, nl):
     """Host pool (pinned, registered), device paged cache, block table, records."""
     L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
@@ -301,6 +398,159 @@ def build_workload(cfg, rank, torch, nl):
     torch.cuda.empty_cache()
     return dict(payload=payload, cache=cache, perm=perm, bits=bits, num_gpu_blocks=num_gpu_blocks)
 
+# Per-GPU attention-side shapes of the configs' models (hidden size, query
+# heads, FFN width of the whole model; a TP=T rank holds 1/T of the heads and
+# of the FFN).
+MODEL_SHAPES = {
+    "Llama-3-8B": dict(hidden=4096, q_heads=32, ffn=14336),
+    "Qwen2.5-7B": dict(hidden=3584, q_heads=28, ffn=18944),
+    "Llama-3-70B": dict(hidden=8192, q_heads=64, ffn=28672),
+}
+
+
+def attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_wait, suffix: int, reps: int = 3):
+    """Reload hidden behind attention (the per-layer gate of the reference's
+    RuntimeWorker.wait_for_layer_load, reuse/connector.py:378-410).
+
+    Per layer l, a load stream reloads l while a compute stream, gated on
+    l's reload (a CUDA event after the device-resident reload; the library's
+    secure_infer_layer_ready_wait after the end-to-end one), runs a stand-in
+    for the suffix prefill of l over the reloaded paged cache:
+      attention: gather of l's K/V prefix blocks through the block table, then
+                 GQA SDPA of `suffix` query tokens over prefix + suffix keys
+                 (no mask);
+      layer:     the same attention plus the layer's QKV / O projections and
+                 SwiGLU MLP GEMMs for the suffix tokens (random bf16 weights,
+                 one set shared by all layers).
+    exposed_us_per_layer = (overlapped time - compute-alone time) / layers;
+    pipeline_finish_ms is the reference's own estimate of the overlapped time
+    (reuse/completion_model.py:4-5: max(load + compute/L, compute + load/L)).
+    The stand-in is measurement scaffolding, not part of the path."""
+    import torch.nn.functional as F
+    L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
+    m = MODEL_SHAPES[cfg["model"]]
+    tp = cfg["tp"]
+    qh, hid, ffn = m["q_heads"] // tp, m["hidden"], m["ffn"] // tp
+    P, S, D = B * 128, suffix, 128
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(5)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    table = torch.tensor(perm[:B], dtype=torch.long, device=dev)
+    x = rnd(S, hid)
+    q_only = rnd(1, qh, S, D)
+    w_qkv, w_o = rnd(hid, (qh + 2 * H) * D, scale=0.02), rnd(qh * D, hid, scale=0.02)
+    w_gu, w_d = rnd(hid, 2 * ffn, scale=0.02), rnd(ffn, hid, scale=0.02)
+    kbuf, vbuf = rnd(P + S, H, D), rnd(P + S, H, D)
+    ls, cs = torch.cuda.Stream(), torch.cuda.Stream()
+    lsp = ct.c_void_p(ls.cuda_stream)
+    csp = ct.c_void_p(cs.cuda_stream)
+
+    def attend(layer, q):
+        torch.index_select(cache[layer][0], 0, table, out=kbuf[:P].view(B, 128, H, D))
+        torch.index_select(cache[layer][1], 0, table, out=vbuf[:P].view(B, 128, H, D))
+        return F.scaled_dot_product_attention(q, kbuf.view(1, P + S, H, D).transpose(1, 2),
+                                              vbuf.view(1, P + S, H, D).transpose(1, 2), enable_gqa=True)
+
+    def attention(layer):
+        attend(layer, q_only)
+
+    def full_layer(layer):
+        qkv = x @ w_qkv
+        kbuf[P:].copy_(qkv[:, qh * D:(qh + H) * D].view(S, H, D))
+        vbuf[P:].copy_(qkv[:, (qh + H) * D:].view(S, H, D))
+        o = attend(layer, qkv[:, :qh * D].view(S, qh, D).transpose(0, 1).unsqueeze(0))
+        h = o.squeeze(0).transpose(0, 1).reshape(S, qh * D) @ w_o
+        gu = h @ w_gu
+        (F.silu(gu[:, :ffn]) * gu[:, ffn:]) @ w_d
+
+    def timed(enqueue, sleep_s=0.02):
+        """Device time of what `enqueue` puts on the two streams; both start
+        together behind a device sleep on the compute stream, so the host's
+        enqueue runs ahead of the device (sleep_s = 0: host-paced)."""
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        if sleep_s:
+            with torch.cuda.stream(cs):
+                torch.cuda._sleep(int(sleep_s * 2.0e9))
+        t0.record(cs)
+        ls.wait_event(t0)
+        enqueue()
+        cs.wait_stream(ls)
+        t1.record(cs)
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1)
+
+    def median(fn):
+        return statistics.median(fn() for _ in range(reps))
+
+    events = [torch.cuda.Event() for _ in range(L)]
+
+    def dev_reload_all():
+        for layer in range(L):
+            dev_reload(layer, lsp)
+
+    def e2e_reload_all():
+        for layer in range(L):
+            e2e_reload(layer, lsp)
+
+    out = {"suffix_tokens": S, "prefix_tokens": P, "layers": L,
+           "stand_in": f"per layer: {qh} query heads x {S} suffix tokens over {P} + {S} keys of {H} KV heads "
+                       f"(GQA SDPA after a block-table gather); 'layer' adds the QKV/O projections and the "
+                       f"SwiGLU MLP ({hid} -> {ffn} -> {hid}) GEMMs",
+           "gate": "compute stream waits on each layer's reload (CUDA event after secure_infer_reload_records; "
+                   "secure_infer_layer_ready_wait after secure_infer_h2d_reload_layer)"}
+    # Warm up every piece (kernels, SDPA backend, cuBLAS heuristics).
+    for fn in (attention, full_layer):
+        with torch.cuda.stream(cs):
+            fn(0)
+    timed(dev_reload_all)
+    timed(e2e_reload_all, 0)
+    assert e2e_wait() == 0
+    reload_dev_ms = median(lambda: timed(dev_reload_all))
+    reload_e2e_ms = median(lambda: timed(e2e_reload_all, 0))
+    assert e2e_wait() == 0
+    for name, fn in (("attention", attention), ("layer", full_layer)):
+        def compute_all():
+            with torch.cuda.stream(cs):
+                for layer in range(L):
+                    fn(layer)
+
+        def dev_overlap():
+            for layer in range(L):
+                dev_reload(layer, lsp)
+                events[layer].record(ls)
+                cs.wait_event(events[layer])
+                with torch.cuda.stream(cs):
+                    fn(layer)
+
+        def e2e_overlap():
+            for layer in range(L):
+                e2e_reload(layer, lsp)
+                assert lib.secure_infer_layer_ready_wait(layer, csp) == 0
+                with torch.cuda.stream(cs):
+                    fn(layer)
+
+        compute_ms = median(lambda: timed(compute_all))
+        dev_ms = median(lambda: timed(dev_overlap))
+        e2e_ms = median(lambda: timed(e2e_overlap, 0))
+        assert e2e_wait() == 0
+
+        def row(load_ms, both_ms):
+            finish = max(load_ms + compute_ms / L, compute_ms + load_ms / L)
+            return {"reload_alone_ms": round(load_ms, 3), "overlapped_ms": round(both_ms, 3),
+                    "exposed_us_per_layer": round(max(0.0, both_ms - compute_ms) * 1e3 / L, 2),
+                    "pipeline_finish_ms": round(finish, 3)}
+
+        out[name] = {"compute_alone_ms": round(compute_ms, 3),
+                     "compute_us_per_layer": round(compute_ms * 1e3 / L, 2),
+                     "device_resident_reload": row(reload_dev_ms, dev_ms),
+                     "e2e_reload": row(reload_e2e_ms, e2e_ms)}
+    return out
+
+
 
 def run_gpu(args, cfg):
     import torch
@@ -315,6 +565,7 @@ def run_gpu(args, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     key, salt = rank_session_material(rank)
     nl.Session(local, key, salt)
+    host_pool = rank_host_pool(world)
     L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
     W = build_workload(cfg, rank, torch, nl)
     payload, cache, perm, bits = W["payload"], W["cache"], W["perm"], W["bits"]
@@ -457,6 +708,24 @@ def run_gpu(args, cfg):
     d2h_bytes = L * n * 4
     link = link_gbs(torch, stream, "h2d")
     link_wc = link_gbs(torch, stream, "h2d", write_combined=True)
+    host_mem = measure_host_bound(torch, dist, rank)
+
+    overlap = None
+    if world == 1 and args.suffix > 0:
+        def dev_reload(layer, lsp):
+            assert lib.secure_infer_reload_records(layer, rec_ptr[layer], strides[layer], count[layer], n,
+                                                   tickets[layer], dst_all[layer], ks_ptr, st_ptr[layer],
+                                                   codec_arg[layer], lsp, lsp) == 0
+
+        def e2e_reload(layer, lsp):
+            assert lib.secure_infer_h2d_reload_layer(layer, src_all[layer], dst_all[layer], n, count[layer],
+                                                     codec_arg[layer], 0, None, lsp) == 0
+
+        def e2e_wait():
+            return max(lib.secure_infer_recovery_wait_layer_authentication(layer) != 0 for layer in range(L))
+
+        overlap = attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_wait, args.suffix)
+        assert int(status.min().item()) == 1
 
     result = None
     if rank == 0:
@@ -467,7 +736,7 @@ def run_gpu(args, cfg):
         hbm_peak = peaks.get("hbm_gbs", 6650.0)
         dom_us = vf_mean if dominant == "gcm_layer_verify_kernel" else ks_mean
         achieved = layer_algo / (dom_us * 1e-6) / 1e9
-        traffic = NCU_TRAFFIC_BYTES.get((args.config, dominant))
+        traffic = NCU_TRAFFIC_BYTES.get((args.config, H, dominant))
         # Binding pipe: shared-memory wavefronts (1 per SM per clock) at the
         # clock sampled during the timed region.
         clk = clocks.summary()
@@ -494,16 +763,20 @@ def run_gpu(args, cfg):
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic: N(0,1) bf16 KV from seed, seeded AES-128 key/salt per rank, random block table",
-            "config": {"workload": f"{args.config}: {cfg['model']} {L} layers x {H} KV heads x 128 dim, "
-                                   f"{B} blocks x 128 tokens, KV_CODEC={cfg['codec']}, per-rank session (TP shard)",
-                       "layers": L, "kv_heads": H, "blocks": B, "records_per_layer": n,
+            "config": {"workload": f"{args.config}: {cfg['model']} TP={cfg['tp']}, {L} layers x {H} of "
+                                   f"{cfg['heads_total']} KV heads per GPU x 128 dim, {B} blocks x 128 tokens, "
+                                   f"KV_CODEC={cfg['codec']}, per-rank session (TP shard)",
+                       "layers": L, "kv_heads": H, "kv_heads_total": cfg["heads_total"], "tp": cfg["tp"],
+                       "blocks": B, "records_per_layer": n,
                        "payload_bytes_per_record": count[0], "codec": cfg["codec"],
                        "algorithmic_bytes_per_step": algo,
                        "l2": "inputs larger than L2 (%.0f MB of records resident per step)" % (
                            sum(strides[layer] * n for layer in range(L)) / 1e6),
-                       "parallelism": f"{world} independent per-GPU sessions, no collective"},
+                       "parallelism": f"tp{cfg['tp']} on {world} GPUs: independent per-GPU sessions, "
+                                      f"no collective", "host_pool": host_pool},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "per_layer_reload_us": round(e2e_ms * 1e3 / L, 2),
+                    "host_bound": host_bound(host_mem, algo, h2d_bytes, world),
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                     "link_h2d_gbs": round(link, 2),
                     "link_h2d_wc_gbs": round(link_wc, 2) if link_wc else None,
@@ -516,6 +789,7 @@ def run_gpu(args, cfg):
                     "lookahead_note": "same steps, each layer's reload announced one layer ahead "
                                       "(secure_infer_h2d_prepare_layer); encryption stays in the timed region"},
             "gpu_launches": launches,
+            "attention_overlap": overlap,
             "kernels": {"gcm_layer_ctr_kernel_us_per_layer": round(ks_mean, 2),
                         "gcm_layer_verify_kernel_us_per_layer": round(vf_mean, 2),
                         "timing": "the library's CUDA events around each launch (secure_infer_kernel_profile_*), "
@@ -562,6 +836,7 @@ def run_gpu_writeback(args, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     key, salt = rank_session_material(rank)
     nl.Session(local, key, salt)
+    host_pool = rank_host_pool(world)
     L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
     n = 2 * B
     stream = torch.cuda.Stream()
@@ -646,6 +921,7 @@ def run_gpu_writeback(args, cfg):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), dist) / args.steps
     e2e_value = world * algo / (e2e_ms * 1e-3) / 1e9
     link = link_gbs(torch, stream, "d2h")
+    host_mem = measure_host_bound(torch, dist, rank)
     d2h_step = sum(strides[layer] * n for layer in range(L))
 
     # Round trip: the host pool of layer 0 reloads through the authenticated
@@ -692,14 +968,18 @@ def run_gpu_writeback(args, cfg):
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic: N(0,1) bf16 KV from seed, seeded AES-128 key/salt per rank, shuffled block table",
-            "config": {"workload": f"{args.config}: {cfg['model']} writeback, {L} layers x {H} KV heads x 128 dim, "
-                                   f"{B} blocks x 128 tokens, KV_CODEC={cfg['codec']}, per-rank session",
-                       "layers": L, "kv_heads": H, "blocks": B, "records_per_layer": n,
+            "config": {"workload": f"{args.config}: {cfg['model']} writeback TP={cfg['tp']}, {L} layers x {H} of "
+                                   f"{cfg['heads_total']} KV heads per GPU x 128 dim, {B} blocks x 128 tokens, "
+                                   f"KV_CODEC={cfg['codec']}, per-rank session",
+                       "layers": L, "kv_heads": H, "kv_heads_total": cfg["heads_total"], "tp": cfg["tp"],
+                       "blocks": B, "records_per_layer": n,
                        "packet_bytes": sorted(set(count)), "codec": cfg["codec"], "algorithmic_bytes_per_step": algo,
                        "l2": "inputs larger than L2 (%.0f MB of bf16 KV read per step)" % (L * n * bb / 1e6),
-                       "parallelism": f"{world} independent per-GPU sessions, no collective"},
+                       "parallelism": f"tp{cfg['tp']} on {world} GPUs: independent per-GPU sessions, "
+                                      f"no collective", "host_pool": host_pool},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "per_layer_us": round(e2e_ms * 1e3 / L, 2),
+                    "host_bound": host_bound(host_mem, algo, d2h_step, world),
                     "h2d_bytes_per_step": L * n * (64 + 8),
                     "d2h_bytes_per_step": d2h_step,
                     "link_d2h_gbs": round(link, 2),
@@ -711,7 +991,7 @@ def run_gpu_writeback(args, cfg):
             "kernels": {k + "_us_per_layer": round(v[0], 2) for k, v in prof.items()},
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4), "traffic": NCU_TRAFFIC_BYTES.get(
-                             (args.config, dominant)), "smem_pipe_frac": smem,
+                             (args.config, H, dominant)), "smem_pipe_frac": smem,
                          "note": "achieved = per-layer algorithmic bytes (bf16 read + wire written) / dominant kernel "
                                  "time, the dominant kernel taken among those on the caller's stream (the "
                                  "keystream overlaps the quantiser on the producer stream); peak = measured HBM "
@@ -794,11 +1074,14 @@ def cpu_reference(cfg, args, sample_steps=3):
     host KV blocks (secure_infer.cpp:6508-6537), OpenSSL decrypt + tag verify
     (secure_infer.cpp:2479-2501) straight into the block-table position of a
     host paged cache, and for codec configs the reference decode_into
-    (optimized_decode.py:5-27) restated in numpy (the codec runs once per
-    layer on the decrypted packets).
+    (optimized_decode.py:5-27) with its own torch CPU ops on all host cores
+    (torch.set_num_threads; the codec runs once per layer and kind on the
+    decrypted packets, into a bf16 host paged cache through the block table).
     """
+    import torch
     from oracle import codec_oracle, gcm as orc
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(threads)
     L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
     rng = np.random.default_rng(7)
     key = np.frombuffer(bytes(range(16)), np.uint8).copy()
@@ -818,7 +1101,10 @@ def cpu_reference(cfg, args, sample_steps=3):
             geo[b] = (qb, sb)
     num_gpu_blocks = B + 16
     dest = np.zeros((2, num_gpu_blocks, 128, H, 128), np.uint16)
+    dest_t = torch.from_numpy(dest.view(np.int16)).view(torch.bfloat16)   # the same memory, as bf16
     perm = rng.permutation(num_gpu_blocks)[:B]
+    perm_t = torch.from_numpy(perm.astype(np.int64))
+    work = None
     ivs = np.zeros((n, 16), np.uint8)
     for i in range(n):
         ivs[i] = np.frombuffer(orc.derive_transfer_iv(b"\x01\x02\x03\x04", i + 1), np.uint8)
@@ -836,6 +1122,7 @@ def cpu_reference(cfg, args, sample_steps=3):
     st = np.zeros(n, np.uint32)
 
     def step():
+        nonlocal work
         for layer in range(L):
             b = bits_per_layer[layer]
             src, count, recs, outs = bufs[b]
@@ -844,9 +1131,9 @@ def cpu_reference(cfg, args, sample_steps=3):
             orc.host_batch(key, ivs, recs, count, outs, st, threads, encrypt=False)
             if b:
                 qb, sb = geo[b]
-                wire = np.stack(outs)
-                codec_oracle.decode_into(wire[:B], dest[0], perm, b, 0, qb, sb)
-                codec_oracle.decode_into(wire[B:], dest[1], perm, b, 1, qb, sb)
+                wire = torch.from_numpy(np.stack(outs))
+                work = codec_oracle.decode_into_torch(wire[:B], dest_t[0], perm_t, b, 0, qb, sb, work)
+                work = codec_oracle.decode_into_torch(wire[B:], dest_t[1], perm_t, b, 1, qb, sb, work)
 
     step()  # warm caches / page in
     assert st.all()
@@ -861,13 +1148,19 @@ def cpu_reference(cfg, args, sample_steps=3):
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": f"{sample_steps} full steps of {args.config} ({L} layers x {n} records: "
                                        f"OpenSSL GCM encrypt + decrypt/verify into a block-table host cache"
-                                       + (", numpy reference decode" if cfg["codec"] != "none" else "") + ")"}}
+                                       + (", reference decode_into on torch CPU (optimized_decode.py:5-27)"
+                                          if cfg["codec"] != "none" else "") + ")"}}
 
 
 def run_reference(args, cfg):
+    """The reference's CPU path for the whole job of this launch: at N GPUs
+    rank 0 alone runs the work of all N ranks (N x the per-rank KV heads) on
+    every host core, so its GB/s is the same whole-job figure as our arm's
+    `value`; the other ranks exit without work."""
     rank, world, _ = dist_env()
     if rank != 0:
         return None
+    cfg = dict(cfg, heads=cfg["heads"] * world, job_note=f"whole job: {world} rank(s) x {cfg['heads']} KV heads")
     if cfg.get("direction") == "d2h":
         r = cpu_reference_writeback(cfg, args, sample_layers=args.cpu_layers, steps=args.steps)
         L = cfg["layers"]
@@ -902,11 +1195,17 @@ def main():
     parser.add_argument("--cpu-layers", type=int, default=2,
                         help="writeback configs: layers per CPU-baseline step (a bounded sample)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--tp", type=int, default=None,
+                        help="tensor-parallel degree: each GPU owns kv_heads / tp heads (default: the config's own "
+                             "TP, else the number of GPUs)")
+    parser.add_argument("--suffix", type=int, default=512,
+                        help="reload configs at N=1: suffix tokens of the attention stand-in that the per-layer "
+                             "reload overlaps (0 skips the attention_overlap measurement)")
     parser.add_argument("--layers", type=int, default=None,
                         help="override the layer count (smaller cases for profiling)")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
-    cfg = dict(CONFIGS[args.config])
+    cfg = shard_config(CONFIGS[args.config], int(os.environ.get("WORLD_SIZE", "1")), args.tp)
     if args.layers:
         cfg["layers"] = args.layers
     if args.impl == "reference":

@@ -75,6 +75,18 @@ void secure_infer_register_host_range_ex(const void* base, size_t bytes, uint32_
 
 /* ------------------------------------------------------ record helpers */
 
+/* Host worker pool of this process.  No counterpart in the reference, whose
+ * CPU worker counts come from PIPE_D2H_CPU_WORKERS and friends
+ * (secure_infer.cpp:2568-2577).  Ranks that share a host (LOCAL_WORLD_SIZE >
+ * 1) split the CPU affinity set into equal disjoint slices (slice LOCAL_RANK)
+ * and pin their OpenSSL workers to it; a lone rank uses every allowed CPU.
+ * Writes the worker count to *threads (the calling thread encrypts as well),
+ * up to max_cpus CPU ids of the slice to cpus, and 1 to *pinned when the
+ * workers are pinned.  Returns the slice's CPU count, or -1 when threads is
+ * null.  SECURE_INFER_CRYPTO_THREADS overrides the worker count and
+ * SECURE_INFER_PIN_THREADS=0/1 the pinning. */
+int secure_infer_host_pool_info(uint32_t* threads, int32_t* cpus, uint32_t max_cpus, uint32_t* pinned);
+
 /* Next transfer ticket (secure_infer.cpp:262-272); never 0.  Tickets handed
  * out here or by secure_infer_h2d_encrypt_records are redeemable once by a
  * pre-encrypted reload; a replayed or never-issued ticket is rejected. */

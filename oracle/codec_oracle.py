@@ -8,6 +8,8 @@ Restated from (paths relative to the reference project):
   * ``settings`` / ``layer_bits``  -- secure_infer/kv_offload/transport_codec.py:9-19
   * ``encode``                      -- secure_infer/kv_offload/transport_codec.py:22-42
   * ``decode_into``                 -- secure_infer/kv_offload/optimized_decode.py:5-27
+  * ``encode_torch`` / ``decode_into_torch`` -- the same two steps with the
+    reference's torch CPU ops (the CPU baseline's codec, multi-threaded by torch)
 
 Layout of one bf16 KV slice: ``[block][token=128][head][dim]``.  Grouping:
 kind 0 (K) reduces 64 consecutive tokens of one (head, dim) channel; kind 1
@@ -146,3 +148,40 @@ def decode_into(wire: np.ndarray, destination_bf16: np.ndarray, indices, bits: i
     values = (values + offset.reshape(pshape)).astype(np.float32)
     restored = f32_to_bf16(values.reshape(b, tokens, heads, dim))
     destination_bf16[np.asarray(indices, dtype=np.int64)] = restored
+
+
+def decode_into_torch(wire, destination, indices, bits: int, kind: int, qbytes: int, sbytes: int,
+                      temporary=None):
+    """optimized_decode.py:5-27 with torch CPU ops, as the reference runs it:
+    int8 q -> fp32; int4 hi = floor(p / 16), lo = p - 16 hi, interleaved lo,
+    hi; then in place v *= scale, v += offset (two fp32 roundings), RNE to
+    the destination's bf16 and ``index_copy_`` along the block axis.
+    wire: uint8 tensor [b, width]; destination: bf16 tensor [num_blocks, 128,
+    heads, dim]; indices: int64 tensor.  Returns the fp32 work buffer, which a
+    caller may pass back as `temporary`."""
+    import torch
+    b = wire.shape[0]
+    _, tokens, heads, dim = destination.shape
+    total = b * tokens * heads * dim
+    work = temporary if temporary is not None and temporary.numel() >= total else \
+        torch.empty(total, dtype=torch.float32)
+    q = wire[:, :qbytes]
+    full = work[:total].view(b, -1)
+    if bits == 8:
+        full.copy_(q)
+    else:
+        p = q.float()
+        hi = torch.floor(p / 16)
+        torch.stack((p - 16 * hi, hi), dim=-1, out=full.view(b, -1, 2))
+    if kind == 0:
+        shape, pshape = (b, tokens // GROUP, GROUP, heads, dim), (b, tokens // GROUP, 1, heads, dim)
+    else:
+        shape, pshape = (b, tokens, heads, dim // GROUP, GROUP), (b, tokens, heads, dim // GROUP, 1)
+    params = wire.view(torch.float32)
+    scale = params[:, qbytes // 4:(qbytes + sbytes) // 4].reshape(pshape)
+    offset = params[:, (qbytes + sbytes) // 4:(qbytes + 2 * sbytes) // 4].reshape(pshape)
+    v = full.view(shape)
+    v.mul_(scale)
+    v.add_(offset)
+    destination.index_copy_(0, indices, v.reshape(b, tokens, heads, dim).to(destination.dtype))
+    return work

@@ -48,6 +48,7 @@ HOST_SIGNATURES: dict[str, tuple[list, object]] = {
     "secure_infer_session_shutdown": ([], I32),
     "secure_infer_register_host_range": ([P, SZ], None),
     "secure_infer_register_host_range_ex": ([P, SZ, U32, U32, SZ], None),
+    "secure_infer_host_pool_info": ([ct.POINTER(U32), ct.POINTER(I32), U32, ct.POINTER(U32)], I32),
     "secure_infer_new_transfer_ticket": ([], U64),
     "secure_infer_derive_transfer_iv": ([P, U64, U64, P], I32),
     "secure_infer_build_gcm_aad": ([P, SZ, ct.c_uint8, U64, U64, P], I32),
@@ -134,6 +135,16 @@ def lib() -> ct.CDLL:
                 fn.restype = res
         _lib = handle
     return _lib
+
+
+def host_pool_info() -> dict:
+    """This rank's host worker pool: OpenSSL worker threads (the calling
+    thread encrypts as well), the CPUs of the rank's slice and whether the
+    workers are pinned to them."""
+    threads, pinned = U32(), U32()
+    cpus = (I32 * 1024)()
+    n = lib().secure_infer_host_pool_info(ct.byref(threads), cpus, 1024, ct.byref(pinned))
+    return {"threads": int(threads.value), "cpus": list(cpus[:max(0, min(n, 1024))]), "pinned": bool(pinned.value)}
 
 
 def exported_symbols() -> list[str]:

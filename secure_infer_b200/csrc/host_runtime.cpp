@@ -28,6 +28,8 @@
 #include "../../include/secure_infer.h"
 
 #include <openssl/evp.h>
+#include <pthread.h>
+#include <sched.h>
 #include <openssl/rand.h>
 #include <openssl/crypto.h>
 
@@ -141,11 +143,28 @@ void build_aad(const void* host_ptr, size_t bytes, uint8_t direction, uint64_t t
 }
 
 // ---------------------------------------------------------------- worker pool
+// Restricts the calling thread to `cpus` (best effort: a failure leaves the
+// thread where it was).
+void pin_self(const std::vector<int>& cpus)
+{
+    cpu_set_t set;
+    CPU_ZERO(&set);
+    for (int c : cpus)
+        if (c >= 0 && c < CPU_SETSIZE) CPU_SET(c, &set);
+    if (CPU_COUNT(&set) > 0) pthread_setaffinity_np(pthread_self(), sizeof(set), &set);
+}
+
 class Pool {
 public:
-    explicit Pool(unsigned n)
+    // n workers; with a non-empty `pin`, worker i runs on pin[(i + 1) % size]
+    // (pin[0] is left to the calling thread, which works too).
+    Pool(unsigned n, const std::vector<int>& pin)
     {
-        for (unsigned i = 0; i < n; ++i) threads_.emplace_back([this] { run(); });
+        for (unsigned i = 0; i < n; ++i)
+            threads_.emplace_back([this, i, pin] {
+                if (!pin.empty()) pin_self({pin[(i + 1) % pin.size()]});
+                run();
+            });
     }
     ~Pool()
     {
@@ -226,17 +245,70 @@ private:
     bool stop_ = false;
 };
 
-unsigned pool_threads()
+// Host cores of this rank.  Ranks that share a host (LOCAL_WORLD_SIZE > 1, as
+// torchrun sets it) split the process's CPU affinity set into disjoint equal
+// slices, rank LOCAL_RANK taking slice LOCAL_RANK, so that N ranks start N
+// small OpenSSL pools instead of N pools as large as the host.  One rank alone
+// uses every allowed CPU.  SECURE_INFER_CRYPTO_THREADS overrides the worker
+// count, SECURE_INFER_PIN_THREADS=0 turns pinning off (=1 pins a lone rank too).
+struct PoolPlan {
+    unsigned threads = 0;
+    std::vector<int> cpus;   // this rank's slice, in CPU order
+    bool pinned = false;
+};
+
+unsigned env_unsigned(const char* name, unsigned fallback)
 {
-    if (const char* v = std::getenv("SECURE_INFER_CRYPTO_THREADS")) return static_cast<unsigned>(std::max(0, std::atoi(v)));
-    const unsigned hw = std::thread::hardware_concurrency();
-    return hw > 1 ? std::min(hw - 1, 31u) : 0u;
+    const char* v = std::getenv(name);
+    if (v == nullptr || *v == 0) return fallback;
+    const int x = std::atoi(v);
+    return x < 0 ? fallback : static_cast<unsigned>(x);
+}
+
+PoolPlan make_pool_plan()
+{
+    PoolPlan plan;
+    std::vector<int> all;
+    cpu_set_t set;
+    CPU_ZERO(&set);
+    if (sched_getaffinity(0, sizeof(set), &set) == 0) {
+        for (int c = 0; c < CPU_SETSIZE; ++c)
+            if (CPU_ISSET(c, &set)) all.push_back(c);
+    }
+    if (all.empty()) {
+        const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+        for (unsigned c = 0; c < hw; ++c) all.push_back(static_cast<int>(c));
+    }
+    const unsigned local_world = std::max(1u, env_unsigned("LOCAL_WORLD_SIZE", 1));
+    const unsigned local_rank = std::min(env_unsigned("LOCAL_RANK", 0), local_world - 1);
+    const size_t share = std::max<size_t>(1, all.size() / local_world);
+    const size_t first = std::min(all.size() - 1, static_cast<size_t>(local_rank) * share);
+    plan.cpus.assign(all.begin() + first, all.begin() + std::min(all.size(), first + share));
+    // The calling thread encrypts too, so a slice of c cores gets c - 1 workers.
+    const unsigned fallback = static_cast<unsigned>(std::min<size_t>(plan.cpus.size() - 1, 31));
+    plan.threads = std::getenv("SECURE_INFER_CRYPTO_THREADS") ? env_unsigned("SECURE_INFER_CRYPTO_THREADS", fallback)
+                                                              : fallback;
+    plan.pinned = env_unsigned("SECURE_INFER_PIN_THREADS", local_world > 1 ? 1u : 0u) != 0;
+    return plan;
+}
+
+const PoolPlan& pool_plan()
+{
+    static const PoolPlan plan = make_pool_plan();
+    return plan;
 }
 
 Pool& pool()
 {
-    static Pool p(pool_threads());
+    static Pool p(pool_plan().threads, pool_plan().pinned ? pool_plan().cpus : std::vector<int>{});
     return p;
+}
+
+// Library threads other than the pool's (D2H verifier, lookahead encryptor)
+// stay on the rank's slice when pinning is on.
+void pin_library_thread()
+{
+    if (pool_plan().pinned) pin_self(pool_plan().cpus);
 }
 
 // ---------------------------------------------------------------- OpenSSL
@@ -1009,6 +1081,7 @@ uint8_t* prep_buffer_locked(uint64_t bytes, uint64_t* got)
 
 void prep_worker()
 {
+    pin_library_thread();
     for (;;) {
         std::shared_ptr<Prepared> e;
         {
@@ -1269,6 +1342,7 @@ thread_local std::vector<Submission> t_d2h_group;
 
 void d2h_worker()
 {
+    pin_library_thread();
     std::unique_lock<std::mutex> lock(g_d2h_mu);
     for (;;) {
         g_s.d2h_cv.wait(lock, [] { return g_s.d2h_stop || !g_s.d2h_queue.empty(); });
@@ -1707,6 +1781,16 @@ SI_EXPORT void secure_infer_register_host_range_ex(const void* base, size_t byte
 SI_EXPORT void secure_infer_register_host_range(const void* base, size_t bytes)
 {
     secure_infer_register_host_range_ex(base, bytes, UINT32_MAX, UINT32_MAX, 0);
+}
+
+SI_EXPORT int secure_infer_host_pool_info(uint32_t* threads, int32_t* cpus, uint32_t max_cpus, uint32_t* pinned)
+{
+    if (threads == nullptr) return -1;
+    const PoolPlan& plan = pool_plan();
+    *threads = static_cast<uint32_t>(pool().size());
+    if (pinned) *pinned = plan.pinned ? 1u : 0u;
+    for (uint32_t i = 0; cpus != nullptr && i < max_cpus && i < plan.cpus.size(); ++i) cpus[i] = plan.cpus[i];
+    return static_cast<int>(plan.cpus.size());
 }
 
 SI_EXPORT uint64_t secure_infer_new_transfer_ticket(void)

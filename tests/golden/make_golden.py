@@ -22,6 +22,14 @@ Fixtures:
   codec_*.npz       -- outputs of the reference codec itself, imported from the
                        checkout: transport_codec.encode (:22-42) and
                        optimized_decode.decode_into (:5-27) on CPU torch.
+  codec_shapes.json -- the same reference encode / decode_into at the shapes of
+                       the benchmark configs (4 heads int8 + int4 with 1%
+                       outliers at 8 sigma; 8 heads int8 + int4 at the mixed
+                       split's layers; 1 head int4 over 64 blocks), stored as
+                       SHA-256 digests of the packets and of the decoded
+                       blocks.  The source values are regenerated from the
+                       stored seed (numpy PCG64 normal draws, RNE to bf16) and
+                       pinned by their own digest.
 """
 from __future__ import annotations
 
@@ -165,6 +173,57 @@ def codec(reference: Path):
     (HERE / "layer_bits.json").write_text(json.dumps(bits))
 
 
+# name, KV heads, 1% outliers at 8 sigma, host blocks, (bits, layer) pairs.
+# Encoded host blocks and destination cache blocks are seeded permutations.
+CONFIG_SHAPES = (
+    ("c3_h4", 4, True, 8, 10, ((8, 3), (4, 3))),
+    ("c4_h8", 8, False, 6, 9, ((8, 10), (4, 11))),
+    ("c5_h1", 1, False, 64, 80, ((4, 79),)),
+)
+
+
+def config_source(seed: int, blocks: int, heads: int, outliers: bool) -> np.ndarray:
+    """float32 KV values [blocks, 128, heads, 128]: N(0,1), optionally with 1%
+    of the entries replaced by +-8."""
+    g = np.random.default_rng(seed)
+    x = g.standard_normal((blocks, 128, heads, 128)).astype(np.float32)
+    if outliers:
+        mask = g.random(x.shape) < 0.01
+        sign = np.where(g.random(x.shape) < 0.5, -1.0, 1.0).astype(np.float32)
+        x = np.where(mask, 8.0 * sign, x).astype(np.float32)
+    return x
+
+
+def codec_shapes(reference: Path):
+    import torch
+    tc, od = import_reference_codec(reference)
+    out = {}
+    for i, (name, heads, outliers, blocks, dst_blocks, pairs) in enumerate(CONFIG_SHAPES):
+        seed = 20261202 + i
+        source = torch.from_numpy(config_source(seed, blocks, heads, outliers)).to(torch.bfloat16)
+        g = np.random.default_rng(seed + 1000)
+        n = min(blocks, 5) if blocks < 64 else blocks
+        enc = [int(v) for v in g.permutation(blocks)[:n]]
+        dst = [int(v) for v in g.permutation(dst_blocks)[:n]]
+        entry = dict(seed=seed, heads=heads, outliers=outliers, blocks=blocks, dst_blocks=dst_blocks,
+                     enc_idx=enc, dst_idx=dst,
+                     source_sha256=hashlib.sha256(source.view(torch.int16).numpy().tobytes()).hexdigest(),
+                     cases={})
+        for bits, layer in pairs:
+            for kind in (0, 1):
+                packet, qb, sb = tc.encode(source, torch.tensor(enc), bits, kind, layer=layer)
+                dest = torch.zeros((dst_blocks, 128, heads, 128), dtype=torch.bfloat16)
+                od.decode_into(packet, dest, torch.tensor(dst), bits, kind, qb, sb)
+                rows = packet.numpy()
+                entry["cases"][f"k{kind}_b{bits}"] = dict(
+                    bits=bits, kind=kind, layer=layer, qb=int(qb), sb=int(sb), width=int(rows.shape[1]),
+                    packet_sha256=hashlib.sha256(rows.tobytes()).hexdigest(),
+                    packet_row_sha256=[hashlib.sha256(r.tobytes()).hexdigest()[:16] for r in rows],
+                    dest_sha256=hashlib.sha256(dest[torch.tensor(dst)].view(torch.int16).numpy().tobytes()).hexdigest())
+        out[name] = entry
+    (HERE / "codec_shapes.json").write_text(json.dumps(out, indent=1))
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--reference", required=True, type=Path)
@@ -172,6 +231,7 @@ def main():
     gcm_kat()
     records()
     codec(args.reference)
+    codec_shapes(args.reference)
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".json", ".npz")))
 
 

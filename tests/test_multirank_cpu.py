@@ -76,3 +76,36 @@ def test_two_rank_sessions_are_independent(tmp_path):
     mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     assert sorted(os.listdir(tmp_path)) == ["ok0", "ok1"]
+
+
+def _pool_info_child(local_rank: int, local_world: int):
+    import sys
+    os.environ.update(LOCAL_RANK=str(local_rank), LOCAL_WORLD_SIZE=str(local_world))
+    os.environ.pop("SECURE_INFER_CRYPTO_THREADS", None)
+    os.environ.pop("SECURE_INFER_PIN_THREADS", None)
+    sys.path.insert(0, str(ROOT))
+    from secure_infer_b200 import _native
+    info = _native.host_pool_info()
+    return info, sorted(os.sched_getaffinity(0))
+
+
+def test_ranks_sharing_a_host_split_its_cpus():
+    """Ranks on one host (LOCAL_WORLD_SIZE > 1) size and pin their OpenSSL
+    pools to disjoint equal slices of the CPUs instead of each starting a pool
+    as large as the host; a lone rank uses every CPU, unpinned."""
+    import multiprocessing as mpc
+    ctx = mpc.get_context("spawn")
+    local_world = 2
+    with ctx.Pool(1) as p:
+        alone, cpus = p.apply(_pool_info_child, (0, 1))
+    assert alone["cpus"] == cpus and not alone["pinned"]
+    assert alone["threads"] == min(len(cpus) - 1, 31)
+    slices = []
+    for r in range(local_world):
+        with ctx.Pool(1) as p:
+            info, _ = p.apply(_pool_info_child, (r, local_world))
+        share = max(1, len(cpus) // local_world)
+        assert len(info["cpus"]) == share and info["pinned"]
+        assert info["threads"] == share - 1
+        slices.append(set(info["cpus"]))
+    assert not (slices[0] & slices[1]) or len(cpus) < local_world

@@ -7,7 +7,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, det_bytes, load_codec
+from conftest import GOLDEN, codec_shape_source, codec_shapes, det_bytes, load_codec, sha256
 from oracle import codec_oracle, gcm
 
 
@@ -183,3 +183,46 @@ def test_reciprocal_quantise_matches_division(bits):
     fast = np.where(near, exact, np.rint(y))
     assert np.array_equal(fast, exact)
     assert near.mean() < 1e-3
+
+
+SHAPE_CASES = [(name, tag) for name, e in codec_shapes().items() for tag in e["cases"]]
+
+
+@pytest.mark.parametrize("name,tag", SHAPE_CASES)
+def test_codec_oracle_at_config_shapes(name, tag):
+    """The numpy and torch restatements reproduce the reference's own packets
+    and decode_into output at the benchmark configs' shapes (4 heads with
+    outliers, 8 heads int8 / int4, 1 head int4 over 64 blocks); this is where
+    the K-group index depends on the head count."""
+    torch = pytest.importorskip("torch")
+    e = codec_shapes()[name]
+    c = e["cases"][tag]
+    src = codec_shape_source(e)
+    packet, qb, sb = codec_oracle.encode(src, e["enc_idx"], c["bits"], c["kind"], c["layer"])
+    assert (qb, sb, packet.shape[1]) == (c["qb"], c["sb"], c["width"])
+    assert sha256(packet) == c["packet_sha256"]
+    tpacket, _, _ = codec_oracle.encode_torch(src, e["enc_idx"], c["bits"], c["kind"], c["layer"])
+    assert np.array_equal(tpacket, packet)
+    dest = np.zeros((e["dst_blocks"], 128, e["heads"], 128), np.uint16)
+    codec_oracle.decode_into(packet, dest, e["dst_idx"], c["bits"], c["kind"], qb, sb)
+    assert sha256(dest[e["dst_idx"]]) == c["dest_sha256"]
+    tdest = torch.zeros((e["dst_blocks"], 128, e["heads"], 128), dtype=torch.bfloat16)
+    codec_oracle.decode_into_torch(torch.from_numpy(packet), tdest, torch.tensor(e["dst_idx"]), c["bits"], c["kind"],
+                                   qb, sb)
+    assert np.array_equal(tdest.view(torch.int16).numpy().view(np.uint16), dest)
+
+
+@pytest.mark.parametrize("heads", [1, 2])
+@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("bits", [8, 4])
+def test_codec_torch_decode_bit_exact_vs_reference(heads, kind, bits):
+    """The torch restatement of decode_into (the CPU baseline's decode) gives
+    the reference's own output."""
+    torch = pytest.importorskip("torch")
+    g = load_codec(heads)
+    tag = f"k{kind}_b{bits}"
+    dest = torch.zeros((6, 128, heads, 128), dtype=torch.bfloat16)
+    codec_oracle.decode_into_torch(torch.from_numpy(g[f"packet_{tag}"]), dest, torch.from_numpy(g["dst_idx"]), bits,
+                                   kind, int(g[f"qb_{tag}"]), int(g[f"sb_{tag}"]))
+    got = dest.view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got[g["dst_idx"]], g[f"dest_{tag}"])
