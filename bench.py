@@ -408,25 +408,38 @@ MODEL_SHAPES = {
 }
 
 
-def attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_wait, suffix: int, reps: int = 3):
+def attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, suffix: int, reps: int = 3):
     """Reload hidden behind attention (the per-layer gate of the reference's
     RuntimeWorker.wait_for_layer_load, reuse/connector.py:378-410).
 
-    Per layer l, a load stream reloads l while a compute stream, gated on
-    l's reload (a CUDA event after the device-resident reload; the library's
-    secure_infer_layer_ready_wait after the end-to-end one), runs a stand-in
-    for the suffix prefill of l over the reloaded paged cache:
+    A compute stream runs, per layer l, a stand-in for the suffix prefill of l
+    over the reloaded paged cache, gated on l's reload:
       attention: gather of l's K/V prefix blocks through the block table, then
                  GQA SDPA of `suffix` query tokens over prefix + suffix keys
                  (no mask);
       layer:     the same attention plus the layer's QKV / O projections and
                  SwiGLU MLP GEMMs for the suffix tokens (random bf16 weights,
                  one set shared by all layers).
+    Two reload sources:
+      device_resident_reload: records already in HBM, secure_infer_reload_records
+                 per layer on a load stream, the compute stream waiting on a
+                 CUDA event per layer; both streams fed ahead of the device
+                 (a device sleep holds them while the host enqueues).
+      e2e_reload: the drop-in connector (secure_infer_b200.connector.
+                 LayerwiseReloader, the reference's RuntimeWorker): a fetch
+                 thread reloads every layer from host plaintext with the
+                 next layer announced ahead, an observer thread waits for each
+                 layer's authentication, and the model thread calls
+                 wait_for_layer_load(l) before the layer's compute.
     exposed_us_per_layer = (overlapped time - compute-alone time) / layers;
     pipeline_finish_ms is the reference's own estimate of the overlapped time
     (reuse/completion_model.py:4-5: max(load + compute/L, compute + load/L)).
     The stand-in is measurement scaffolding, not part of the path."""
+    import itertools
+
     import torch.nn.functional as F
+
+    from secure_infer_b200.connector import LayerwiseReloader
     L, H, B = cfg["layers"], cfg["heads"], cfg["blocks"]
     m = MODEL_SHAPES[cfg["model"]]
     tp = cfg["tp"]
@@ -446,7 +459,6 @@ def attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_
     kbuf, vbuf = rnd(P + S, H, D), rnd(P + S, H, D)
     ls, cs = torch.cuda.Stream(), torch.cuda.Stream()
     lsp = ct.c_void_p(ls.cuda_stream)
-    csp = ct.c_void_p(cs.cuda_stream)
 
     def attend(layer, q):
         torch.index_select(cache[layer][0], 0, table, out=kbuf[:P].view(B, 128, H, D))
@@ -467,9 +479,9 @@ def attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_
         (F.silu(gu[:, :ffn]) * gu[:, ffn:]) @ w_d
 
     def timed(enqueue, sleep_s=0.02):
-        """Device time of what `enqueue` puts on the two streams; both start
-        together behind a device sleep on the compute stream, so the host's
-        enqueue runs ahead of the device (sleep_s = 0: host-paced)."""
+        """Device time of what `enqueue` puts on the streams, from a start
+        event on the compute stream to its end; sleep_s > 0 first holds the
+        device so the host enqueues ahead (sleep_s = 0: host-paced)."""
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         if sleep_s:
@@ -487,31 +499,41 @@ def attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_
         return statistics.median(fn() for _ in range(reps))
 
     events = [torch.cuda.Event() for _ in range(L)]
+    names = [f"model.layers.{layer}.self_attn.attn" for layer in range(L)]
+    reloader = LayerwiseReloader(names, cache, payload, mode=cfg["codec"])
+    requests = itertools.count()
+    src_blocks, dst_blocks = list(range(B)), list(perm[:B])
 
     def dev_reload_all():
         for layer in range(L):
             dev_reload(layer, lsp)
 
-    def e2e_reload_all():
-        for layer in range(L):
-            e2e_reload(layer, lsp)
+    def connector_run(fn):
+        def enqueue():
+            with torch.cuda.stream(cs):
+                reloader.start_load(next(requests), src_blocks, dst_blocks)
+                for layer in range(L):
+                    reloader.wait_for_layer_load(names[layer])
+                    if fn is not None:
+                        fn(layer)
+            reloader.get_finished()
+        return enqueue
 
     out = {"suffix_tokens": S, "prefix_tokens": P, "layers": L,
            "stand_in": f"per layer: {qh} query heads x {S} suffix tokens over {P} + {S} keys of {H} KV heads "
                        f"(GQA SDPA after a block-table gather); 'layer' adds the QKV/O projections and the "
                        f"SwiGLU MLP ({hid} -> {ffn} -> {hid}) GEMMs",
-           "gate": "compute stream waits on each layer's reload (CUDA event after secure_infer_reload_records; "
-                   "secure_infer_layer_ready_wait after secure_infer_h2d_reload_layer)"}
-    # Warm up every piece (kernels, SDPA backend, cuBLAS heuristics).
+           "gate": "device-resident: CUDA event per layer after secure_infer_reload_records; e2e: "
+                   "LayerwiseReloader.wait_for_layer_load (host-observed authentication, then a device-side "
+                   "wait on the layer's event)"}
+    # Warm up every piece (kernels, SDPA backend, cuBLAS heuristics, connector threads).
     for fn in (attention, full_layer):
         with torch.cuda.stream(cs):
             fn(0)
     timed(dev_reload_all)
-    timed(e2e_reload_all, 0)
-    assert e2e_wait() == 0
+    timed(connector_run(None), 0)
     reload_dev_ms = median(lambda: timed(dev_reload_all))
-    reload_e2e_ms = median(lambda: timed(e2e_reload_all, 0))
-    assert e2e_wait() == 0
+    reload_e2e_ms = median(lambda: timed(connector_run(None), 0))
     for name, fn in (("attention", attention), ("layer", full_layer)):
         def compute_all():
             with torch.cuda.stream(cs):
@@ -526,30 +548,23 @@ def attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_
                 with torch.cuda.stream(cs):
                     fn(layer)
 
-        def e2e_overlap():
-            for layer in range(L):
-                e2e_reload(layer, lsp)
-                assert lib.secure_infer_layer_ready_wait(layer, csp) == 0
-                with torch.cuda.stream(cs):
-                    fn(layer)
-
-        compute_ms = median(lambda: timed(compute_all))
+        compute_dev_ms = median(lambda: timed(compute_all))
+        compute_host_ms = median(lambda: timed(compute_all, 0))
         dev_ms = median(lambda: timed(dev_overlap))
-        e2e_ms = median(lambda: timed(e2e_overlap, 0))
-        assert e2e_wait() == 0
+        e2e_ms = median(lambda: timed(connector_run(fn), 0))
 
-        def row(load_ms, both_ms):
+        def row(load_ms, both_ms, compute_ms):
             finish = max(load_ms + compute_ms / L, compute_ms + load_ms / L)
-            return {"reload_alone_ms": round(load_ms, 3), "overlapped_ms": round(both_ms, 3),
+            return {"reload_alone_ms": round(load_ms, 3), "compute_alone_ms": round(compute_ms, 3),
+                    "overlapped_ms": round(both_ms, 3),
                     "exposed_us_per_layer": round(max(0.0, both_ms - compute_ms) * 1e3 / L, 2),
                     "pipeline_finish_ms": round(finish, 3)}
 
-        out[name] = {"compute_alone_ms": round(compute_ms, 3),
-                     "compute_us_per_layer": round(compute_ms * 1e3 / L, 2),
-                     "device_resident_reload": row(reload_dev_ms, dev_ms),
-                     "e2e_reload": row(reload_e2e_ms, e2e_ms)}
+        out[name] = {"compute_us_per_layer": round(compute_dev_ms * 1e3 / L, 2),
+                     "device_resident_reload": row(reload_dev_ms, dev_ms, compute_dev_ms),
+                     "e2e_reload": row(reload_e2e_ms, e2e_ms, compute_host_ms)}
+    reloader.close()
     return out
-
 
 
 def run_gpu(args, cfg):
@@ -615,42 +630,66 @@ def run_gpu(args, cfg):
                                                    codec_arg[layer], sp, sp) == 0
         return 2 * L
 
+    def device_step_inline():
+        """The same reload with no keystream buffer (raw records): per layer
+        one C-ABI call = one fused kernel that computes the keystream itself."""
+        for layer in range(L):
+            assert lib.secure_infer_reload_records(layer, rec_ptr[layer], strides[layer], count[layer], n,
+                                                   tickets[layer], dst_all[layer], None, st_ptr[layer],
+                                                   None, sp, sp) == 0
+        return L
+
     def barrier():
         if dist is not None:
             dist.barrier()
 
     # ---- device-resident throughput (value) ----
-    for _ in range(args.warmup):
-        device_step()
-    torch.cuda.synchronize()
-    assert int(status.min().item()) == 1, "authentication failed during warm-up"
-    # correctness spot check against the host payload (raw configs)
-    if bits[0] == 0:
-        assert torch.equal(cache[0][0][perm[0]].cpu(), payload[0][0][0])
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     gpu_id = "GPU-" + str(torch.cuda.get_device_properties(local).uuid)
-    barrier()
-    torch.cuda.synchronize()
-    launches = 0
-    with ClockSampler(gpu_id) as clocks:
-        start.record(stream)
-        for k in range(args.steps):
-            launches += device_step()
-        end.record(stream)
-        torch.cuda.synchronize()
-    barrier()
-    dev_ms = max_over_ranks(start.elapsed_time(end), dist)
-    assert int(status.min().item()) == 1
     wire = sum(count[layer] * n for layer in range(L))
     out_bytes = L * n * 128 * H * 128 * 2
     algo = wire + out_bytes
-    ms_per_step = dev_ms / args.steps
+
+    def timed_steps(step):
+        """Device time of args.steps steps (after args.warmup untimed ones),
+        max over ranks; every rank takes the same barriers."""
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        assert int(status.min().item()) == 1, "authentication failed during warm-up"
+        if bits[0] == 0:   # spot check against the host payload (raw configs)
+            assert torch.equal(cache[0][0][perm[0]].cpu(), payload[0][0][0])
+        status.zero_()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        launches = 0
+        with ClockSampler(gpu_id) as clk:
+            start.record(stream)
+            for _ in range(args.steps):
+                launches += step()
+            end.record(stream)
+            torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(start.elapsed_time(end), dist)
+        assert int(status.min().item()) == 1
+        return ms / args.steps, launches, clk
+
+    paths = {"prefetched_keystream": device_step}
+    if all(b == 0 for b in bits):
+        paths["inline_keystream"] = device_step_inline
+    timings = {name: timed_steps(fn) for name, fn in paths.items()}
+    best = min(timings, key=lambda name: timings[name][0])
+    ms_per_step, launches, clocks = timings[best]
     value = world * algo / (ms_per_step * 1e-3) / 1e9
+    path_values = {name: round(world * algo / (t[0] * 1e-3) / 1e9, 3) for name, t in timings.items()}
 
     # ---- per-kernel device time (roofline) ----
     prof = kernel_profile(lib, torch, device_step, L)
     ks_us = prof["gcm_layer_ctr_kernel"][0]
     vf_us = prof["gcm_layer_verify_kernel"][0]
+    inline_us = None
+    if "inline_keystream" in paths:
+        inline_us = kernel_profile(lib, torch, device_step_inline, L)["gcm_layer_verify_inline_kernel"][0]
     assert int(status.min().item()) == 1
 
     # ---- end to end through the C ABI from host plaintext ----
@@ -712,29 +751,32 @@ def run_gpu(args, cfg):
 
     overlap = None
     if world == 1 and args.suffix > 0:
+        # The device-resident reload of the faster path.
+        ks_arg = None if best == "inline_keystream" else ks_ptr
+
         def dev_reload(layer, lsp):
             assert lib.secure_infer_reload_records(layer, rec_ptr[layer], strides[layer], count[layer], n,
-                                                   tickets[layer], dst_all[layer], ks_ptr, st_ptr[layer],
+                                                   tickets[layer], dst_all[layer], ks_arg, st_ptr[layer],
                                                    codec_arg[layer], lsp, lsp) == 0
 
-        def e2e_reload(layer, lsp):
-            assert lib.secure_infer_h2d_reload_layer(layer, src_all[layer], dst_all[layer], n, count[layer],
-                                                     codec_arg[layer], 0, None, lsp) == 0
-
-        def e2e_wait():
-            return max(lib.secure_infer_recovery_wait_layer_authentication(layer) != 0 for layer in range(L))
-
-        overlap = attention_overlap(torch, lib, cfg, cache, perm, dev_reload, e2e_reload, e2e_wait, args.suffix)
+        overlap = attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, args.suffix)
         assert int(status.min().item()) == 1
 
     result = None
     if rank == 0:
         ks_mean, vf_mean = ks_us, vf_us
-        dominant = "gcm_layer_verify_kernel" if vf_mean >= ks_mean else "gcm_layer_ctr_kernel"
+        per_kernel = {"gcm_layer_ctr_kernel": ks_mean, "gcm_layer_verify_kernel": vf_mean}
+        if inline_us is not None:
+            per_kernel["gcm_layer_verify_inline_kernel"] = inline_us
+        # The dominant kernel of the path that gave `value`.
+        if best == "inline_keystream":
+            dominant = "gcm_layer_verify_inline_kernel"
+        else:
+            dominant = "gcm_layer_verify_kernel" if vf_mean >= ks_mean else "gcm_layer_ctr_kernel"
         layer_algo = algo / L
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
         hbm_peak = peaks.get("hbm_gbs", 6650.0)
-        dom_us = vf_mean if dominant == "gcm_layer_verify_kernel" else ks_mean
+        dom_us = per_kernel[dominant]
         achieved = layer_algo / (dom_us * 1e-6) / 1e9
         traffic = NCU_TRAFFIC_BYTES.get((args.config, H, dominant))
         # Binding pipe: shared-memory wavefronts (1 per SM per clock) at the
@@ -743,12 +785,12 @@ def run_gpu(args, cfg):
         sm_hz = (clk["sm_mhz"] or clk["sm_max_mhz"] or 1965.0) * 1e6
         sms = torch.cuda.get_device_properties(local).multi_processor_count
         payload_blocks = sum((count[layer] + 15) // 16 for layer in range(L)) * n / L
-        # verify hashes AAD (4) + payload + length block; keystream adds E_K(J0)
-        blocks_per_layer = {"gcm_layer_verify_kernel": payload_blocks + 5 * n, "gcm_layer_ctr_kernel": payload_blocks + n}
-        smem = {}
-        for name, us in (("gcm_layer_verify_kernel", vf_mean), ("gcm_layer_ctr_kernel", ks_mean)):
-            wf = SMEM_WAVEFRONTS_PER_BLOCK[name] * blocks_per_layer[name]
-            smem[name] = round(wf / (us * 1e-6 * sms * sm_hz), 4)
+        # GHASH covers AAD (4) + payload + length block; AES covers the
+        # payload + E_K(J0).  The fused inline kernel does both.
+        wavefronts = {"gcm_layer_verify_kernel": 2.0 * (payload_blocks + 5 * n),
+                      "gcm_layer_ctr_kernel": 5.5 * (payload_blocks + n),
+                      "gcm_layer_verify_inline_kernel": 2.0 * (payload_blocks + 5 * n) + 5.5 * (payload_blocks + n)}
+        smem = {name: round(wavefronts[name] / (us * 1e-6 * sms * sm_hz), 4) for name, us in per_kernel.items()}
         result = {
             "metric": "Verified KV reload GB/s/GPU (AES-GCM+dequant+scatter); per-layer reload us",
             "value": round(value, 3),
@@ -790,19 +832,21 @@ def run_gpu(args, cfg):
                                       "(secure_infer_h2d_prepare_layer); encryption stays in the timed region"},
             "gpu_launches": launches,
             "attention_overlap": overlap,
-            "kernels": {"gcm_layer_ctr_kernel_us_per_layer": round(ks_mean, 2),
-                        "gcm_layer_verify_kernel_us_per_layer": round(vf_mean, 2),
+            "value_by_path": path_values,
+            "value_path": best,
+            "kernels": {**{f"{name}_us_per_layer": round(us, 2) for name, us in per_kernel.items()},
                         "timing": "the library's CUDA events around each launch (secure_infer_kernel_profile_*), "
                                   "one step queued behind a device sleep so host enqueue time is excluded"},
             "roofline": {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 2),
                          "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                          "traffic": traffic,
                          "smem_pipe_frac": smem,
-                         "note": "achieved = per-layer algorithmic bytes (ciphertext in + bf16 out) / dominant "
-                                 "kernel time; peak = measured HBM copy bandwidth (of measured). The binding "
-                                 "resource is the shared-memory pipe (AES T-tables, GHASH byte tables): "
-                                 "smem_pipe_frac = algorithmic wavefronts (GHASH 2, AES 5.5 per 16-byte block) / "
-                                 "(kernel time x SMs x sampled SM clock), 1 wavefront per SM per clock peak."},
+                         "note": "achieved = per-layer algorithmic bytes (ciphertext in + bf16 out) / the dominant "
+                                 "kernel's time on the path that gave `value`; peak = measured HBM copy bandwidth "
+                                 "(of measured). The binding resource is the shared-memory pipe (AES T-tables, "
+                                 "GHASH byte tables): smem_pipe_frac = algorithmic wavefronts (GHASH 2, AES 5.5 per "
+                                 "16-byte block; the inline kernel both) / (kernel time x SMs x sampled SM clock), "
+                                 "1 wavefront per SM per clock peak."},
             "clocks": clocks.summary(),
         }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

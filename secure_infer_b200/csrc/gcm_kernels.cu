@@ -1059,6 +1059,182 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
     }
 }
 
+// Fused verify with the keystream computed inside the kernel, for raw,
+// 16-byte aligned records already in device memory (nothing to overlap a
+// keystream prefetch with).  Shared memory holds what the main loop reads:
+// the four AES T-table replicas and round keys (128 KiB, as the keystream
+// kernel) and the H^32 byte tables (64 KiB); the lane, quarter and join
+// tables of the segment combine are read through L1 from the schedule, once
+// per segment.  Segments, lanes and the combine are those of
+// gcm_layer_verify_kernel.  An interior step of a warp loads 16 bytes of
+// ciphertext per lane two steps ahead, encrypts the lane's counter block,
+// XORs, stores and takes one Horner step; the AES lookups of one warp fill
+// the load latency of the others, and no keystream crosses HBM.  The warp
+// that joins a record's partials computes E_K(J0) itself.
+constexpr uint32_t kInlineThreads = 512;
+constexpr size_t kInlineSmem = kCtrTableBytes + 256 + kGhashSmem;
+
+template <int kCap>
+__global__ void __launch_bounds__(kInlineThreads, 1)
+    gcm_layer_verify_inline_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint4* gtab = reinterpret_cast<uint4*>(smem + kCtrTableBytes + 256);
+    const GcmSchedule* __restrict__ S = L.h.sched;
+    const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u, quarter = lane >> 3;
+    const uint32_t seg_steps = L.h.seg_steps;
+    __shared__ __align__(8) uint64_t gtab_bar;
+    if (tid == 0) {
+        mbar_init_expect(&gtab_bar, 65536u);
+        bulk_g2s(gtab, S->byte32, 65536u, &gtab_bar);
+    }
+    fill_aes4_smem(smem, S);
+    __syncthreads();
+    // Records and destinations are touched only after the previous grid in
+    // the stream has completed.
+    allow_dependent_launch();
+    grid_dependency_wait();
+    // If the table copy never completes, every partial is poisoned and the
+    // records fail closed (status 0, output zeroed) instead of hanging.
+    const bool gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
+    const uint32_t* rk = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
+    const Aes4Tables T = aes4_view(smem);
+
+    const uint64_t count = L.h.count;
+    const int64_t seg_blocks = 32 * static_cast<int64_t>(seg_steps);
+    const int64_t a_blk = 4;   // 64-byte AAD
+    const int64_t n_blk = static_cast<int64_t>((count + 15) >> 4);
+    const int64_t m = a_blk + n_blk + 1;
+    const uint32_t nseg = L.h.nseg;
+    const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * seg_blocks;
+    const uint64_t tag_off = ((count + 31) & ~uint64_t(31)) ? ((count + 31) & ~uint64_t(31)) : 32;
+    const uint32_t total = nseg * L.h.n;
+    const uint4 len_blk = len_block_le(64, count);
+    constexpr uint32_t kWarps = kInlineThreads / 32;
+    constexpr int kPf = 2;
+
+    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * kWarps) {
+        const uint32_t r = w / nseg, k = w - r * nseg;
+        const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
+        const uint8_t* aad = in + tag_off + 32;
+        uint8_t* out = L.rec[r].dst;
+        uint32_t iv[4];
+        layer_iv(L.h.iv0, L.rec[r].ticket, iv);
+        const int64_t seg_end = len0 + static_cast<int64_t>(k) * seg_blocks;
+        const int64_t seg_len = k == 0 ? len0 : seg_blocks;
+        const int J = static_cast<int>((seg_len + 31) / 32);
+        const int64_t base = seg_end - static_cast<int64_t>(J) * 32;
+        // Interior steps [lo, hi): every lane on a full payload block.
+        const int64_t n_full = static_cast<int64_t>(count >> 4);
+        const int64_t lo_num = a_blk - base, hi_num = a_blk + n_full - 32 - base;
+        const int j_lo = lo_num <= 0 ? 0 : static_cast<int>((lo_num + 31) / 32);
+        const int j_hi = hi_num < 0 ? 0 : (hi_num / 32 + 1 < J ? static_cast<int>(hi_num / 32 + 1) : J);
+        const int lo = j_lo < J ? j_lo : J;
+        const int hi = j_hi > lo ? j_hi : lo;
+        const int64_t c0 = base + lane - a_blk;   // payload block of step 0 (negative on the AAD)
+        uint4 Y = zero4();
+
+        // Any step through the general path: AAD, payload, partial and length
+        // blocks in any mix.
+        auto general = [&](int j) {
+            const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
+            uint4 x = zero4();
+            if (j < J && i >= 0) {
+                if (i < a_blk) {
+                    x = ldg16(aad + 16 * i);
+                } else if (i < a_blk + n_blk) {
+                    const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
+                    const uint64_t avail = count - off;
+                    x = avail >= 16 ? ldg16(in + off) : load_partial16(in + off, avail);
+                    const uint4 ks = aes128_encrypt_t4(ctr_block_le(iv, static_cast<uint64_t>(i - a_blk)), T, rk);
+                    store_block(out + off, xor4(x, ks), avail, true);
+                } else {
+                    x = len_blk;
+                }
+            }
+            Y = xor4(gf_mul_byte8(Y, gtab, rep), x);
+        };
+
+        if (lane == 0 && hi > lo)
+            l2_prefetch_bulk(in + (base - a_blk) * 16 + 512ll * lo, static_cast<uint32_t>(hi - lo) * 512u);
+        uint4 xq[kPf];
+#pragma unroll
+        for (int u = 0; u < kPf; ++u)
+            if (lo + u < hi) xq[u] = ldg16(in + static_cast<uint64_t>(c0 + 32ll * (lo + u)) * 16u);
+#pragma unroll 1
+        for (int j = 0; j < lo; ++j) general(j);
+#pragma unroll 1
+        for (int j0 = lo; j0 < hi; j0 += kPf) {
+#pragma unroll
+            for (int u = 0; u < kPf; ++u) {
+                const int j = j0 + u;
+                if (j >= hi) break;
+                const uint4 x0 = xq[u];
+                if (j + kPf < hi) xq[u] = ldg16(in + static_cast<uint64_t>(c0 + 32ll * (j + kPf)) * 16u);
+                const uint64_t c = static_cast<uint64_t>(c0 + 32ll * j);
+                const uint4 ks = aes128_encrypt_t4(ctr_block_le(iv, c), T, rk);
+                *reinterpret_cast<uint4*>(out + c * 16u) = xor4(x0, ks);
+                Y = xor4(gf_mul_byte8(Y, gtab, rep), x0);
+            }
+        }
+#pragma unroll 1
+        for (int j = hi; j < J; ++j) general(j);
+
+        // Two-stage lane combine (tables through L1).
+        if (!gtab_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
+        Y = gf_mul_table<8, true>(Y, S->lane8, rep);                    // * H^(8 - r)
+        Y = xor4(Y, shfl_xor4(Y, 1));
+        Y = xor4(Y, shfl_xor4(Y, 2));
+        Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
+        if (quarter != 3) Y = gf_mul_table<1, true>(Y, S->tab[tab_pow_small(8 * (3 - static_cast<int>(quarter)))], 0);
+        Y = xor4(Y, shfl_xor4(Y, 8));
+        const uint4 part = xor4(Y, shfl_xor4(Y, 16));
+
+        __threadfence();
+        __syncwarp();
+        uint32_t last = 0;
+        if (lane == 0) {
+            L.h.partials[w] = part;
+            __threadfence();
+            last = atomicAdd(&L.h.counters[r], 1u) == nseg - 1 ? 1u : 0u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        // Join the record's partials as gcm_layer_verify_kernel does: level b
+        // of the lane tree multiplies by H^(L 2^b) (b = 0 from the schedule,
+        // b = 1..4 from the session join tables), chunks of 32 by H^(32 L).
+        uint4 acc = zero4();
+        const uint32_t first = nseg - (nseg - 1) / 32 * 32;
+        for (uint32_t k0 = 0; k0 < nseg;) {
+            const uint32_t cnt = k0 == 0 ? first : 32;
+            const uint32_t pad = 32 - cnt;
+            uint4 v = lane >= pad ? __ldcg(&L.h.partials[r * nseg + k0 + lane - pad]) : zero4();
+#pragma unroll
+            for (int b = 0; b < 5; ++b) {
+                const uint4 left = shfl_up4(v, 1u << b);
+                const uint32_t grp = (2u << b) - 1u;
+                const uint4* tb = b == 0 ? S->tab[tab_pow_32k(static_cast<int>(seg_steps))] : L.h.join_pow + 512 * (b - 1);
+                if ((lane & grp) == grp) v = xor4(gf_mul_table<1, true>(left, tb, 0), v);
+            }
+            v = make_uint4(__shfl_sync(0xffffffffu, v.x, 31), __shfl_sync(0xffffffffu, v.y, 31),
+                           __shfl_sync(0xffffffffu, v.z, 31), __shfl_sync(0xffffffffu, v.w, 31));
+            acc = k0 == 0 ? v : xor4(gf_mul_warp<true>(acc, L.h.join_pow + 4 * 512, lane), v);
+            k0 += cnt;
+        }
+        const uint4 mask = aes128_encrypt_t4(j0_block_le(iv), T, rk);
+        const bool ok = equal4(xor4(acc, mask), ldg16(in + tag_off));
+        if (lane == 0) {
+            L.h.status[r] = ok ? 1u : 0u;
+            L.h.counters[r] = 0u;
+        }
+        if (!ok) {
+            for (uint64_t off = static_cast<uint64_t>(lane) * 16u; off < count; off += 512u)
+                store_block(out + off, zero4(), count - off, true);
+        }
+    }
+}
+
 // ----------------------------------------------------------------------------
 // Writeback quantisation (transport_codec.py:22-42), one thread per group.
 // ----------------------------------------------------------------------------
@@ -1495,7 +1671,8 @@ const char* kernel_kind_name(uint32_t kind)
 {
     static const char* names[kKernKinds] = {"gcm_layer_ctr_kernel", "gcm_layer_verify_kernel", "gcm_layer_encrypt",
                                             "kv_encode_kernel", "gcm_segment_kernel", "gcm_ctr_kernel",
-                                            "gcm_schedule_kernel", "auth_gate_kernel"};
+                                            "gcm_schedule_kernel", "auth_gate_kernel",
+                                            "gcm_layer_verify_inline_kernel"};
     return kind < kKernKinds ? names[kind] : nullptr;
 }
 
@@ -1692,6 +1869,24 @@ int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t 
                                             layer_threads(kLayerVerifyRaw), kLayerSmem, grid, set_small[dev & 63], stream, 1);
     return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyRaw>, h, rec,
                                         layer_threads(kLayerVerifyRaw), kLayerSmem, grid, set_large[dev & 63], stream, 1);
+}
+
+int launch_layer_verify_inline(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
+{
+    if (h.n == 0) return cudaSuccess;
+    if (h.n > static_cast<uint32_t>(kLayerCapLarge) || h.join_pow == nullptr || h.seg_steps < 1 ||
+        h.seg_steps > static_cast<uint32_t>(kMaxWarpSegSteps) || h.unaligned || h.codec.bits)
+        return cudaErrorInvalidValue;
+    static bool set_small[64], set_large[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint32_t warps = kInlineThreads / 32;
+    const uint32_t grid = (h.nseg * h.n + warps - 1) / warps;
+    if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
+        return layer_launch<kLayerCapSmall>(kKernLayerVerifyInline, gcm_layer_verify_inline_kernel<kLayerCapSmall>, h,
+                                            rec, kInlineThreads, kInlineSmem, grid, set_small[dev & 63], stream, 1);
+    return layer_launch<kLayerCapLarge>(kKernLayerVerifyInline, gcm_layer_verify_inline_kernel<kLayerCapLarge>, h, rec,
+                                        kInlineThreads, kInlineSmem, grid, set_large[dev & 63], stream, 1);
 }
 
 int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)

@@ -149,12 +149,15 @@ void layer_segments_for(uint64_t count, uint32_t n, uint32_t codec_bits, uint32_
 int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
+// Fused verify with the AES keystream computed in the kernel (h.ks unused):
+// raw payloads (codec.bits 0), 16-byte aligned records and destinations.
+int launch_layer_verify_inline(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 
 // Kernel profile: while enabled, every launch below is bracketed by timing
 // events on its stream; collect() sums device time and launches per kind.
 enum KernelKind : uint32_t {
     kKernLayerCtr = 0, kKernLayerVerify, kKernLayerEncrypt, kKernEncode, kKernSegment, kKernCtr, kKernSchedule,
-    kKernAuthGate, kKernKinds
+    kKernAuthGate, kKernLayerVerifyInline, kKernKinds
 };
 void profile_enable(bool on);
 int profile_collect(double* total_us, uint64_t* launches, uint32_t kinds);

@@ -830,6 +830,40 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
         return 0;
     }
 
+    // No keystream buffer, raw and 16-byte aligned records and destinations:
+    // one fused layer kernel computes the keystream itself.
+    bool dsts_aligned = !rec_misaligned;
+    for (uint32_t i = 0; dsts_aligned && i < n; ++i) dsts_aligned = !misaligned(dsts[i]);
+    if (!cp.bits && dsts_aligned) {
+        std::vector<LayerRec> recs(std::min<uint32_t>(n, kLayerCapLarge));
+        for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
+            const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
+            uint32_t seg_steps = 0, nseg = 0;
+            layer_segments_for(count, m, 0, &seg_steps, &nseg);
+            LaunchSlot& slot = g_s.launch[g_s.launch_next];
+            g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
+            if (!ensure_launch_slot(slot, m, nseg * m)) return -1;
+            LayerHeader h{};
+            h.sched = g_s.sched;
+            h.records = records + first * stride;
+            h.stride = stride;
+            h.count = count;
+            h.status = status + first;
+            h.partials = slot.partials;
+            h.counters = slot.counters;
+            h.iv0 = load_be32(g_s.salt);
+            h.n = m;
+            h.nseg = nseg;
+            h.seg_steps = seg_steps;
+            h.join_pow = sib::join_tables_for(g_s.join_tabs, seg_steps);
+            for (uint32_t i = 0; i < m; ++i) recs[i] = LayerRec{static_cast<uint8_t*>(dsts[first + i]), tickets[first + i]};
+            if (launch_layer_verify_inline(h, recs.data(), stream) != cudaSuccess) return -1;
+            cudaEventRecord(slot.free_ev, stream);
+            slot.used = true;
+        }
+        return 0;
+    }
+
     const uint32_t seg_blocks = segment_blocks_for(
         static_cast<uint64_t>(n) * ((kAadBytes + 15u) / 16u + (count + 15u) / 16u + 1u));
     const uint32_t nseg = segments_for(count, kAadBytes, seg_blocks);
