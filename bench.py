@@ -674,39 +674,7 @@ def run_gpu(args, cfg):
         assert int(status.min().item()) == 1
         return ms / args.steps, launches, clk
 
-    # Keystream of layer l + 1 on a producer stream beside the verify of layer
-    # l on the caller's stream, through the two halves of reload_records
-    # (secure_infer_keystream_records / secure_infer_verify_records), with two
-    # keystream buffers: the keystream kernel runs while the previous layer
-    # verifies, on the same SMs when the verify kernel leaves room for it.
-    ks_pair = [ks, torch.empty(max_ks, dtype=torch.uint8, device="cuda")]
-    ks_pair_ptr = [t.data_ptr() for t in ks_pair]
-    producer = torch.cuda.Stream()
-    pp = ct.c_void_p(producer.cuda_stream)
-    ev_ks = [torch.cuda.Event() for _ in range(L)]
-    ev_vf = [torch.cuda.Event() for _ in range(L)]
-    ev_start = torch.cuda.Event()
-
-    def device_step_pipelined():
-        ev_start.record(stream)           # the previous step's verifies have read both buffers
-        producer.wait_event(ev_start)
-        assert lib.secure_infer_keystream_records(tickets[0], n, count[0], ks_pair_ptr[0], pp) == 0
-        ev_ks[0].record(producer)
-        for layer in range(L):
-            if layer + 1 < L:
-                if layer >= 1:
-                    producer.wait_event(ev_vf[layer - 1])   # its buffer is free again
-                assert lib.secure_infer_keystream_records(tickets[layer + 1], n, count[layer + 1],
-                                                          ks_pair_ptr[(layer + 1) % 2], pp) == 0
-                ev_ks[layer + 1].record(producer)
-            stream.wait_event(ev_ks[layer])
-            assert lib.secure_infer_verify_records(layer, rec_ptr[layer], strides[layer], count[layer], n,
-                                                   tickets[layer], dst_all[layer], ks_pair_ptr[layer % 2],
-                                                   st_ptr[layer], codec_arg[layer], sp) == 0
-            ev_vf[layer].record(stream)
-        return 2 * L
-
-    paths = {"prefetched_keystream": device_step, "pipelined_keystream": device_step_pipelined}
+    paths = {"prefetched_keystream": device_step}
     if all(b == 0 for b in bits):
         paths["inline_keystream"] = device_step_inline
     timings = {name: timed_steps(fn) for name, fn in paths.items()}
@@ -716,7 +684,7 @@ def run_gpu(args, cfg):
     path_values = {name: round(world * algo / (t[0] * 1e-3) / 1e9, 3) for name, t in timings.items()}
 
     # ---- per-kernel device time (roofline) ----
-    prof = kernel_profile(lib, torch, paths[best] if best != "inline_keystream" else device_step, L)
+    prof = kernel_profile(lib, torch, device_step, L)
     ks_us = prof["gcm_layer_ctr_kernel"][0]
     vf_us = prof["gcm_layer_verify_kernel"][0]
     inline_us = None

@@ -25,7 +25,6 @@
 #include <cuda_bf16.h>
 
 #include <atomic>
-#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -650,10 +649,8 @@ __device__ __forceinline__ void layer_iv(uint32_t iv0, uint64_t ticket, uint32_t
 }
 
 // Keystream of every record plus E_K(J0) in the record's last 16 bytes.
-// At most 64 registers per thread (512 x 64 = half the register file), so a
-// shared-SM verify CTA or a quantise CTA fits beside it.
 template <int kCap>
-__global__ void __launch_bounds__(kLayerCtrThreads, 2) gcm_layer_ctr_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+__global__ void __launch_bounds__(kLayerCtrThreads, 1) gcm_layer_ctr_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     fill_aes4_smem(smem, L.h.sched);
@@ -783,40 +780,19 @@ __device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecPa
     }
 }
 
-// The shared-SM form of the raw verify (kLite): 8 warps (128 registers each,
-// half the register file) and only the H^32 byte tables in shared memory
-// (64 KiB); the lane, quarter and join tables are read through L1 from the
-// schedule.  A keystream CTA (512 threads x 64 registers, 128 KiB of tables)
-// then fits on the same SM, so the keystream of the next layer, launched on
-// another stream, runs beside this layer's verify: the two share the SM's
-// issue slots and shared-memory pipe instead of taking turns.
-constexpr uint32_t kLiteThreads = 256;
-__host__ __device__ constexpr uint32_t verify_threads(int mode, bool lite) { return lite ? kLiteThreads : layer_threads(mode); }
-
-template <int kCap, int kMode, bool kLite = false>
-__global__ void __launch_bounds__(verify_threads(kMode, kLite), kLite ? 2 : 1)
-    gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+template <int kCap, int kMode>
+__global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
     constexpr bool kCodec = kMode == kLayerVerifyCodec8 || kMode == kLayerVerifyCodec4;
     constexpr bool kEncrypt = kMode == kLayerEncrypt;
-    static_assert(!kLite || kMode == kLayerVerifyRaw, "the shared-SM form is raw verify only");
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* gtab = reinterpret_cast<uint4*>(smem);
+    uint4* ltab = reinterpret_cast<uint4*>(smem + kGhashSmem);
+    uint4* qtab = reinterpret_cast<uint4*>(smem + 2 * kGhashSmem);   // [3][512]: H^8, H^16, H^24
+    uint4* jtab = qtab + 3 * 512;                                    // [5][512]: H^(32 S 2^b), b = 0..4
     const GcmSchedule* __restrict__ S = L.h.sched;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u, quarter = lane >> 3;
     const uint32_t seg_steps = L.h.seg_steps;
-    // Combine tables: shared memory (bulk copied below), or the schedule and
-    // the session join tables through L1 in the shared-SM form.
-    const uint4* ltab = kLite ? S->lane8 : reinterpret_cast<const uint4*>(smem + kGhashSmem);
-    const uint4* qtab_s = reinterpret_cast<const uint4*>(smem + 2 * kGhashSmem);   // [3][512]: H^8, H^16, H^24
-    const uint4* jtab_s = qtab_s + 3 * 512;                                         // [5][512]: H^(32 S 2^b)
-    auto qtab_for = [&](uint32_t q) -> const uint4* {                               // H^(24 - 8 q)
-        return kLite ? S->tab[tab_pow_small(8 * (3 - static_cast<int>(q)))] : qtab_s + 512 * (2 - q);
-    };
-    auto jtab_for = [&](int b) -> const uint4* {                                    // H^(32 S 2^b)
-        return kLite ? (b == 0 ? S->tab[tab_pow_32k(static_cast<int>(seg_steps))] : L.h.join_pow + 512 * (b - 1))
-                     : jtab_s + 512 * b;
-    };
     __shared__ __align__(8) uint64_t tables_bar, gtab_bar;
     // Tables used only after a warp's main loop (lane, quarter and join
     // tables, 128 KiB) stream in by bulk copy while the main loop runs.
@@ -825,26 +801,21 @@ __global__ void __launch_bounds__(verify_threads(kMode, kLite), kLite ? 2 : 1)
         // first step on; waited for after each warp has issued its first loads.
         mbar_init_expect(&gtab_bar, 65536u);
         bulk_g2s(gtab, S->byte32, 65536u, &gtab_bar);
-        if constexpr (!kLite) {
-            uint4* ltab_w = reinterpret_cast<uint4*>(smem + kGhashSmem);
-            uint4* qtab_w = reinterpret_cast<uint4*>(smem + 2 * kGhashSmem);
-            uint4* jtab_w = qtab_w + 3 * 512;
-            mbar_init_expect(&tables_bar, 65536u + 8u * 8192u);
-            bulk_g2s(ltab_w, S->lane8, 65536u, &tables_bar);
-            bulk_g2s(qtab_w, S->tab[tab_pow_small(8)], 8192u, &tables_bar);
-            bulk_g2s(qtab_w + 512, S->tab[tab_pow_small(16)], 8192u, &tables_bar);
-            bulk_g2s(qtab_w + 1024, S->tab[tab_pow_small(24)], 8192u, &tables_bar);
-            bulk_g2s(jtab_w, S->tab[tab_pow_32k(seg_steps)], 8192u, &tables_bar);
-            bulk_g2s(jtab_w + 512, L.h.join_pow, 4u * 8192u, &tables_bar);
-        }
+        mbar_init_expect(&tables_bar, 65536u + 8u * 8192u);
+        bulk_g2s(ltab, S->lane8, 65536u, &tables_bar);
+        bulk_g2s(qtab, S->tab[tab_pow_small(8)], 8192u, &tables_bar);
+        bulk_g2s(qtab + 512, S->tab[tab_pow_small(16)], 8192u, &tables_bar);
+        bulk_g2s(qtab + 1024, S->tab[tab_pow_small(24)], 8192u, &tables_bar);
+        bulk_g2s(jtab, S->tab[tab_pow_32k(seg_steps)], 8192u, &tables_bar);
+        bulk_g2s(jtab + 512, L.h.join_pow, 4u * 8192u, &tables_bar);
     }
-    constexpr uint32_t kLayerThreads = verify_threads(kMode, kLite), kLayerWarps = kLayerThreads / 32;
+    constexpr uint32_t kLayerThreads = layer_threads(kMode), kLayerWarps = kLayerThreads / 32;
     __syncthreads();
     // Records, keystream and destinations are touched only after the
     // previous grid (the keystream kernel) has completed.
     allow_dependent_launch();
     grid_dependency_wait();
-    bool tables_ready = kLite, gtab_ready = false;
+    bool tables_ready = false, gtab_ready = false;
 
     const uint64_t count = L.h.count;
     const bool aligned = L.h.unaligned == 0;
@@ -1020,11 +991,11 @@ __global__ void __launch_bounds__(verify_threads(kMode, kLite), kLite ? 2 : 1)
         // (status 0, output zeroed) instead of waiting forever.
         if (!tables_ready) tables_ready = mbar_wait_bounded(&tables_bar, 0);
         if (!tables_ready || !gtab_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
-        Y = gf_mul_table<8, kLite>(Y, ltab, rep);                       // * H^(8 - r)
+        Y = gf_mul_table<8, false>(Y, ltab, rep);                       // * H^(8 - r)
         Y = xor4(Y, shfl_xor4(Y, 1));
         Y = xor4(Y, shfl_xor4(Y, 2));
         Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
-        if (quarter != 3) Y = gf_mul_table<1, kLite>(Y, qtab_for(quarter), 0);   // * H^(24 - 8 q)
+        if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
         Y = xor4(Y, shfl_xor4(Y, 8));
         const uint4 part = xor4(Y, shfl_xor4(Y, 16));
 
@@ -1054,7 +1025,7 @@ __global__ void __launch_bounds__(verify_threads(kMode, kLite), kLite ? 2 : 1)
             for (int b = 0; b < 5; ++b) {
                 const uint4 left = shfl_up4(v, 1u << b);
                 const uint32_t grp = (2u << b) - 1u;
-                if ((lane & grp) == grp) v = xor4(gf_mul_table<1, kLite>(left, jtab_for(b), 0), v);
+                if ((lane & grp) == grp) v = xor4(gf_mul_table<1, false>(left, jtab + 512 * b, 0), v);
             }
             v = make_uint4(__shfl_sync(0xffffffffu, v.x, 31), __shfl_sync(0xffffffffu, v.y, 31),
                            __shfl_sync(0xffffffffu, v.z, 31), __shfl_sync(0xffffffffu, v.w, 31));
@@ -1864,17 +1835,6 @@ int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream
                                         set_large[dev & 63], stream);
 }
 
-// Raw verify in its shared-SM form (SECURE_INFER_VERIFY_SHARE_SM=1): a
-// keystream launched on another stream runs beside it on every SM.
-bool verify_shares_sm()
-{
-    static const bool on = [] {
-        const char* v = std::getenv("SECURE_INFER_VERIFY_SHARE_SM");
-        return v != nullptr && std::atoi(v) != 0;
-    }();
-    return on;
-}
-
 int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
 {
     if (h.n == 0) return cudaSuccess;
@@ -1903,16 +1863,6 @@ int launch_layer_verify(const LayerHeader& h, const LayerRec* rec, cudaStream_t 
                                                 h, rec, layer_threads(kLayerVerifyCodec4), kLayerSmem, grid, set_small_4[dev & 63], stream, 1);
         return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyCodec4>,
                                             h, rec, layer_threads(kLayerVerifyCodec4), kLayerSmem, grid, set_large_4[dev & 63], stream, 1);
-    }
-    if (verify_shares_sm()) {
-        static bool set_small_l[64], set_large_l[64];
-        const uint32_t lgrid = (items + kLiteThreads / 32 - 1) / (kLiteThreads / 32);
-        if (small)
-            return layer_launch<kLayerCapSmall>(kKernLayerVerify,
-                                                gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyRaw, true>, h, rec,
-                                                kLiteThreads, kGhashSmem, lgrid, set_small_l[dev & 63], stream, 1);
-        return layer_launch<kLayerCapLarge>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapLarge, kLayerVerifyRaw, true>,
-                                            h, rec, kLiteThreads, kGhashSmem, lgrid, set_large_l[dev & 63], stream, 1);
     }
     if (small)
         return layer_launch<kLayerCapSmall>(kKernLayerVerify, gcm_layer_verify_kernel<kLayerCapSmall, kLayerVerifyRaw>, h, rec,
