@@ -342,19 +342,22 @@ def measure_host_bound(torch, dist, rank: int) -> dict | None:
     return out
 
 
-def host_bound(host_mem: dict | None, algo: int, link_bytes: int, world: int) -> dict | None:
-    """The host's memory bound on e2e: every record crosses host memory three
-    times per step (plaintext read and ciphertext written by OpenSSL, then read
-    by the copy engine; or, for writeback, written by the copy engine, read by
-    OpenSSL and the plaintext written), on every rank."""
+def host_bound(host_mem: dict | None, encrypt_gbs: float | None = None, algo: int = 0, wire: int = 0) -> dict | None:
+    """The host side of e2e: the host's copy bandwidth (rank 0 alone, every
+    CPU) and, for reloads, the measured aggregate rate at which all ranks
+    encrypt records on their own host pools at once (wire bytes/s), with the
+    e2e ceiling it implies (algorithmic bytes per wire byte)."""
     if not host_mem:
         return None
-    host_bytes = 3 * link_bytes * world
-    return {"host_copy_gbs": host_mem["gbs"], "copy_threads": host_mem["threads"],
-            "host_bytes_per_step_all_ranks": host_bytes,
-            "e2e_bound_gbs": round(host_mem["gbs"] * algo * world / host_bytes, 1),
-            "note": "host copy bandwidth = (read + write) bytes/s of a 1 GiB torch CPU copy on all host CPUs; "
-                    "e2e_bound = that bandwidth spread over 3 host-memory passes per record byte"}
+    out = {"host_copy_gbs": host_mem["gbs"], "copy_threads": host_mem["threads"],
+           "copy_note": "(read + write) bytes/s of a 1 GiB torch CPU copy on every host CPU, rank 0 alone"}
+    if encrypt_gbs:
+        out.update(host_encrypt_gbs=round(encrypt_gbs, 1), e2e_bound_gbs=round(encrypt_gbs * algo / wire, 1),
+                   encrypt_note="all ranks at once: secure_infer_h2d_encrypt_records of one layer's records into "
+                                "pinned staging on each rank's own OpenSSL pool, wire bytes/s summed over ranks; "
+                                "e2e_bound = that rate x algorithmic bytes per wire byte (no copy engine reading "
+                                "host memory meanwhile, so an upper bound)")
+    return out
 
 
 def build_workload(cfg, rank, torch, nl):
@@ -749,6 +752,22 @@ def run_gpu(args, cfg):
     link_wc = link_gbs(torch, stream, "h2d", write_combined=True)
     host_mem = measure_host_bound(torch, dist, rank)
 
+    # Host encryption capacity: every rank encrypts layer 0's records on its
+    # own pool at the same time (no device work).
+    stage = torch.empty(strides[0] * n, dtype=torch.uint8).pin_memory()
+    tk_scratch = (ct.c_uint64 * n)()
+    reps = 4
+    assert lib.secure_infer_h2d_encrypt_records(src_all[0], count[0], n, stage.data_ptr(), strides[0], tk_scratch) == 0
+    barrier()
+    t_enc = time.perf_counter()
+    for _ in range(reps):
+        assert lib.secure_infer_h2d_encrypt_records(src_all[0], count[0], n, stage.data_ptr(), strides[0],
+                                                    tk_scratch) == 0
+    enc_s = max_over_ranks(time.perf_counter() - t_enc, dist)
+    barrier()
+    encrypt_gbs = world * reps * count[0] * n / enc_s / 1e9
+    del stage
+
     overlap = None
     if world == 1 and args.suffix > 0:
         # The device-resident reload of the faster path.
@@ -818,7 +837,7 @@ def run_gpu(args, cfg):
                                       f"no collective", "host_pool": host_pool},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "per_layer_reload_us": round(e2e_ms * 1e3 / L, 2),
-                    "host_bound": host_bound(host_mem, algo, h2d_bytes, world),
+                    "host_bound": host_bound(host_mem, encrypt_gbs, algo, wire),
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                     "link_h2d_gbs": round(link, 2),
                     "link_h2d_wc_gbs": round(link_wc, 2) if link_wc else None,
@@ -1023,7 +1042,7 @@ def run_gpu_writeback(args, cfg):
                                       f"no collective", "host_pool": host_pool},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "per_layer_us": round(e2e_ms * 1e3 / L, 2),
-                    "host_bound": host_bound(host_mem, algo, d2h_step, world),
+                    "host_bound": host_bound(host_mem),
                     "h2d_bytes_per_step": L * n * (64 + 8),
                     "d2h_bytes_per_step": d2h_step,
                     "link_d2h_gbs": round(link, 2),
