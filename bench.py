@@ -688,7 +688,9 @@ def run_gpu(args, cfg):
 
     # ---- per-kernel device time (roofline) ----
     prof = kernel_profile(lib, torch, device_step, L)
-    ks_us = prof["gcm_layer_ctr_kernel"][0]
+    # The keystream kernel: T-table (default) or bitsliced (SECURE_INFER_AES_KEYSTREAM=bitsliced).
+    ks_name = "gcm_layer_ctr_bs_kernel" if "gcm_layer_ctr_bs_kernel" in prof else "gcm_layer_ctr_kernel"
+    ks_us = prof[ks_name][0]
     vf_us = prof["gcm_layer_verify_kernel"][0]
     inline_us = None
     if "inline_keystream" in paths:
@@ -784,14 +786,14 @@ def run_gpu(args, cfg):
     result = None
     if rank == 0:
         ks_mean, vf_mean = ks_us, vf_us
-        per_kernel = {"gcm_layer_ctr_kernel": ks_mean, "gcm_layer_verify_kernel": vf_mean}
+        per_kernel = {ks_name: ks_mean, "gcm_layer_verify_kernel": vf_mean}
         if inline_us is not None:
             per_kernel["gcm_layer_verify_inline_kernel"] = inline_us
         # The dominant kernel of the path that gave `value`.
         if best == "inline_keystream":
             dominant = "gcm_layer_verify_inline_kernel"
         else:
-            dominant = "gcm_layer_verify_kernel" if vf_mean >= ks_mean else "gcm_layer_ctr_kernel"
+            dominant = "gcm_layer_verify_kernel" if vf_mean >= ks_mean else ks_name
         layer_algo = algo / L
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
         hbm_peak = peaks.get("hbm_gbs", 6650.0)
@@ -809,7 +811,8 @@ def run_gpu(args, cfg):
         wavefronts = {"gcm_layer_verify_kernel": 2.0 * (payload_blocks + 5 * n),
                       "gcm_layer_ctr_kernel": 5.5 * (payload_blocks + n),
                       "gcm_layer_verify_inline_kernel": 2.0 * (payload_blocks + 5 * n) + 5.5 * (payload_blocks + n)}
-        smem = {name: round(wavefronts[name] / (us * 1e-6 * sms * sm_hz), 4) for name, us in per_kernel.items()}
+        smem = {name: round(wavefronts[name] / (us * 1e-6 * sms * sm_hz), 4) for name, us in per_kernel.items()
+                if name in wavefronts}
         result = {
             "metric": "Verified KV reload GB/s/GPU (AES-GCM+dequant+scatter); per-layer reload us",
             "value": round(value, 3),

@@ -27,7 +27,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden,-O3",
           f"-I{CSRC}", f"-I{ROOT / 'include'}"]
 SOURCES = ["gcm_kernels.cu", "plugin_abi.cpp", "host_runtime.cpp"]
-HEADERS = ["gcm_device.cuh", "gcm_kernels.cuh", "host_runtime.h"]
+HEADERS = ["gcm_device.cuh", "gcm_kernels.cuh", "host_runtime.h", "bitsliced_aes.cuh", "bitsliced_sbox.cuh"]
 
 
 def _stale(target: Path, deps: list[Path]) -> bool:

@@ -20,6 +20,7 @@
 // (secure_infer/kv_offload/transport_codec.py:22-42, optimized_decode.py:5-27).
 #include "gcm_device.cuh"
 #include "gcm_kernels.cuh"
+#include "bitsliced_aes.cuh"
 #include "kx.cuh"
 
 #include <cuda_bf16.h>
@@ -671,6 +672,74 @@ __global__ void __launch_bounds__(kLayerCtrThreads, 1) gcm_layer_ctr_kernel(cons
         const uint4 in = c == payload_blocks ? j0_block_le(iv) : ctr_block_le(iv, c);
         const uint4 ks = aes128_encrypt_t4(in, T, rk);
         if (L.h.unaligned) store_partial16(out, ks, 16); else *reinterpret_cast<uint4*>(out) = ks;
+    }
+}
+
+// The same keystream (and E_K(J0) in each record's last 16 bytes) from the
+// bitsliced AES of bitsliced_aes.cuh: no table lookups, only integer logic
+// (the S-box circuit, MixColumns XORs, a bit transpose per output word).  A
+// thread takes one counter group of a record, v = 32 g .. 32 g + 31 (v = 1 is
+// J0, payload block c has v = c + 2, v = 0 is not used); the round keys become
+// plane masks in shared memory once per CTA.  It exists to be measured
+// against the T-table kernel (SECURE_INFER_AES_KEYSTREAM=bitsliced selects it).
+constexpr uint32_t kBsThreads = 256;
+
+template <int kCap>
+__global__ void __launch_bounds__(kBsThreads, 1) gcm_layer_ctr_bs_kernel(const __grid_constant__ LayerLaunch<kCap> L)
+{
+    __shared__ __align__(16) uint32_t mask[1408];
+    for (uint32_t i = threadIdx.x; i < 1408u; i += blockDim.x) {
+        const uint32_t b = i >> 3, k = i & 7u;
+        const uint32_t byte = (L.h.sched->rk[b >> 2] >> (8u * (b & 3u))) & 0xffu;
+        mask[i] = ((byte >> (7u - k)) & 1u) ? 0xffffffffu : 0u;
+    }
+    __syncthreads();
+    // The keystream buffer may still be read by the previous verify grid.
+    allow_dependent_launch();
+    grid_dependency_wait();
+    const uint32_t payload_blocks = static_cast<uint32_t>((L.h.count + 15) >> 4);
+    const uint32_t groups = (payload_blocks + 2u + 31u) / 32u;
+    const uint32_t total = groups * L.h.n;
+    for (uint32_t item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += gridDim.x * blockDim.x) {
+        const uint32_t r = item / groups, g = item - r * groups;
+        const uint64_t ticket = L.rec[r].ticket;
+        const uint32_t iv[3] = {L.h.iv0, static_cast<uint32_t>(ticket >> 32), static_cast<uint32_t>(ticket)};
+        uint32_t st[16][8];
+        bs_load_group(st, iv, g, mask);
+        bs_encrypt(st, mask);
+        uint8_t* rec = L.h.ks + static_cast<uint64_t>(r) * L.h.ks_stride;
+        // Each output word goes out as soon as it is transposed, so only 32
+        // of its words are live beside the remaining planes.
+        auto store_word = [&](const uint32_t (&w)[32], int word) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const uint32_t v = 32u * g + static_cast<uint32_t>(j);
+                if (v == 0u || (v >= 2u && v - 2u >= payload_blocks)) continue;
+                uint8_t* out = (v == 1u ? rec + (L.h.ks_stride - 16) : rec + 16ull * (v - 2u)) + 4 * word;
+                if (L.h.unaligned) store_partial16(out, make_uint4(w[j], 0, 0, 0), 4);
+                else *reinterpret_cast<uint32_t*>(out) = w[j];
+            }
+        };
+        {
+            uint32_t w[32];
+            bs_store_word<0>(st, w);
+            store_word(w, 0);
+        }
+        {
+            uint32_t w[32];
+            bs_store_word<1>(st, w);
+            store_word(w, 1);
+        }
+        {
+            uint32_t w[32];
+            bs_store_word<2>(st, w);
+            store_word(w, 2);
+        }
+        {
+            uint32_t w[32];
+            bs_store_word<3>(st, w);
+            store_word(w, 3);
+        }
     }
 }
 
@@ -1672,7 +1741,7 @@ const char* kernel_kind_name(uint32_t kind)
     static const char* names[kKernKinds] = {"gcm_layer_ctr_kernel", "gcm_layer_verify_kernel", "gcm_layer_encrypt",
                                             "kv_encode_kernel", "gcm_segment_kernel", "gcm_ctr_kernel",
                                             "gcm_schedule_kernel", "auth_gate_kernel",
-                                            "gcm_layer_verify_inline_kernel"};
+                                            "gcm_layer_verify_inline_kernel", "gcm_layer_ctr_bs_kernel"};
     return kind < kKernKinds ? names[kind] : nullptr;
 }
 
@@ -1819,10 +1888,30 @@ int layer_launch(uint32_t kind, Kernel kernel, const LayerHeader& h, const Layer
     return cudaLaunchKernelEx(&cfg, kernel, L);
 }
 
+// SECURE_INFER_AES_KEYSTREAM=bitsliced selects the bitsliced keystream kernel
+// (read at every launch); the T-table kernel is the default.
+bool keystream_bitsliced()
+{
+    const char* v = std::getenv("SECURE_INFER_AES_KEYSTREAM");
+    return v != nullptr && v[0] == 'b';
+}
+
 int launch_layer_keystream(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
 {
     if (h.n == 0) return cudaSuccess;
     if (h.n > static_cast<uint32_t>(kLayerCapLarge)) return cudaErrorInvalidValue;
+    if (keystream_bitsliced()) {
+        static bool bs_small[64], bs_large[64];
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const uint32_t groups = static_cast<uint32_t>(((h.count + 15) / 16 + 2 + 31) / 32);
+        const uint32_t items = (groups * h.n + kBsThreads - 1) / kBsThreads;
+        if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
+            return layer_launch<kLayerCapSmall>(kKernLayerCtrBitsliced, gcm_layer_ctr_bs_kernel<kLayerCapSmall>, h, rec,
+                                                kBsThreads, 0, items, bs_small[dev & 63], stream);
+        return layer_launch<kLayerCapLarge>(kKernLayerCtrBitsliced, gcm_layer_ctr_bs_kernel<kLayerCapLarge>, h, rec,
+                                            kBsThreads, 0, items, bs_large[dev & 63], stream);
+    }
     const uint32_t blocks = static_cast<uint32_t>(((h.count + 15) / 16 + 1) * h.n);
     const uint32_t items = (blocks + kLayerCtrThreads - 1) / kLayerCtrThreads;
     static bool set_small[64], set_large[64];

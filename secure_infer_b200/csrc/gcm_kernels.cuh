@@ -157,7 +157,7 @@ int launch_layer_verify_inline(const LayerHeader& h, const LayerRec* rec, cudaSt
 // events on its stream; collect() sums device time and launches per kind.
 enum KernelKind : uint32_t {
     kKernLayerCtr = 0, kKernLayerVerify, kKernLayerEncrypt, kKernEncode, kKernSegment, kKernCtr, kKernSchedule,
-    kKernAuthGate, kKernLayerVerifyInline, kKernKinds
+    kKernAuthGate, kKernLayerVerifyInline, kKernLayerCtrBitsliced, kKernKinds
 };
 void profile_enable(bool on);
 int profile_collect(double* total_us, uint64_t* launches, uint32_t kinds);
