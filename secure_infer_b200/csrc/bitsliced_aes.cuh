@@ -10,13 +10,14 @@
 // input plane is all zeros or all ones.
 //
 // Rounds (FIPS-197 5.1): SubBytes is bs_sbox on the eight planes of each byte;
-// ShiftRows moves no data -- after k rounds, logical byte (row r, column c) is
-// kept in slot 4 ((c + k r) mod 4) + r, a compile-time index; MixColumns works
-// on the planes of a column, with xtime as a rewiring plus three XORs, in place
-// over the slots it reads; AddRoundKey XORs each plane with a mask that is all
-// ones where the round-key bit is set (rk_mask, 11 x 128 words, built once per
-// CTA from the key schedule).  A 32 x 32 bit transpose per output word brings
-// each block back to byte order.
+// ShiftRows rotates the planes of rows 1-3 between columns (register moves);
+// MixColumns works on the planes of a column, with xtime as a rewiring plus
+// three XORs; AddRoundKey XORs each plane with a mask that is all ones where
+// the round-key bit is set (rk_mask, 11 x 128 words, built once per CTA from
+// the key schedule).  Rounds 1-9 run as a loop over one round body: unrolled,
+// the ten rounds are about 25k instructions and the kernel stalls on
+// instruction fetch.  A 32 x 32 bit transpose per output word brings each
+// block back to byte order.  Byte b of the block is row b mod 4, column b / 4.
 //
 // Everything is __host__ __device__ so the CPU tests can run the same code.
 #pragma once
@@ -26,9 +27,6 @@
 #include "bitsliced_sbox.cuh"
 
 namespace sib {
-
-// Slot of logical byte (row r, column c) after k ShiftRows.
-SIB_HD constexpr int bs_slot(int r, int c, int k) { return 4 * ((c + k * r) & 3) + r; }
 
 // Round-key masks: rk_mask[(round * 16 + byte) * 8 + bit] for the 176 round-key
 // bytes (byte order of FIPS-197, round keys one after the other).
@@ -68,20 +66,31 @@ SIB_HD void bs_sub_bytes(uint32_t st[16][8])
                 st[b][2], st[b][3], st[b][4], st[b][5], st[b][6], st[b][7]);
 }
 
-// MixColumns + AddRoundKey of round K (1..9), after that round's ShiftRows:
-// column c holds logical rows r in slots bs_slot(r, c, K).
+// ShiftRows: row r of the state moves r columns to the left.
+SIB_HD void bs_shift_rows(uint32_t st[16][8])
+{
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t r1 = st[1][k];
+        st[1][k] = st[5][k]; st[5][k] = st[9][k]; st[9][k] = st[13][k]; st[13][k] = r1;
+        const uint32_t r2a = st[2][k], r2b = st[6][k];
+        st[2][k] = st[10][k]; st[6][k] = st[14][k]; st[10][k] = r2a; st[14][k] = r2b;
+        const uint32_t r3 = st[15][k];
+        st[15][k] = st[11][k]; st[11][k] = st[7][k]; st[7][k] = st[3][k]; st[3][k] = r3;
+    }
+}
+
+// MixColumns + AddRoundKey with the round key's 128 masks `key`:
 // b_r = xtime(a_r ^ a_{r+1}) ^ a_r ^ (a_0 ^ a_1 ^ a_2 ^ a_3) ^ key.
-template <int K>
-SIB_HD void bs_mix_add(uint32_t st[16][8], const uint32_t* rk_mask)
+SIB_HD void bs_mix_add(uint32_t st[16][8], const uint32_t* key)
 {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-        const int slot[4] = {bs_slot(0, c, K), bs_slot(1, c, K), bs_slot(2, c, K), bs_slot(3, c, K)};
         uint32_t sum[8], a0[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            sum[k] = st[slot[0]][k] ^ st[slot[1]][k] ^ st[slot[2]][k] ^ st[slot[3]][k];
-            a0[k] = st[slot[0]][k];
+            sum[k] = st[4 * c][k] ^ st[4 * c + 1][k] ^ st[4 * c + 2][k] ^ st[4 * c + 3][k];
+            a0[k] = st[4 * c][k];
         }
         // Rows in order, each overwriting its own slot: row r still sees the
         // original row r + 1 (row 3 pairs with the saved row 0).
@@ -89,39 +98,34 @@ SIB_HD void bs_mix_add(uint32_t st[16][8], const uint32_t* rk_mask)
         for (int r = 0; r < 4; ++r) {
             uint32_t t[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) t[k] = st[slot[r]][k] ^ (r == 3 ? a0[k] : st[slot[r + 1]][k]);
+            for (int k = 0; k < 8; ++k) t[k] = st[4 * c + r][k] ^ (r == 3 ? a0[k] : st[4 * c + r + 1][k]);
             // xtime on planes (k = 0 is bit 7): shift left, reduce by 0x1b.
             const uint32_t x[8] = {t[1], t[2], t[3], t[4] ^ t[0], t[5] ^ t[0], t[6], t[7] ^ t[0], t[0]};
-            const uint32_t* key = rk_mask + (K * 16 + 4 * c + r) * 8;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) st[slot[r]][k] ^= x[k] ^ sum[k] ^ key[k];
+            for (int k = 0; k < 8; ++k) st[4 * c + r][k] ^= x[k] ^ sum[k] ^ key[(4 * c + r) * 8 + k];
         }
     }
 }
 
-// AddRoundKey of the last round (no MixColumns), after its ShiftRows.
-SIB_HD void bs_add_last(uint32_t st[16][8], const uint32_t* rk_mask)
+SIB_HD void bs_add_key(uint32_t st[16][8], const uint32_t* key)
 {
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int b = 0; b < 16; ++b)
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int k = 0; k < 8; ++k) st[bs_slot(r, c, 10)][k] ^= rk_mask[(160 + 4 * c + r) * 8 + k];
+        for (int k = 0; k < 8; ++k) st[b][k] ^= key[b * 8 + k];
 }
 
 SIB_HD void bs_encrypt(uint32_t st[16][8], const uint32_t* rk_mask)
 {
-    bs_sub_bytes(st); bs_mix_add<1>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<2>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<3>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<4>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<5>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<6>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<7>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<8>(st, rk_mask);
-    bs_sub_bytes(st); bs_mix_add<9>(st, rk_mask);
-    bs_sub_bytes(st); bs_add_last(st, rk_mask);
+#pragma unroll 1
+    for (int round = 1; round < 10; ++round) {
+        bs_sub_bytes(st);
+        bs_shift_rows(st);
+        bs_mix_add(st, rk_mask + round * 128);
+    }
+    bs_sub_bytes(st);
+    bs_shift_rows(st);
+    bs_add_key(st, rk_mask + 1280);
 }
 
 // Transpose of a 32 x 32 bit matrix in place: afterwards bit m of a[j] is
@@ -141,14 +145,14 @@ SIB_HD void bs_transpose32(uint32_t a[32])
 }
 
 // Little-endian output word w (bytes 4w .. 4w + 3) of the 32 blocks: out[j] is
-// word w of block j.  Logical byte 4w + t sits in slot bs_slot(t, w, 10).
+// word w of block j.
 template <int W>
 SIB_HD void bs_store_word(const uint32_t st[16][8], uint32_t out[32])
 {
 #pragma unroll
     for (int t = 0; t < 4; ++t)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) out[8 * t + i] = st[bs_slot(t, W, 10)][7 - i];
+        for (int i = 0; i < 8; ++i) out[8 * t + i] = st[4 * W + t][7 - i];
     bs_transpose32(out);
 }
 
