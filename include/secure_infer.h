@@ -73,6 +73,13 @@ void secure_infer_register_host_range(const void* base, size_t bytes);
 void secure_infer_register_host_range_ex(const void* base, size_t bytes, uint32_t layer_id, uint32_t tensor_kind,
                                          size_t block_bytes);
 
+/* 1 when [ptr, ptr + bytes) lies inside one registered host range, else 0.
+ * No separate reference export: it is the reference's internal check
+ * host_prediction_in_same_range (secure_infer.cpp:7733-7737), which decides
+ * whether an interposed copy takes the authenticated path; the opt-in
+ * cudaMemcpyAsync interposer (libsecure_infer_interpose.so) calls it. */
+int secure_infer_is_registered_host_range(const void* ptr, size_t bytes);
+
 /* ------------------------------------------------------ record helpers */
 
 /* Host worker pool of this process.  No counterpart in the reference, whose

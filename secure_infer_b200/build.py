@@ -21,6 +21,10 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = BUILD / "libsecure_infer.so"
+# Opt-in cudaMemcpyAsync interposer (LD_PRELOAD), host code only; it links
+# libsecure_infer.so from its own directory and resolves the real
+# cudaMemcpyAsync at run time.
+INTERPOSE = BUILD / "libsecure_infer_interpose.so"
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -55,6 +59,19 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objects):
         cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objects), "-lcrypto", "-lpthread"]
+        print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+    src = CSRC / "memcpy_interpose.cpp"
+    if force or _stale(INTERPOSE, [src, LIB]):
+        cxx = os.environ.get("CXX", "g++")
+        cuda_inc = Path(NVCC).resolve().parent.parent / "include"
+        # Export cudaMemcpyAsync alone: a preloaded library must not shadow the
+        # process's C++ runtime with the copy a static libstdc++ brings along.
+        script = BUILD / "interpose.map"
+        script.write_text("{ global: cudaMemcpyAsync; local: *; };\n")
+        cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden", f"-I{cuda_inc}", str(src),
+               "-o", str(INTERPOSE), f"-L{BUILD}", "-lsecure_infer", "-Wl,-rpath,$ORIGIN", "-ldl",
+               f"-Wl,--version-script={script}", "-Wl,--exclude-libs,ALL"]
         print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
     return LIB

@@ -1827,6 +1827,14 @@ SI_EXPORT int secure_infer_host_pool_info(uint32_t* threads, int32_t* cpus, uint
     return static_cast<int>(plan.cpus.size());
 }
 
+SI_EXPORT int secure_infer_is_registered_host_range(const void* ptr, size_t bytes)
+{
+    if (ptr == nullptr || bytes == 0) return 0;
+    HostRange r{};
+    uint64_t block = 0, off = 0;
+    return lookup_range(ptr, bytes, &r, &block, &off) ? 1 : 0;
+}
+
 SI_EXPORT uint64_t secure_infer_new_transfer_ticket(void)
 {
     uint64_t t = 0;
