@@ -86,14 +86,15 @@ dev = torch.zeros((blocks + 2, 128, heads, 128), dtype=torch.bfloat16, device="c
 before = nl.auth_stats()
 # An unmodified caller: per-block torch copies of the registered host pool
 # inside the reference's layer bracket.
+table = [4, 0, 3, 2]                  # host block i -> device block table[i]
 assert lib.secure_infer_h2d_layer_group_begin(blocks) == 0
 for i in range(blocks):
-    dev[(i * 3 + 1) % (blocks + 2)].copy_(host[i], non_blocking=True)
+    dev[table[i]].copy_(host[i], non_blocking=True)
 assert lib.secure_infer_h2d_layer_group_end() == 0
 auth = lib.secure_infer_recovery_wait_layer_authentication(layer)
 torch.cuda.synchronize()
 after = nl.auth_stats()
-ok = all(torch.equal(dev[(i * 3 + 1) % (blocks + 2)].cpu(), host[i]) for i in range(blocks))
+ok = all(torch.equal(dev[table[i]].cpu(), host[i]) for i in range(blocks))
 # A copy from an unregistered buffer is a plain copy: no new authentications.
 dev[blocks + 1].copy_(plain_host[0])
 torch.cuda.synchronize()
