@@ -71,6 +71,14 @@ CONFIGS = {
 }
 
 
+def scaling_kind(cfg: dict, world: int) -> str:
+    """'strong' when the GPUs split one model's KV heads between them (TP equal
+    to the number of GPUs: the job's work is fixed as N grows), 'weak' when
+    each GPU runs a fixed shard (the config's own TP, or more GPUs than
+    shards)."""
+    return "strong" if cfg.get("tp_from_gpus") and cfg["tp"] == world else "weak"
+
+
 def shard_config(cfg: dict, world: int, tp: int | None) -> dict:
     """The per-rank share of a TP-sharded job (the path's partition: every GPU
     owns heads / TP KV heads of every layer with its own session, and no data
@@ -84,7 +92,7 @@ def shard_config(cfg: dict, world: int, tp: int | None) -> dict:
     if total % t:
         raise SystemExit(f"--tp {t} does not divide the {total} KV heads of {cfg['model']}")
     out = dict(cfg)
-    out.update(heads=total // t, heads_total=total, tp=t)
+    out.update(heads=total // t, heads_total=total, tp=t, tp_from_gpus=not tp and not cfg.get("tp"))
     return out
 
 
@@ -354,7 +362,8 @@ def host_bound(host_mem: dict | None, encrypt_gbs: float | None = None, algo: in
     if encrypt_gbs:
         out.update(host_encrypt_gbs=round(encrypt_gbs, 1), e2e_bound_gbs=round(encrypt_gbs * algo / wire, 1),
                    encrypt_note="all ranks at once: secure_infer_h2d_encrypt_records of one layer's records into "
-                                "pinned staging on each rank's own OpenSSL pool, wire bytes/s summed over ranks; "
+                                "write-combined pinned staging on each rank's own OpenSSL pool, wire bytes/s summed "
+                                "over ranks; "
                                 "e2e_bound = that rate x algorithmic bytes per wire byte (no copy engine reading "
                                 "host memory meanwhile, so an upper bound)")
     return out
@@ -755,19 +764,33 @@ def run_gpu(args, cfg):
     host_mem = measure_host_bound(torch, dist, rank)
 
     # Host encryption capacity: every rank encrypts layer 0's records on its
-    # own pool at the same time (no device work).
-    stage = torch.empty(strides[0] * n, dtype=torch.uint8).pin_memory()
+    # own pool at the same time (no device work), into write-combined pinned
+    # staging like the staged reload's (cached pinned memory if cuda-python
+    # cannot allocate it).
+    stage_bytes = strides[0] * n
+    stage, wc_ptr = None, None
+    try:
+        from cuda.bindings import runtime as cudart
+        err, wc_ptr = cudart.cudaHostAlloc(stage_bytes, cudart.cudaHostAllocWriteCombined)
+        if err != cudart.cudaError_t.cudaSuccess:
+            wc_ptr = None
+    except Exception:
+        wc_ptr = None
+    if wc_ptr is None:
+        stage = torch.empty(stage_bytes, dtype=torch.uint8).pin_memory()
+    stage_ptr = wc_ptr if wc_ptr is not None else stage.data_ptr()
     tk_scratch = (ct.c_uint64 * n)()
-    reps = 4
-    assert lib.secure_infer_h2d_encrypt_records(src_all[0], count[0], n, stage.data_ptr(), strides[0], tk_scratch) == 0
+    reps = 8
+    assert lib.secure_infer_h2d_encrypt_records(src_all[0], count[0], n, stage_ptr, strides[0], tk_scratch) == 0
     barrier()
     t_enc = time.perf_counter()
     for _ in range(reps):
-        assert lib.secure_infer_h2d_encrypt_records(src_all[0], count[0], n, stage.data_ptr(), strides[0],
-                                                    tk_scratch) == 0
+        assert lib.secure_infer_h2d_encrypt_records(src_all[0], count[0], n, stage_ptr, strides[0], tk_scratch) == 0
     enc_s = max_over_ranks(time.perf_counter() - t_enc, dist)
     barrier()
     encrypt_gbs = world * reps * count[0] * n / enc_s / 1e9
+    if wc_ptr is not None:
+        cudart.cudaFreeHost(wc_ptr)
     del stage
 
     overlap = None
@@ -823,7 +846,7 @@ def run_gpu(args, cfg):
             "ms_per_step": round(ms_per_step, 4),
             "per_layer_reload_us": round(ms_per_step * 1e3 / L, 2),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling_kind(cfg, world),
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic: N(0,1) bf16 KV from seed, seeded AES-128 key/salt per rank, random block table",
@@ -1030,7 +1053,7 @@ def run_gpu_writeback(args, cfg):
             "ms_per_step": round(ms_per_step, 4),
             "per_layer_us": round(ms_per_step * 1e3 / L, 2),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": scaling_kind(cfg, world),
             "vs_baseline": None,
             "dtype": "u8",
             "data": "synthetic: N(0,1) bf16 KV from seed, seeded AES-128 key/salt per rank, shuffled block table",
@@ -1234,7 +1257,7 @@ def run_reference(args, cfg):
                 "metric": "Verified KV writeback GB/s/GPU (gather+quantise+AES-GCM encrypt+tag); per-layer us",
                 "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": r["ms_per_step"], "per_layer_us": round(r["ms_per_step"] * 1e3 / L, 2),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+                "higher_is_better": True, "scaling": scaling_kind(cfg, world), "vs_baseline": None, "dtype": "u8",
                 "data": "synthetic N(0,1) bf16 KV", "config": {"workload": args.config, **cfg},
                 "cpu_baseline": r["cpu_baseline"],
                 "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -1244,7 +1267,7 @@ def run_reference(args, cfg):
             "metric": "Verified KV reload GB/s/GPU (AES-GCM+dequant+scatter); per-layer reload us",
             "value": r["value"], "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": r["ms_per_step"], "per_layer_reload_us": round(r["ms_per_step"] * 1e3 / L, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "higher_is_better": True, "scaling": scaling_kind(cfg, world), "vs_baseline": None, "dtype": "u8",
             "data": "synthetic N(0,1) bf16 KV", "config": {"workload": args.config, **cfg},
             "cpu_baseline": r["cpu_baseline"],
             "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
