@@ -310,6 +310,23 @@ void secure_infer_get_auth_stats(uint64_t* verified, uint64_t* rejected, uint64_
  * (direction 2).  nth = 0 disarms. */
 void secure_infer_arm_tamper(uint32_t direction, uint64_t nth, uint32_t target);
 
+/* ------------------------------------------------ opt-in memcpy interposer
+ *
+ * libsecure_infer_interpose.so (built beside this library) defines one symbol,
+ * the CUDA runtime's own
+ *
+ *     cudaError_t cudaMemcpyAsync(void* dst, const void* src, size_t count,
+ *                                 cudaMemcpyKind kind, cudaStream_t stream);
+ *
+ * standing in for the reference's interposed aclrtMemcpyAsync
+ * (secure_infer.cpp:7729-7855).  Preloaded with SECURE_INFER_INTERPOSE=1, it
+ * sends a cudaMemcpyHostToDevice copy whose source lies in a registered host
+ * range to secure_infer_h2d_submit and a cudaMemcpyDeviceToHost copy into a
+ * registered range to secure_infer_d2h_submit (cudaErrorInvalidValue if the
+ * library refuses it); every other copy, and every copy without the variable,
+ * goes to the next cudaMemcpyAsync in the lookup order.  It is not declared
+ * here so that this header stays free of CUDA runtime types. */
+
 #ifdef __cplusplus
 }
 #endif
