@@ -114,11 +114,16 @@ NCU_TRAFFIC_BYTES = {
 }
 
 
-# Shared-memory wavefronts per 16-byte block that the algorithm needs (the
-# binding pipe): GHASH with byte tables = 16 conflict-free LDS.128 per lane per
-# block = 2 wavefronts; AES-128 = 160 T-table LDS.32 + 16 final-round = 176 per
-# 32 blocks = 5.5.
-SMEM_WAVEFRONTS_PER_BLOCK = {"gcm_layer_verify_kernel": 2.0, "gcm_layer_ctr_kernel": 5.5}
+# Shared-memory wavefronts per 16-byte block that the algorithms need (the
+# binding pipe), one conflict-free wavefront per warp-wide lookup: GHASH with
+# byte tables = 16 LDS.128 per lane per block = 2 wavefronts; AES-128 with
+# T-tables = 16 lookups in each of rounds 1-9 and 16 in the final round = 160
+# per 32 blocks = 5.0, and 138 (4.3125) with the keystream kernel's counter-mode
+# caching (records of fewer than 2^16 - 2 blocks: round 1 needs 2 lookups,
+# round 2 needs 8).
+GHASH_WAVEFRONTS_PER_BLOCK = 2.0
+AES_WAVEFRONTS_PER_BLOCK = 160 / 32
+AES_CACHED_WAVEFRONTS_PER_BLOCK = 138 / 32
 
 
 def layer_bits(mode, layer, layers):
@@ -350,15 +355,43 @@ def measure_host_bound(torch, dist, rank: int) -> dict | None:
     return out
 
 
-def host_bound(host_mem: dict | None, encrypt_gbs: float | None = None, algo: int = 0, wire: int = 0) -> dict | None:
+def concurrent_link_gbs(torch, stream, dist, barrier, world: int, nbytes: int = 256 << 20, reps: int = 4) -> float:
+    """Aggregate pinned host -> device copy bandwidth with every rank copying
+    at once (the host's share of the fabric all GPUs reload through): bytes of
+    all ranks / the slowest rank's time."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dev.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        dev.copy_(host, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), dist)
+    barrier()
+    del host, dev
+    return world * reps * nbytes / (ms * 1e-3) / 1e9
+
+
+def host_bound(host_mem: dict | None, encrypt_gbs: float | None = None, algo: int = 0, wire: int = 0,
+               link_all_gbs: float | None = None, link_bytes: int = 0) -> dict | None:
     """The host side of e2e: the host's copy bandwidth (rank 0 alone, every
-    CPU) and, for reloads, the measured aggregate rate at which all ranks
-    encrypt records on their own host pools at once (wire bytes/s), with the
-    e2e ceiling it implies (algorithmic bytes per wire byte)."""
+    CPU) and, for reloads, two measured aggregate rates with the e2e ceiling
+    each implies: all ranks encrypting records on their own host pools at
+    once, and all ranks copying pinned memory to their GPUs at once."""
     if not host_mem:
         return None
     out = {"host_copy_gbs": host_mem["gbs"], "copy_threads": host_mem["threads"],
            "copy_note": "(read + write) bytes/s of a 1 GiB torch CPU copy on every host CPU, rank 0 alone"}
+    if link_all_gbs:
+        out.update(h2d_all_ranks_gbs=round(link_all_gbs, 1),
+                   e2e_link_bound_gbs=round(link_all_gbs * algo / link_bytes, 1),
+                   h2d_all_ranks_note="every rank copies 256 MiB of pinned memory to its GPU at once, 4 times; "
+                                      "bytes of all ranks / slowest rank's time; e2e_link_bound = that rate x "
+                                      "algorithmic bytes per record byte crossing")
     if encrypt_gbs:
         out.update(host_encrypt_gbs=round(encrypt_gbs, 1), e2e_bound_gbs=round(encrypt_gbs * algo / wire, 1),
                    encrypt_note="all ranks at once: secure_infer_h2d_encrypt_records of one layer's records into "
@@ -792,6 +825,7 @@ def run_gpu(args, cfg):
     if wc_ptr is not None:
         cudart.cudaFreeHost(wc_ptr)
     del stage
+    link_all = concurrent_link_gbs(torch, stream, dist, barrier, world)
 
     overlap = None
     if world == 1 and args.suffix > 0:
@@ -831,9 +865,11 @@ def run_gpu(args, cfg):
         payload_blocks = sum((count[layer] + 15) // 16 for layer in range(L)) * n / L
         # GHASH covers AAD (4) + payload + length block; AES covers the
         # payload + E_K(J0).  The fused inline kernel does both.
-        wavefronts = {"gcm_layer_verify_kernel": 2.0 * (payload_blocks + 5 * n),
-                      "gcm_layer_ctr_kernel": 5.5 * (payload_blocks + n),
-                      "gcm_layer_verify_inline_kernel": 2.0 * (payload_blocks + 5 * n) + 5.5 * (payload_blocks + n)}
+        aes_ctr = AES_CACHED_WAVEFRONTS_PER_BLOCK if (count[0] + 15) // 16 + 2 <= 65536 else AES_WAVEFRONTS_PER_BLOCK
+        wavefronts = {"gcm_layer_verify_kernel": GHASH_WAVEFRONTS_PER_BLOCK * (payload_blocks + 5 * n),
+                      "gcm_layer_ctr_kernel": aes_ctr * (payload_blocks + n),
+                      "gcm_layer_verify_inline_kernel": GHASH_WAVEFRONTS_PER_BLOCK * (payload_blocks + 5 * n)
+                      + AES_WAVEFRONTS_PER_BLOCK * (payload_blocks + n)}
         smem = {name: round(wavefronts[name] / (us * 1e-6 * sms * sm_hz), 4) for name, us in per_kernel.items()
                 if name in wavefronts}
         result = {
@@ -863,7 +899,7 @@ def run_gpu(args, cfg):
                                       f"no collective", "host_pool": host_pool},
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "per_layer_reload_us": round(e2e_ms * 1e3 / L, 2),
-                    "host_bound": host_bound(host_mem, encrypt_gbs, algo, wire),
+                    "host_bound": host_bound(host_mem, encrypt_gbs, algo, wire, link_all, h2d_bytes),
                     "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
                     "link_h2d_gbs": round(link, 2),
                     "link_h2d_wc_gbs": round(link_wc, 2) if link_wc else None,
@@ -889,9 +925,10 @@ def run_gpu(args, cfg):
                          "note": "achieved = per-layer algorithmic bytes (ciphertext in + bf16 out) / the dominant "
                                  "kernel's time on the path that gave `value`; peak = measured HBM copy bandwidth "
                                  "(of measured). The binding resource is the shared-memory pipe (AES T-tables, "
-                                 "GHASH byte tables): smem_pipe_frac = algorithmic wavefronts (GHASH 2, AES 5.5 per "
-                                 "16-byte block; the inline kernel both) / (kernel time x SMs x sampled SM clock), "
-                                 "1 wavefront per SM per clock peak."},
+                                 "GHASH byte tables): smem_pipe_frac = algorithmic wavefronts (GHASH 2 per 16-byte "
+                                 "block; AES 5.0, or 4.3125 with the keystream kernel's counter-mode caching; the "
+                                 "inline kernel both, uncached) / (kernel time x SMs x sampled SM clock), 1 "
+                                 "wavefront per SM per clock peak."},
             "clocks": clocks.summary(),
         }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1041,7 +1078,9 @@ def run_gpu_writeback(args, cfg):
         sm_hz = (clk["sm_mhz"] or clk["sm_max_mhz"] or 1965.0) * 1e6
         sms = torch.cuda.get_device_properties(local).multi_processor_count
         payload_blocks = sum((c + 15) // 16 for c in count) * n / L
-        per_block = {"gcm_layer_ctr_kernel": (5.5, payload_blocks + n), "gcm_layer_encrypt": (2.0, payload_blocks + 5 * n)}
+        aes_ctr = AES_CACHED_WAVEFRONTS_PER_BLOCK if max(count) // 16 + 3 <= 65536 else AES_WAVEFRONTS_PER_BLOCK
+        per_block = {"gcm_layer_ctr_kernel": (aes_ctr, payload_blocks + n),
+                     "gcm_layer_encrypt": (GHASH_WAVEFRONTS_PER_BLOCK, payload_blocks + 5 * n)}
         smem = {k: round(w * b / (prof[k][0] * 1e-6 * sms * sm_hz), 4) for k, (w, b) in per_block.items() if k in prof}
         result = {
             "metric": "Verified KV writeback GB/s/GPU (gather+quantise+AES-GCM encrypt+tag); per-layer us",

@@ -322,12 +322,14 @@ struct Aes4Tables {
     }
 };
 
-__device__ __forceinline__ uint4 aes128_encrypt_t4(uint4 in, const Aes4Tables& T, const uint32_t* __restrict__ rk)
+// Rounds first .. 10 of AES-128 on state s (the output of round first - 1).
+__device__ __forceinline__ uint4 aes128_rounds_from(uint4 s, int first, const Aes4Tables& T,
+                                                    const uint32_t* __restrict__ rk)
 {
-    uint32_t s0 = in.x ^ rk[0], s1 = in.y ^ rk[1], s2 = in.z ^ rk[2], s3 = in.w ^ rk[3];
+    uint32_t s0 = s.x, s1 = s.y, s2 = s.z, s3 = s.w;
 #pragma unroll
-    for (int r = 1; r < 10; ++r) {
-        const uint4 k4 = *reinterpret_cast<const uint4*>(rk + 4 * r);
+    for (int r = first; r < 10; ++r) {
+        const uint4 k4 = make_uint4(rk[4 * r], rk[4 * r + 1], rk[4 * r + 2], rk[4 * r + 3]);
         const uint32_t t0 = T.look(0, s0, 0) ^ T.look(1, s1, 1) ^ T.look(2, s2, 2) ^ T.look(3, s3, 3) ^ k4.x;
         const uint32_t t1 = T.look(0, s1, 0) ^ T.look(1, s2, 1) ^ T.look(2, s3, 2) ^ T.look(3, s0, 3) ^ k4.y;
         const uint32_t t2 = T.look(0, s2, 0) ^ T.look(1, s3, 1) ^ T.look(2, s0, 2) ^ T.look(3, s1, 3) ^ k4.z;
@@ -336,7 +338,7 @@ __device__ __forceinline__ uint4 aes128_encrypt_t4(uint4 in, const Aes4Tables& T
     }
     // Final round: S(x) sits in byte 0 of Te2, byte 1 of Te3, byte 2 of Te0,
     // byte 3 of Te1; PRMT gathers the four bytes of each output column.
-    const uint4 k4 = *reinterpret_cast<const uint4*>(rk + 40);
+    const uint4 k4 = make_uint4(rk[40], rk[41], rk[42], rk[43]);
     auto column = [&](uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
         const uint32_t lo = __byte_perm(T.look(2, a, 0), T.look(3, b, 1), 0x0050u);
         const uint32_t hi = __byte_perm(T.look(0, c, 2), T.look(1, d, 3), 0x7200u);
@@ -344,6 +346,11 @@ __device__ __forceinline__ uint4 aes128_encrypt_t4(uint4 in, const Aes4Tables& T
     };
     return make_uint4(column(s0, s1, s2, s3) ^ k4.x, column(s1, s2, s3, s0) ^ k4.y,
                       column(s2, s3, s0, s1) ^ k4.z, column(s3, s0, s1, s2) ^ k4.w);
+}
+
+__device__ __forceinline__ uint4 aes128_encrypt_t4(uint4 in, const Aes4Tables& T, const uint32_t* __restrict__ rk)
+{
+    return aes128_rounds_from(make_uint4(in.x ^ rk[0], in.y ^ rk[1], in.z ^ rk[2], in.w ^ rk[3]), 1, T, rk);
 }
 
 __device__ __forceinline__ void fill_aes4_smem(uint8_t* smem, const GcmSchedule* S)
@@ -649,7 +656,48 @@ __device__ __forceinline__ void layer_iv(uint32_t iv0, uint64_t ticket, uint32_t
     iv[3] = 2u;
 }
 
+// Counter-mode constants of one record (IV words iv[0..2], counters below
+// 2^16).  After AddRoundKey 0 the state is s0..s2 = IV ^ rk, s3 = BE32(ctr) ^
+// rk[3]; only bytes 14 and 15 of the counter change, and they reach round 1's
+// columns 1 and 0 alone.  So round 1 is t0 = a0 ^ Te3[byte 15],
+// t1 = a1 ^ Te2[byte 14], t2 = a2, t3 = a3, and round 2 needs the eight
+// lookups of t0 and t1 beside the constants b0..b3 (Bernstein and Schwabe's
+// counter-mode caching for table AES): 138 lookups per block instead of 176.
+struct CtrCache {
+    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+};
+
+__device__ __forceinline__ CtrCache ctr_cache(const uint32_t iv[4], const Aes4Tables& T, const uint32_t* __restrict__ rk)
+{
+    const uint32_t s0 = bswap32(iv[0]) ^ rk[0], s1 = bswap32(iv[1]) ^ rk[1], s2 = bswap32(iv[2]) ^ rk[2];
+    const uint32_t s3 = rk[3];   // counter bytes 12 and 13 are zero; 14 and 15 are looked up per block
+    CtrCache K;
+    K.a0 = T.look(0, s0, 0) ^ T.look(1, s1, 1) ^ T.look(2, s2, 2) ^ rk[4];
+    K.a1 = T.look(0, s1, 0) ^ T.look(1, s2, 1) ^ T.look(3, s0, 3) ^ rk[5];
+    K.a2 = T.look(0, s2, 0) ^ T.look(1, s3, 1) ^ T.look(2, s0, 2) ^ T.look(3, s1, 3) ^ rk[6];
+    K.a3 = T.look(0, s3, 0) ^ T.look(1, s0, 1) ^ T.look(2, s1, 2) ^ T.look(3, s2, 3) ^ rk[7];
+    K.b0 = T.look(2, K.a2, 2) ^ T.look(3, K.a3, 3) ^ rk[8];
+    K.b1 = T.look(1, K.a2, 1) ^ T.look(2, K.a3, 2) ^ rk[9];
+    K.b2 = T.look(0, K.a2, 0) ^ T.look(1, K.a3, 1) ^ rk[10];
+    K.b3 = T.look(0, K.a3, 0) ^ T.look(3, K.a2, 3) ^ rk[11];
+    return K;
+}
+
+// E_K(IV || BE32(ctr)) for ctr < 2^16 from the record's constants.
+__device__ __forceinline__ uint4 aes128_ctr_cached(uint32_t ctr, const CtrCache& K, const Aes4Tables& T,
+                                                   const uint32_t* __restrict__ rk)
+{
+    const uint32_t s3 = bswap32(ctr) ^ rk[3];
+    const uint32_t t0 = K.a0 ^ T.look(3, s3, 3), t1 = K.a1 ^ T.look(2, s3, 2);
+    uint32_t s[4] = {K.b0 ^ T.look(0, t0, 0) ^ T.look(1, t1, 1), K.b1 ^ T.look(0, t1, 0) ^ T.look(3, t0, 3),
+                     K.b2 ^ T.look(2, t0, 2) ^ T.look(3, t1, 3), K.b3 ^ T.look(1, t0, 1) ^ T.look(2, t1, 2)};
+    return aes128_rounds_from(make_uint4(s[0], s[1], s[2], s[3]), 3, T, rk);
+}
+
 // Keystream of every record plus E_K(J0) in the record's last 16 bytes.
+// Each CTA takes one contiguous range of the layer's (record, block) space and
+// its threads stride through it, so a thread meets at most a few records and
+// derives each record's counter-mode constants once.
 template <int kCap>
 __global__ void __launch_bounds__(kLayerCtrThreads, 1) gcm_layer_ctr_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
@@ -659,19 +707,45 @@ __global__ void __launch_bounds__(kLayerCtrThreads, 1) gcm_layer_ctr_kernel(cons
     // The keystream buffer may still be read by the previous verify grid.
     allow_dependent_launch();
     grid_dependency_wait();
-    const uint32_t* rk = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
+    // Round keys in registers: the lookups are the kernel's only shared loads.
+    uint32_t rk[44];
+#pragma unroll
+    for (int i = 0; i < 44; ++i) rk[i] = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes)[i];
     const Aes4Tables T = aes4_view(smem);
     const uint32_t payload_blocks = static_cast<uint32_t>((L.h.count + 15) >> 4);
     const uint32_t nb = payload_blocks + 1;
     const uint32_t total = nb * L.h.n;
-    for (uint32_t gb = blockIdx.x * blockDim.x + threadIdx.x; gb < total; gb += gridDim.x * blockDim.x) {
-        const uint32_t r = gb / nb, c = gb - r * nb;
-        uint32_t iv[4];
-        layer_iv(L.h.iv0, L.rec[r].ticket, iv);
+    // Counters 2 .. payload_blocks + 1 (and 1 for J0) below 2^16: cached rounds.
+    const bool cached = payload_blocks + 2u <= 65536u;
+    const uint32_t per_cta = (total + gridDim.x - 1) / gridDim.x;
+    const uint32_t beg = blockIdx.x * per_cta;
+    const uint32_t end = beg + per_cta < total ? beg + per_cta : total;
+    // (record, block) of the thread's position, advanced without a division.
+    uint32_t gb = beg + threadIdx.x;
+    uint32_t r = gb / nb, c = gb - r * nb;
+    uint32_t cur = ~0u;
+    uint32_t iv[4] = {0, 0, 0, 0};
+    CtrCache K{};
+    for (; gb < end; gb += blockDim.x) {
+        if (r != cur) {
+            layer_iv(L.h.iv0, L.rec[r].ticket, iv);
+            if (cached) K = ctr_cache(iv, T, rk);
+            cur = r;
+        }
         uint8_t* out = L.h.ks + static_cast<uint64_t>(r) * L.h.ks_stride + 16ull * c;
-        const uint4 in = c == payload_blocks ? j0_block_le(iv) : ctr_block_le(iv, c);
-        const uint4 ks = aes128_encrypt_t4(in, T, rk);
+        uint4 ks;
+        if (cached) {
+            ks = aes128_ctr_cached(c == payload_blocks ? 1u : 2u + c, K, T, rk);
+        } else {
+            const uint4 in = c == payload_blocks ? j0_block_le(iv) : ctr_block_le(iv, c);
+            ks = aes128_encrypt_t4(in, T, rk);
+        }
         if (L.h.unaligned) store_partial16(out, ks, 16); else *reinterpret_cast<uint4*>(out) = ks;
+        c += blockDim.x;
+        while (c >= nb) {
+            c -= nb;
+            ++r;
+        }
     }
 }
 
