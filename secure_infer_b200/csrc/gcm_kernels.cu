@@ -1140,7 +1140,20 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
         Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
         if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
         Y = xor4(Y, shfl_xor4(Y, 8));
-        const uint4 part = xor4(Y, shfl_xor4(Y, 16));
+        uint4 part = xor4(Y, shfl_xor4(Y, 16));
+        // The record's GHASH is S = sum_k p_k H^(L (nseg - 1 - k)), L = 32
+        // seg_steps blocks per segment.  With at most 64 segments each warp
+        // scales its own partial by H^(L e), e = nseg - 1 - k, one warp-wide
+        // product per set bit of e (tables H^(L 2^b), b = 0..5), so the warp
+        // that completes the record only XORs the partials.
+        const bool prescaled = nseg <= 64u;
+        if (prescaled) {
+            const uint32_t e = nseg - 1u - k;
+#pragma unroll
+            for (int b = 0; b < 5; ++b)
+                if (e & (1u << b)) part = gf_mul_warp<false>(part, jtab + 512 * b, static_cast<int>(lane));
+            if (e & 32u) part = gf_mul_warp<true>(part, L.h.join_pow + 4 * 512, static_cast<int>(lane));
+        }
 
         __threadfence();
         __syncwarp();
@@ -1153,14 +1166,18 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
-        // Join the record's partials, S = sum_k p_k H^(L (nseg - 1 - k)) with
-        // L = 32 seg_steps blocks per segment: chunks of 32 partials (the
-        // first chunk takes the remainder), each reduced by a tree over the
-        // lanes (level b combines pairs of 2^b-partial groups with H^(L 2^b)),
-        // chunks joined by Horner with H^(32 L).
         uint4 acc = zero4();
+        if (prescaled) {
+            uint4 v = zero4();
+            for (uint32_t i = lane; i < nseg; i += 32) v = xor4(v, __ldcg(&L.h.partials[r * nseg + i]));
+            acc = warp_xor_reduce(v);
+        }
+        // Otherwise join the partials here: chunks of 32 partials (the first
+        // chunk takes the remainder), each reduced by a tree over the lanes
+        // (level b combines pairs of 2^b-partial groups with H^(L 2^b)),
+        // chunks joined by Horner with H^(32 L).
         const uint32_t first = nseg - (nseg - 1) / 32 * 32;
-        for (uint32_t k0 = 0; k0 < nseg;) {
+        for (uint32_t k0 = 0; !prescaled && k0 < nseg;) {
             const uint32_t cnt = k0 == 0 ? first : 32;
             const uint32_t pad = 32 - cnt;     // zero partials in front keep the powers aligned
             uint4 v = lane >= pad ? __ldcg(&L.h.partials[r * nseg + k0 + lane - pad]) : zero4();
@@ -1331,7 +1348,17 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
         Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
         if (quarter != 3) Y = gf_mul_table<1, true>(Y, S->tab[tab_pow_small(8 * (3 - static_cast<int>(quarter)))], 0);
         Y = xor4(Y, shfl_xor4(Y, 8));
-        const uint4 part = xor4(Y, shfl_xor4(Y, 16));
+        uint4 part = xor4(Y, shfl_xor4(Y, 16));
+        // Pre-scaled partials as in gcm_layer_verify_kernel (tables H^(L 2^b):
+        // b = 0 from the schedule, b = 1..5 from the session join tables).
+        const bool prescaled = nseg <= 64u;
+        if (prescaled) {
+            const uint32_t e = nseg - 1u - k;
+            if (e & 1u) part = gf_mul_warp<true>(part, S->tab[tab_pow_32k(static_cast<int>(seg_steps))], static_cast<int>(lane));
+#pragma unroll
+            for (int b = 1; b < 6; ++b)
+                if (e & (1u << b)) part = gf_mul_warp<true>(part, L.h.join_pow + 512 * (b - 1), static_cast<int>(lane));
+        }
 
         __threadfence();
         __syncwarp();
@@ -1344,12 +1371,18 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
-        // Join the record's partials as gcm_layer_verify_kernel does: level b
-        // of the lane tree multiplies by H^(L 2^b) (b = 0 from the schedule,
-        // b = 1..4 from the session join tables), chunks of 32 by H^(32 L).
         uint4 acc = zero4();
+        if (prescaled) {
+            uint4 v = zero4();
+            for (uint32_t i = lane; i < nseg; i += 32) v = xor4(v, __ldcg(&L.h.partials[r * nseg + i]));
+            acc = warp_xor_reduce(v);
+        }
+        // Otherwise join the record's partials as gcm_layer_verify_kernel does:
+        // level b of the lane tree multiplies by H^(L 2^b) (b = 0 from the
+        // schedule, b = 1..4 from the session join tables), chunks of 32 by
+        // H^(32 L).
         const uint32_t first = nseg - (nseg - 1) / 32 * 32;
-        for (uint32_t k0 = 0; k0 < nseg;) {
+        for (uint32_t k0 = 0; !prescaled && k0 < nseg;) {
             const uint32_t cnt = k0 == 0 ? first : 32;
             const uint32_t pad = 32 - cnt;
             uint4 v = lane >= pad ? __ldcg(&L.h.partials[r * nseg + k0 + lane - pad]) : zero4();
