@@ -502,7 +502,9 @@ def attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, suffix:
     w_qkv, w_o = rnd(hid, (qh + 2 * H) * D, scale=0.02), rnd(qh * D, hid, scale=0.02)
     w_gu, w_d = rnd(hid, 2 * ffn, scale=0.02), rnd(ffn, hid, scale=0.02)
     kbuf, vbuf = rnd(P + S, H, D), rnd(P + S, H, D)
-    ls, cs = torch.cuda.Stream(), torch.cuda.Stream()
+    # The load stream at high priority, as the connector's: the reload's
+    # kernels are scheduled ahead of the compute that waits for them.
+    ls, cs = torch.cuda.Stream(priority=-1), torch.cuda.Stream()
     lsp = ct.c_void_p(ls.cuda_stream)
 
     def attend(layer, q):

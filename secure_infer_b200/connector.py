@@ -25,6 +25,7 @@ cost models, entry gate) stays with the serving engine.
 """
 from __future__ import annotations
 
+import ctypes as ct
 import itertools
 import threading
 import time
@@ -57,7 +58,9 @@ class LayerwiseReloader:
         self.timeout = timeout
         self.device = kv_caches[0][0].device
         self.heads = kv_caches[0][0].shape[2]
-        self.load_stream = torch.cuda.Stream(device=self.device)
+        # High priority: attention waits on this stream's reloads, so their
+        # kernels are scheduled ahead of normal-priority compute.
+        self.load_stream = torch.cuda.Stream(device=self.device, priority=-1)
         self.lock = threading.Condition()
         self.submission_lock = threading.Lock()
         self.load_jobs: dict = {}
@@ -139,16 +142,20 @@ class LayerwiseReloader:
         observer = threading.Thread(target=self._observe_layers, args=(state,), daemon=True)
         observer.start()
         try:
+            # Every layer's argument arrays are built before the first reload,
+            # so the loop below holds the GIL only between library calls and
+            # the model thread's attention launches are not held up per layer.
+            arrays = [transfer.layer_arrays((self.cpu_tensors[layer], mapping), self.kv_caches[layer], layer)
+                      for layer in range(len(self.names))]
+            stream = ct.c_void_p(self.load_stream.cuda_stream)
             with torch.cuda.stream(self.load_stream):
                 for layer in range(len(self.names)):
                     with self.lock:
                         if state["error"]:
                             raise RuntimeError(state["error"])
                     if self.lookahead and layer + 1 < len(self.names):
-                        transfer.prepare_layer((self.cpu_tensors[layer + 1], mapping), self.heads, layer=layer + 1)
-                    transfer.layer = layer
-                    transfer.single_layer_kv_transfer((self.cpu_tensors[layer], mapping), self.kv_caches[layer],
-                                                      stream=self.load_stream)
+                        transfer.prepare_arrays(arrays[layer + 1])
+                    transfer.reload_arrays(arrays[layer], stream)
                     ready = torch.cuda.Event()
                     ready.record(self.load_stream)
                     with self.lock:

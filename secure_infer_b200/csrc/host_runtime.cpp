@@ -1735,6 +1735,16 @@ SI_EXPORT int secure_infer_session_init_key_agreement(int device)
 }
 
 namespace {
+// The keystream producer runs at the device's highest stream priority: a
+// reload's kernels gate the attention that waits for its layer, so their CTAs
+// are scheduled ahead of compute work queued on normal-priority streams.
+cudaError_t create_priority_stream(cudaStream_t* s)
+{
+    int least = 0, greatest = 0;
+    if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) greatest = 0;
+    return cudaStreamCreateWithPriority(s, cudaStreamNonBlocking, greatest);
+}
+
 int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt4, const void* device_key)
 {
     shutdown_locked();
@@ -1761,7 +1771,7 @@ int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt
         !CUDA_OK(cudaMalloc(&g_s.join_tabs, sib::join_tables_bytes())) || !CUDA_OK(cudaMalloc(&dkey, 16)) ||
         !CUDA_OK(device_key ? cudaMemcpy(dkey, device_key, 16, cudaMemcpyDeviceToDevice)
                             : cudaMemcpy(dkey, key16, 16, cudaMemcpyHostToDevice)) ||
-        !CUDA_OK(cudaStreamCreateWithFlags(&g_s.producer, cudaStreamNonBlocking)) ||
+        !CUDA_OK(create_priority_stream(&g_s.producer)) ||
         !CUDA_OK(cudaStreamCreateWithFlags(&g_s.copier, cudaStreamNonBlocking)) ||
         !CUDA_OK(cudaEventCreateWithFlags(&g_s.consumed_ev, cudaEventDisableTiming)) ||
         !CUDA_OK(cudaEventCreateWithFlags(&g_s.produced_ev, cudaEventDisableTiming))) {

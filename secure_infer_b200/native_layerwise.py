@@ -134,6 +134,15 @@ def register_host_range(tensor: torch.Tensor, layer_id: int | None = None, tenso
                                             0 if tensor_kind is None else tensor_kind, block_bytes)
 
 
+class LayerArrays:
+    """ctypes arguments of one layer's reload (NativeTransfer.layer_arrays)."""
+    __slots__ = ("layer", "srcs", "dsts", "n", "count", "codec", "codec_arg")
+
+    def __init__(self, layer, srcs, dsts, n, count, codec):
+        self.layer, self.srcs, self.dsts, self.n, self.count, self.codec = layer, srcs, dsts, n, count, codec
+        self.codec_arg = ct.byref(codec) if codec is not None else None
+
+
 class NativeTransfer:
     """Per-layer reload of mapped blocks (native_layerwise.py:94-130).
 
@@ -191,6 +200,35 @@ class NativeTransfer:
         if rc != 0:
             raise RuntimeError(f"secure_infer_h2d_reload_layer failed for layer {layer}")
         self.layer += 1
+
+    def layer_arrays(self, payload, destination, layer: int) -> "LayerArrays":
+        """The C-ABI argument arrays of one layer's reload (K records, then V),
+        built once so a caller that reloads many layers back to back (the
+        connector's fetch thread) spends no Python time per layer beyond the
+        two library calls."""
+        host, mapping = payload
+        srcs, count, codec = self._sources(host, mapping, destination[0].shape[2], layer)
+        dst_idx = mapping[:, 1].tolist()
+        dsts = []
+        for dst in destination:
+            dstride = dst.stride(0) * dst.element_size()
+            dsts += [dst.data_ptr() + i * dstride for i in dst_idx]
+        return LayerArrays(layer, _ptrs(srcs), _ptrs(dsts), len(srcs), count, codec)
+
+    def reload_arrays(self, a: "LayerArrays", stream: ct.c_void_p) -> None:
+        """secure_infer_h2d_reload_layer of prepared arrays on `stream` (a raw
+        stream handle)."""
+        rc = self.lib.secure_infer_h2d_reload_layer(a.layer, a.srcs, a.dsts, a.n, a.count, a.codec_arg, 0, None,
+                                                    stream)
+        if rc != 0:
+            raise RuntimeError(f"secure_infer_h2d_reload_layer failed for layer {a.layer}")
+
+    def prepare_arrays(self, a: "LayerArrays") -> bool:
+        """secure_infer_h2d_prepare_layer (the lookahead) of prepared arrays."""
+        rc = self.lib.secure_infer_h2d_prepare_layer(a.layer, a.srcs, a.n, a.count, a.codec_arg)
+        if rc < 0:
+            raise RuntimeError(f"secure_infer_h2d_prepare_layer failed for layer {a.layer}")
+        return rc == 0
 
     def prepare_layer(self, payload, heads: int, layer: int | None = None) -> bool:
         """Announce the reload of ``payload`` for ``layer`` (default: the next

@@ -26,6 +26,8 @@ class FakeEvent:
 
 
 class FakeStream:
+    cuda_stream = 0
+
     def __init__(self, *a, **k):
         self.waited = []
 
@@ -99,6 +101,16 @@ class FakeTransfer:
         if self.layer == FakeTransfer.raise_on_layer:
             FakeTransfer.gate.wait(timeout=30)
             raise ValueError(f"transfer of layer {self.layer} refused")
+
+    def layer_arrays(self, payload, destination, layer):
+        return layer
+
+    def prepare_arrays(self, arrays):
+        return True
+
+    def reload_arrays(self, layer, stream):
+        self.layer = layer
+        self.single_layer_kv_transfer(None, None, stream)
 
 
 @pytest.fixture
