@@ -178,6 +178,26 @@ int secure_infer_h2d_reload_layer(uint32_t layer, const void* const* srcs, void*
                                   uint64_t count, const secure_infer_codec* codec, int records_are_encrypted,
                                   const uint64_t* tickets, void* stream);
 
+/* The connector's per-layer fetch loop (reuse/connector.py:222-331, as
+ * `RuntimeWorker.fetch_serialized`) run by a library thread, so no reload of a
+ * request waits for the caller's interpreter.  Layers first_layer ..
+ * first_layer + nlayers - 1; layer i reloads the n records srcs[i*n ..
+ * (i+1)*n) into dsts[i*n .. (i+1)*n) (K records first, as
+ * secure_infer_h2d_reload_layer) with counts[i] bytes each and codecs[i]
+ * (NULL: all raw; bits 0: raw layer), on `stream`, announcing layer i + 1
+ * before reloading layer i when `lookahead` is set.  Returns at once (0, or
+ * -1 on bad arguments); the arrays are copied.  For a layer of the request,
+ * secure_infer_recovery_wait_layer_authentication and
+ * secure_infer_layer_ready_wait first wait until the thread has submitted it
+ * (-1 if that submission failed).  One request at a time: a new one, a
+ * session init or shutdown first joins the previous.  No separate reference
+ * export: the reference runs this loop in Python. */
+int secure_infer_h2d_reload_layers_async(uint32_t first_layer, uint32_t nlayers, const void* const* srcs,
+                                         void* const* dsts, uint32_t n, const uint64_t* counts,
+                                         const secure_infer_codec* codecs, int lookahead, void* stream);
+/* Joins the request's thread: 0, or -1 if a reload could not be submitted. */
+int secure_infer_h2d_reload_layers_join(void);
+
 /* Record the completion event of the last reload of `layer` on `stream`
  * (device-side release of attention; no host wait).  -1 if none. */
 int secure_infer_layer_ready_wait(uint32_t layer, void* stream);

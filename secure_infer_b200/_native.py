@@ -61,6 +61,8 @@ HOST_SIGNATURES: dict[str, tuple[list, object]] = {
     "secure_infer_verify_records": ([U32, P, U64, U64, U32, U64P, PP, P, P, P, P], I32),
     "secure_infer_h2d_reload_layer": ([U32, PP, PP, U32, U64, P, I32, U64P, P], I32),
     "secure_infer_h2d_prepare_layer": ([U32, PP, U32, U64, P], I32),
+    "secure_infer_h2d_reload_layers_async": ([U32, U32, PP, PP, U32, U64P, P, I32, P], I32),
+    "secure_infer_h2d_reload_layers_join": ([], I32),
     "secure_infer_layer_ready_wait": ([U32, P], I32),
     "secure_infer_h2d_layer_group_begin": ([SZ], I32),
     "secure_infer_h2d_layer_group_end": ([], I32),

@@ -46,7 +46,7 @@ class LayerwiseReloader:
     _jobs = itertools.count(1)
 
     def __init__(self, names, kv_caches, cpu_tensors, mode: str | None = None, lookahead: bool = True,
-                 timeout: float = 120.0):
+                 timeout: float = 120.0, native_loop: bool = True):
         if not (len(names) == len(kv_caches) == len(cpu_tensors)):
             raise ValueError("names, kv_caches and cpu_tensors differ in length")
         self.lib = _native.lib()
@@ -56,6 +56,9 @@ class LayerwiseReloader:
         self.mode = mode if mode is not None else settings()[0]
         self.lookahead = lookahead
         self.timeout = timeout
+        # Run each request's layer loop on a library thread when the library
+        # has secure_infer_h2d_reload_layers_async (otherwise in the fetch thread).
+        self.native_loop = native_loop
         self.device = kv_caches[0][0].device
         self.heads = kv_caches[0][0].shape[2]
         # High priority: attention waits on this stream's reloads, so their
@@ -141,13 +144,23 @@ class LayerwiseReloader:
         self.load_stream.wait_event(state["producer_event"])
         observer = threading.Thread(target=self._observe_layers, args=(state,), daemon=True)
         observer.start()
+        native = None
         try:
-            # Every layer's argument arrays are built before the first reload,
-            # so the loop below holds the GIL only between library calls and
-            # the model thread's attention launches are not held up per layer.
+            # Every layer's argument arrays are built before the first reload.
             arrays = [transfer.layer_arrays((self.cpu_tensors[layer], mapping), self.kv_caches[layer], layer)
                       for layer in range(len(self.names))]
             stream = ct.c_void_p(self.load_stream.cuda_stream)
+            if self.native_loop and hasattr(self.lib, "secure_infer_h2d_reload_layers_async"):
+                # The layer loop runs on a library thread: no reload waits for
+                # the interpreter while the model thread launches attention.
+                # Each layer's authentication wait and device-side release
+                # block until that layer has been submitted.
+                native = self._start_native_loop(arrays, stream)
+                with self.lock:
+                    state["native"] = True
+                    state["submitted"] = [True] * len(self.names)
+                    self.lock.notify_all()
+                return
             with torch.cuda.stream(self.load_stream):
                 for layer in range(len(self.names)):
                     with self.lock:
@@ -172,13 +185,37 @@ class LayerwiseReloader:
                 state["submissions_done"] = True
                 self.lock.notify_all()
             observer.join(timeout=self.timeout)
-            if self.lookahead:
+            if native is not None:
+                if self.lib.secure_infer_h2d_reload_layers_join() != 0:
+                    with self.lock:
+                        state["error"] = state["error"] or "secure_infer_h2d_reload_layers_async: a reload failed"
+            elif self.lookahead:
                 self.lib.secure_infer_retire_transfer_prefetches()
             with self.lock:
                 if observer.is_alive():
                     state["error"] = state["error"] or "authentication observer timeout"
                 elif not state["error"] and not all(state["authenticated"]):
                     state["error"] = "layers left unauthenticated"
+
+    def _start_native_loop(self, arrays, stream):
+        """secure_infer_h2d_reload_layers_async over the request's layers; the
+        argument arrays are kept alive with the request state."""
+        n = arrays[0].n
+        srcs = (ct.c_void_p * (n * len(arrays)))()
+        dsts = (ct.c_void_p * (n * len(arrays)))()
+        for i, a in enumerate(arrays):
+            if a.n != n:
+                raise ValueError("every layer of a request reloads the same blocks")
+            srcs[i * n:(i + 1) * n] = a.srcs[:]
+            dsts[i * n:(i + 1) * n] = a.dsts[:]
+        counts = (ct.c_uint64 * len(arrays))(*[a.count for a in arrays])
+        codecs = (_native.Codec * len(arrays))(*[a.codec if a.codec is not None else _native.Codec(0, 0, 0, 0)
+                                                 for a in arrays])
+        rc = self.lib.secure_infer_h2d_reload_layers_async(0, len(arrays), srcs, dsts, n, counts, codecs,
+                                                           1 if self.lookahead else 0, stream)
+        if rc != 0:
+            raise RuntimeError("secure_infer_h2d_reload_layers_async refused the request")
+        return (srcs, dsts, counts, codecs)
 
     # ----------------------------------------------------------------- wait
     def wait_for_layer_load(self, name) -> None:
@@ -196,7 +233,12 @@ class LayerwiseReloader:
                 if state["error"]:
                     raise RuntimeError(state["error"])
                 ready = state["ready_events"][layer]
-            stream.wait_event(ready)
+                native = state.get("native", False)
+            if native:
+                if self.lib.secure_infer_layer_ready_wait(layer, ct.c_void_p(stream.cuda_stream)) != 0:
+                    raise RuntimeError(f"layer {layer} has no reload to wait for")
+            else:
+                stream.wait_event(ready)
         if layer == len(self.names) - 1:
             for state in self.consuming.values():
                 state["thread"].join(timeout=self.timeout)

@@ -1676,9 +1676,126 @@ namespace {
 int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt4, const void* device_key);
 }  // namespace
 
+// ------------------------------------------------ asynchronous layer loop
+// secure_infer_h2d_reload_layers_async: the connector's per-layer fetch loop
+// (reuse/connector.py:222-331) run by a library thread, so the reloads of a
+// request never wait for the Python interpreter while the model thread
+// launches attention.  One request at a time.
+namespace {
+struct AsyncReload {
+    uint32_t first = 0, nlayers = 0, n = 0;
+    std::vector<const void*> srcs;          // [nlayers][n]
+    std::vector<void*> dsts;                // [nlayers][n]
+    std::vector<uint64_t> counts;           // [nlayers]
+    std::vector<secure_infer_codec> codecs; // [nlayers], bits 0 = raw
+    bool lookahead = true;
+    cudaStream_t stream = nullptr;
+    std::vector<uint8_t> state;             // per layer: 0 pending, 1 submitted, 2 failed
+    int rc = 0;
+    std::thread worker;
+};
+std::mutex g_async_mu;
+std::condition_variable g_async_cv;
+std::shared_ptr<AsyncReload> g_async;
+
+}  // namespace
+
+extern "C" int secure_infer_h2d_reload_layer(uint32_t, const void* const*, void* const*, uint32_t, uint64_t,
+                                             const secure_infer_codec*, int, const uint64_t*, void*);
+extern "C" int secure_infer_h2d_prepare_layer(uint32_t, const void* const*, uint32_t, uint64_t,
+                                              const secure_infer_codec*);
+extern "C" void secure_infer_retire_transfer_prefetches(void);
+
+namespace {
+void async_worker(std::shared_ptr<AsyncReload> a)
+{
+    pin_library_thread();
+    const uint32_t n = a->n;
+    for (uint32_t i = 0; i < a->nlayers; ++i) {
+        // Announce the next layer first (pre-encryption lookahead); a refused
+        // announcement only means that layer is encrypted inline.
+        if (a->lookahead && i + 1 < a->nlayers)
+            secure_infer_h2d_prepare_layer(a->first + i + 1, &a->srcs[(i + 1ull) * n], n, a->counts[i + 1],
+                                           &a->codecs[i + 1]);
+        const int rc = secure_infer_h2d_reload_layer(a->first + i, &a->srcs[1ull * i * n], &a->dsts[1ull * i * n], n,
+                                                     a->counts[i], &a->codecs[i], 0, nullptr, a->stream);
+        {
+            std::lock_guard<std::mutex> lock(g_async_mu);
+            if (rc != 0) {
+                a->rc = -1;
+                for (uint32_t j = i; j < a->nlayers; ++j) a->state[j] = 2;
+            } else {
+                a->state[i] = 1;
+            }
+        }
+        g_async_cv.notify_all();
+        if (rc != 0) break;
+    }
+    if (a->lookahead) secure_infer_retire_transfer_prefetches();
+}
+
+// Waits until `layer` of the active asynchronous request (when it covers that
+// layer) has been submitted; false if its submission failed or the worker
+// gave no answer within two minutes.
+bool await_async_layer(uint32_t layer)
+{
+    std::unique_lock<std::mutex> lock(g_async_mu);
+    const std::shared_ptr<AsyncReload> a = g_async;
+    if (!a || layer < a->first || layer - a->first >= a->nlayers) return true;
+    const uint32_t i = layer - a->first;
+    if (!g_async_cv.wait_for(lock, std::chrono::seconds(120), [&] { return a->state[i] != 0; })) return false;
+    return a->state[i] == 1;
+}
+
+// Joins the active request's worker; its result (0, or -1 if a reload failed).
+int join_async()
+{
+    std::shared_ptr<AsyncReload> a;
+    {
+        std::lock_guard<std::mutex> lock(g_async_mu);
+        a = g_async;
+    }
+    if (!a) return 0;
+    if (a->worker.joinable()) a->worker.join();
+    std::lock_guard<std::mutex> lock(g_async_mu);
+    if (g_async == a) g_async.reset();
+    return a->rc;
+}
+}  // namespace
+
+SI_EXPORT int secure_infer_h2d_reload_layers_async(uint32_t first_layer, uint32_t nlayers, const void* const* srcs,
+                                                   void* const* dsts, uint32_t n, const uint64_t* counts,
+                                                   const secure_infer_codec* codecs, int lookahead, void* stream)
+{
+    if (srcs == nullptr || dsts == nullptr || counts == nullptr || nlayers == 0 || n == 0) return -1;
+    if (UINT32_MAX - first_layer < nlayers) return -1;
+    join_async();   // one request at a time
+    auto a = std::make_shared<AsyncReload>();
+    a->first = first_layer;
+    a->nlayers = nlayers;
+    a->n = n;
+    a->srcs.assign(srcs, srcs + 1ull * nlayers * n);
+    a->dsts.assign(dsts, dsts + 1ull * nlayers * n);
+    a->counts.assign(counts, counts + nlayers);
+    a->codecs.assign(nlayers, secure_infer_codec{});
+    if (codecs != nullptr) a->codecs.assign(codecs, codecs + nlayers);
+    a->lookahead = lookahead != 0;
+    a->stream = static_cast<cudaStream_t>(stream);
+    a->state.assign(nlayers, 0);
+    {
+        std::lock_guard<std::mutex> lock(g_async_mu);
+        g_async = a;
+    }
+    a->worker = std::thread(async_worker, a);
+    return 0;
+}
+
+SI_EXPORT int secure_infer_h2d_reload_layers_join(void) { return join_async(); }
+
 SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const uint8_t* iv_salt4)
 {
     if (key16 == nullptr || iv_salt4 == nullptr) return -1;
+    join_async();   // a running layer loop finishes under the old session
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     return session_init_locked(device, key16, iv_salt4, nullptr);
 }
@@ -1686,6 +1803,7 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
 SI_EXPORT int secure_infer_session_init_key_agreement(int device)
 {
     if (device < 0) return -1;
+    join_async();
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     shutdown_locked();
     if (!CUDA_OK(cudaSetDevice(device))) return -1;
@@ -1801,6 +1919,7 @@ int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt
 
 SI_EXPORT int secure_infer_session_shutdown(void)
 {
+    join_async();   // outside the session lock: the worker takes it per layer
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     shutdown_locked();
     return 0;
@@ -2009,6 +2128,7 @@ SI_EXPORT int secure_infer_h2d_prepare_layer(uint32_t layer, const void* const* 
 
 SI_EXPORT int secure_infer_layer_ready_wait(uint32_t layer, void* stream)
 {
+    if (!await_async_layer(layer)) return -1;
     std::lock_guard<std::recursive_mutex> lock(g_mu);
     auto it = g_s.last_event.find(layer);
     if (it == g_s.last_event.end()) return -1;
@@ -2044,6 +2164,7 @@ SI_EXPORT int secure_infer_h2d_submit(void* dst, size_t dst_capacity, const void
 
 SI_EXPORT int secure_infer_recovery_wait_layer_authentication(uint32_t layer)
 {
+    if (!await_async_layer(layer)) return -1;
     std::vector<std::shared_ptr<LayerBatch>> batches;
     {
         std::lock_guard<std::recursive_mutex> lock(g_mu);

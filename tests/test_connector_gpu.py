@@ -33,12 +33,12 @@ def env():
     s.close()
 
 
-def make_reloader(cpu, mode="none"):
+def make_reloader(cpu, mode="none", native_loop=True):
     from secure_infer_b200.connector import LayerwiseReloader
     caches = [[torch.zeros((CACHE, 128, HEADS, 128), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
               for _ in range(LAYERS)]
     names = [f"model.layers.{i}.self_attn" for i in range(LAYERS)]
-    return LayerwiseReloader(names, caches, cpu, mode=mode), caches, names
+    return LayerwiseReloader(names, caches, cpu, mode=mode, native_loop=native_loop), caches, names
 
 
 def run_model(reloader, names, caches, dest):
@@ -56,9 +56,12 @@ def expected(cpu, src):
                         for layer in range(LAYERS)])
 
 
-def test_two_requests_reload_all_layers(env):
+@pytest.mark.parametrize("native_loop", [True, False])
+def test_two_requests_reload_all_layers(env, native_loop):
+    """The layer loop on the library's thread (secure_infer_h2d_reload_layers_async)
+    or in the connector's fetch thread: the same blocks land either way."""
     nl, cpu = env
-    reloader, caches, names = make_reloader(cpu)
+    reloader, caches, names = make_reloader(cpu, native_loop=native_loop)
     for req, (src, dst) in enumerate([([3, 0, 7, 5], [10, 2, 4, 9]), ([11, 1], [0, 15])]):
         before = nl.prefetch_stats()
         reloader.start_load(f"req-{req}", src, dst)
