@@ -428,6 +428,7 @@ struct StageSlot {
     cudaEvent_t ks_ready = nullptr, copied = nullptr;   // staged reload: keystream / records landed
     std::shared_ptr<LayerBatch> owner;
     std::shared_ptr<struct Prepared> hold;   // pre-encrypted records the slot's copy reads
+    bool encrypting = false;       // a submission is encrypting into `host` with the session lock released
 };
 
 struct RetryInfo {
@@ -704,12 +705,14 @@ bool reserve_given_ticket(uint64_t t)
     return g_s.outstanding.erase(t) == 1;
 }
 
-void iv_for(uint64_t ticket, uint8_t iv[16])
+void iv_for_salt(const uint8_t salt[4], uint64_t ticket, uint8_t iv[16])
 {
-    std::memcpy(iv, g_s.salt, 4);
+    std::memcpy(iv, salt, 4);
     store_be64(iv + 4, ticket);   // session nonce 0 in GCM mode (secure_infer.cpp:242-245)
     store_be32(iv + 12, 2u);
 }
+
+void iv_for(uint64_t ticket, uint8_t iv[16]) { iv_for_salt(g_s.salt, ticket, iv); }
 
 void iv_words_for(uint64_t ticket, uint32_t w[4])
 {
@@ -1226,9 +1229,17 @@ void prep_shutdown()
 }
 
 // Encrypt + stage + device reload.  Returns the batch (not yet registered).
+// Notified when a submission stops encrypting into its staging slot.
+std::condition_variable_any g_slot_cv;
+
+// Caller holds g_mu.  With `held` (the caller's own, non-recursive hold of
+// g_mu) the host encryption runs with the session lock released: the slot is
+// marked `encrypting` so no other submission takes it, and authentication
+// waits, device-side releases and other submissions proceed meanwhile.
 std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* const* srcs, void* const* dsts, uint32_t n,
                                                 uint64_t count, const secure_infer_codec* codec, bool encrypted,
-                                                const uint64_t* given_tickets, cudaStream_t stream)
+                                                const uint64_t* given_tickets, cudaStream_t stream,
+                                                std::unique_lock<std::recursive_mutex>* held = nullptr)
 {
     if (!g_s.ready || srcs == nullptr || dsts == nullptr || n == 0 || count == 0) return nullptr;
     CodecParams cp;
@@ -1236,8 +1247,22 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
     if (!codec_geometry(codec, &cp, &packet, true)) return nullptr;
     if (cp.bits && cp.kind == SECURE_INFER_KIND_KV && (n & 1u)) return nullptr;
     const uint64_t stride = record_bytes(count);
-    StageSlot& slot = g_s.h2d[g_s.h2d_next];
-    g_s.h2d_next = (g_s.h2d_next + 1) % g_s.h2d.size();
+    // The next staging slot that no submission is encrypting into.
+    StageSlot* pick = nullptr;
+    for (;;) {
+        for (size_t t = 0; t < g_s.h2d.size() && pick == nullptr; ++t) {
+            const size_t i = (g_s.h2d_next + t) % g_s.h2d.size();
+            if (!g_s.h2d[i].encrypting) {
+                pick = &g_s.h2d[i];
+                g_s.h2d_next = (i + 1) % g_s.h2d.size();
+            }
+        }
+        if (pick != nullptr) break;
+        if (held == nullptr) return nullptr;    // every slot is being filled by a submission that released the lock
+        g_slot_cv.wait(*held);
+        if (!g_s.ready) return nullptr;
+    }
+    StageSlot& slot = *pick;
     if (slot.owner) harvest(*slot.owner);   // statuses leave the slot before reuse
     if (!ensure_stage(slot, stride * n, layer_ks_stride(count) * n, n, 0, true)) return nullptr;
     if (slot.done) cudaEventSynchronize(slot.done);
@@ -1278,15 +1303,24 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
         if (!encrypt_ring_locked(tickets.data(), srcs, n, count, stride, slot.dev)) return nullptr;
     } else if (!encrypted) {
         std::atomic<bool> ok{true};
-        const uint8_t* key = g_s.key;
+        uint8_t key[16], salt[4];
+        std::memcpy(key, g_s.key, 16);
+        std::memcpy(salt, g_s.salt, 4);
+        uint8_t* host = slot.host;
+        slot.encrypting = true;
+        if (held != nullptr) held->unlock();
         pool().parallel_for(n, [&](size_t i) {
             uint8_t iv[16], aad[64];
-            iv_for(tickets[i], iv);
+            iv_for_salt(salt, tickets[i], iv);
             build_aad(srcs[i], count, SECURE_INFER_DIRECTION_H2D, tickets[i], 0, 0, aad);
-            if (!encrypt_record(key, iv, aad, static_cast<const uint8_t*>(srcs[i]), count, slot.host + i * stride))
+            if (!encrypt_record(key, iv, aad, static_cast<const uint8_t*>(srcs[i]), count, host + i * stride))
                 ok = false;
         });
-        if (!ok) return nullptr;
+        OPENSSL_cleanse(key, sizeof(key));
+        if (held != nullptr) held->lock();
+        slot.encrypting = false;
+        g_slot_cv.notify_all();
+        if (!ok || !g_s.ready) return nullptr;
         for (uint32_t i = 0; i < n; ++i) maybe_tamper_h2d(slot.host + i * stride, count);
     }
 
@@ -1351,7 +1385,7 @@ int flush_submissions(std::vector<Submission>& subs)
         const uint32_t layer = lookup_range(subs[i].src, subs[i].count, &r, &block, &off) ? r.layer : UINT32_MAX;
         buckets[{layer, subs[i].count, subs[i].stream}].push_back(i);
     }
-    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    std::unique_lock<std::recursive_mutex> lock(g_mu);
     for (auto& kv : buckets) {
         std::vector<const void*> srcs;
         std::vector<void*> dsts;
@@ -1360,7 +1394,7 @@ int flush_submissions(std::vector<Submission>& subs)
             dsts.push_back(subs[i].dst);
         }
         auto b = submit_layer_locked(std::get<0>(kv.first), srcs.data(), dsts.data(), static_cast<uint32_t>(srcs.size()),
-                                     std::get<1>(kv.first), nullptr, false, nullptr, std::get<2>(kv.first));
+                                     std::get<1>(kv.first), nullptr, false, nullptr, std::get<2>(kv.first), &lock);
         if (!b) return -1;
         register_batch_locked(b);
     }
@@ -1747,6 +1781,17 @@ bool await_async_layer(uint32_t layer)
     return a->state[i] == 1;
 }
 
+// A session change waits for submissions that are encrypting into staging
+// slots with the session lock released (they take it back to finish).
+void wait_encrypting(std::unique_lock<std::recursive_mutex>& lock)
+{
+    g_slot_cv.wait(lock, [] {
+        for (const auto& slot : g_s.h2d)
+            if (slot.encrypting) return false;
+        return true;
+    });
+}
+
 // Joins the active request's worker; its result (0, or -1 if a reload failed).
 int join_async()
 {
@@ -1796,7 +1841,8 @@ SI_EXPORT int secure_infer_session_init(int device, const uint8_t* key16, const 
 {
     if (key16 == nullptr || iv_salt4 == nullptr) return -1;
     join_async();   // a running layer loop finishes under the old session
-    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    std::unique_lock<std::recursive_mutex> lock(g_mu);
+    wait_encrypting(lock);
     return session_init_locked(device, key16, iv_salt4, nullptr);
 }
 
@@ -1804,7 +1850,8 @@ SI_EXPORT int secure_infer_session_init_key_agreement(int device)
 {
     if (device < 0) return -1;
     join_async();
-    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    std::unique_lock<std::recursive_mutex> lock(g_mu);
+    wait_encrypting(lock);
     shutdown_locked();
     if (!CUDA_OK(cudaSetDevice(device))) return -1;
     // Host half (secure_infer.cpp:449-521): fresh X25519 secret and challenge.
@@ -1920,7 +1967,8 @@ int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt
 SI_EXPORT int secure_infer_session_shutdown(void)
 {
     join_async();   // outside the session lock: the worker takes it per layer
-    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    std::unique_lock<std::recursive_mutex> lock(g_mu);
+    wait_encrypting(lock);
     shutdown_locked();
     return 0;
 }
@@ -2063,9 +2111,9 @@ SI_EXPORT int secure_infer_h2d_reload_layer(uint32_t layer, const void* const* s
                                             uint64_t count, const secure_infer_codec* codec,
                                             int records_are_encrypted, const uint64_t* tickets, void* stream)
 {
-    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    std::unique_lock<std::recursive_mutex> lock(g_mu);
     auto b = submit_layer_locked(layer, srcs, dsts, n, count, codec, records_are_encrypted != 0, tickets,
-                                 static_cast<cudaStream_t>(stream));
+                                 static_cast<cudaStream_t>(stream), &lock);
     if (!b) return -1;
     register_batch_locked(b);
     return 0;
