@@ -1411,260 +1411,6 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
     }
 }
 
-// Warp-specialised fused reload for raw, 16-byte aligned records in device
-// memory (requests without a keystream buffer).  Each CTA runs kWsGroups
-// groups of one consumer warp and kWsProducers producer warps.  A group's
-// consumer takes (record, segment) items exactly as gcm_layer_verify_kernel's
-// warps do (Horner GHASH with H^32 byte tables, XOR, store, lane combine,
-// pre-scaled partials, the record's join and tag check).  Its producers walk
-// the same items and, step by step, encrypt the counter blocks the consumer's
-// lanes need (T-table AES with counter-mode caching, round keys in registers)
-// into a ring of kWsRing 512-byte slots in shared memory.  Slot use is
-// ordered by per-slot "full" and "empty" mbarriers.  So the AES lookups and
-// the GHASH lookups of one layer share each SM's shared-memory pipe at once,
-// and the keystream never crosses L2 or HBM.  Every wait is bounded: the first
-// wait that gives up raises a CTA-wide abort flag, every other wait then
-// returns at once, and the consumer's records fail closed (status 0, output
-// zeroed) instead of the kernel hanging.
-constexpr uint32_t kWsGroups = 4;
-constexpr uint32_t kWsProducers = 3;
-constexpr uint32_t kWsRing = 6;                                  // a multiple of kWsProducers
-constexpr uint32_t kWsThreads = kWsGroups * (1 + kWsProducers) * 32;
-constexpr size_t kWsRingOffset = kCtrTableBytes + 256 + kGhashSmem;
-constexpr size_t kWsSmem = kWsRingOffset + kWsGroups * kWsRing * 512;
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Waits for phase `parity` of `bar`, polling a bounded number of times and
-// giving up at once when another warp has raised `abort`; a wait that gives
-// up raises it.  Warp-uniform: every lane polls, all return the same answer.
-__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort)
-{
-    for (uint32_t it = 0; it < (1u << 20); ++it) {
-        uint32_t done;
-        asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}"
-                     : "=r"(done)
-                     : "r"(smem_u32(bar)), "r"(parity)
-                     : "memory");
-        if (__all_sync(0xffffffffu, done)) return true;
-        if ((it & 63u) == 63u && *abort) return false;
-    }
-    *abort = 1u;
-    return false;
-}
-
-template <int kCap>
-__global__ void __launch_bounds__(kWsThreads, 1) gcm_layer_verify_ws_kernel(const __grid_constant__ LayerLaunch<kCap> L)
-{
-    extern __shared__ __align__(16) uint8_t smem[];
-    uint4* gtab = reinterpret_cast<uint4*>(smem + kCtrTableBytes + 256);
-    uint4* ring = reinterpret_cast<uint4*>(smem + kWsRingOffset);   // [group][slot][lane]
-    __shared__ __align__(8) uint64_t gtab_bar;
-    __shared__ __align__(8) uint64_t full_bar[kWsGroups][kWsRing], empty_bar[kWsGroups][kWsRing];
-    __shared__ uint32_t abort_flag;
-    const GcmSchedule* __restrict__ S = L.h.sched;
-    const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-    const uint32_t group = warp % kWsGroups, role = warp / kWsGroups;   // role 0: consumer, 1..: producer
-    if (tid == 0) {
-        abort_flag = 0u;
-        for (uint32_t g = 0; g < kWsGroups; ++g)
-            for (uint32_t q = 0; q < kWsRing; ++q) {
-                mbar_init(&full_bar[g][q], 1u);
-                mbar_init(&empty_bar[g][q], 1u);
-            }
-        mbar_init_expect(&gtab_bar, 65536u);
-        bulk_g2s(gtab, S->byte32, 65536u, &gtab_bar);
-    }
-    fill_aes4_smem(smem, S);
-    __syncthreads();
-    allow_dependent_launch();
-    grid_dependency_wait();
-    const Aes4Tables T = aes4_view(smem);
-    volatile uint32_t* abort = &abort_flag;
-
-    const uint64_t count = L.h.count;
-    const uint32_t seg_steps = L.h.seg_steps;
-    const int64_t seg_blocks = 32 * static_cast<int64_t>(seg_steps);
-    const int64_t a_blk = 4;   // 64-byte AAD
-    const int64_t n_blk = static_cast<int64_t>((count + 15) >> 4);
-    const int64_t m = a_blk + n_blk + 1;
-    const uint32_t nseg = L.h.nseg;
-    const int64_t len0 = m - static_cast<int64_t>(nseg - 1) * seg_blocks;
-    const uint64_t tag_off = ((count + 31) & ~uint64_t(31)) ? ((count + 31) & ~uint64_t(31)) : 32;
-    const uint32_t total = nseg * L.h.n;
-    const bool cached = static_cast<uint64_t>(n_blk) + 2u <= 65536u;
-    uint4* my_ring = ring + static_cast<size_t>(group) * kWsRing * 32;
-
-    if (role != 0) {
-        // ------------------------------------------------------ producer
-        uint32_t rk[44];
-#pragma unroll
-        for (int i = 0; i < 44; ++i) rk[i] = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes)[i];
-        const uint32_t p = role - 1;
-        uint32_t t = 0, cur = ~0u;
-        uint32_t iv[4] = {0, 0, 0, 0};
-        CtrCache K{};
-        for (uint32_t w = blockIdx.x + gridDim.x * group; w < total; w += gridDim.x * kWsGroups) {
-            const uint32_t r = w / nseg, k = w - r * nseg;
-            const int64_t seg_end = len0 + static_cast<int64_t>(k) * seg_blocks;
-            const int64_t seg_len = k == 0 ? len0 : seg_blocks;
-            const int J = static_cast<int>((seg_len + 31) / 32);
-            const int64_t base = seg_end - static_cast<int64_t>(J) * 32;
-            if (r != cur) {
-                layer_iv(L.h.iv0, L.rec[r].ticket, iv);
-                if (cached) K = ctr_cache(iv, T, rk);
-                cur = r;
-            }
-            for (int j = 0; j < J; ++j, ++t) {
-                if (t % kWsProducers != p) continue;
-                const uint32_t slot = t % kWsRing, use = t / kWsRing;
-                if (use > 0 && !ws_wait(&empty_bar[group][slot], (use - 1u) & 1u, abort)) return;
-                const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
-                uint4 ks = zero4();
-                if (i >= a_blk && i < a_blk + n_blk) {
-                    const uint64_t c = static_cast<uint64_t>(i - a_blk);
-                    ks = cached ? aes128_ctr_cached(static_cast<uint32_t>(c) + 2u, K, T, rk)
-                                : aes128_encrypt_t4(ctr_block_le(iv, c), T, rk);
-                }
-                my_ring[slot * 32 + lane] = ks;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full_bar[group][slot]);
-            }
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------- consumer
-    const bool gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
-    const uint32_t rep = lane & 7u, quarter = lane >> 3;
-    const uint32_t* rk_s = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
-    const uint4 len_blk = len_block_le(64, count);
-    uint32_t t = 0;
-    for (uint32_t w = blockIdx.x + gridDim.x * group; w < total; w += gridDim.x * kWsGroups) {
-        const uint32_t r = w / nseg, k = w - r * nseg;
-        const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
-        const uint8_t* aad = in + tag_off + 32;
-        uint8_t* out = L.rec[r].dst;
-        const int64_t seg_end = len0 + static_cast<int64_t>(k) * seg_blocks;
-        const int64_t seg_len = k == 0 ? len0 : seg_blocks;
-        const int J = static_cast<int>((seg_len + 31) / 32);
-        const int64_t base = seg_end - static_cast<int64_t>(J) * 32;
-        const int64_t c0 = base + lane - a_blk;   // payload block of step 0 (negative on the AAD)
-        bool fine = gtab_ready;
-        uint4 Y = zero4();
-        // Ciphertext two steps ahead; the L2 bulk prefetch covers the segment.
-        if (lane == 0) {
-            const int64_t i0 = base > a_blk ? base : a_blk;
-            const int64_t i1 = seg_end < a_blk + n_blk ? seg_end : a_blk + n_blk;
-            if (i1 > i0) l2_prefetch_bulk(in + (i0 - a_blk) * 16, static_cast<uint32_t>(i1 - i0) * 16u);
-        }
-        auto load = [&](int j) -> uint4 {
-            const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
-            if (j >= J || i < 0) return zero4();
-            if (i < a_blk) return ldg16(aad + 16 * i);
-            if (i < a_blk + n_blk) {
-                const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
-                return count - off >= 16 ? ldg16(in + off) : load_partial16(in + off, count - off);
-            }
-            return len_blk;
-        };
-        uint4 x1 = load(0), x2 = load(1);
-#pragma unroll 1
-        for (int j = 0; j < J; ++j, ++t) {
-            const uint4 x = x1;
-            x1 = x2;
-            x2 = load(j + 2);
-            const uint32_t slot = t % kWsRing, use = t / kWsRing;
-            uint4 ks = zero4();
-            if (ws_wait(&full_bar[group][slot], use & 1u, abort)) {
-                ks = my_ring[slot * 32 + lane];
-            } else {
-                fine = false;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty_bar[group][slot]);
-            const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
-            if (i >= a_blk && i < a_blk + n_blk) {
-                const uint64_t off = static_cast<uint64_t>(c0 + 32ll * j) * 16u;
-                store_block(out + off, xor4(x, ks), count - off, true);
-            }
-            Y = xor4(gf_mul_byte8(Y, gtab, rep), x);
-        }
-
-        // Two-stage lane combine (tables through L1), pre-scaled partial.
-        if (!fine) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
-        Y = gf_mul_table<8, true>(Y, S->lane8, rep);                    // * H^(8 - r)
-        Y = xor4(Y, shfl_xor4(Y, 1));
-        Y = xor4(Y, shfl_xor4(Y, 2));
-        Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
-        if (quarter != 3) Y = gf_mul_table<1, true>(Y, S->tab[tab_pow_small(8 * (3 - static_cast<int>(quarter)))], 0);
-        Y = xor4(Y, shfl_xor4(Y, 8));
-        uint4 part = xor4(Y, shfl_xor4(Y, 16));
-        const bool prescaled = nseg <= 64u;
-        if (prescaled) {
-            const uint32_t e = nseg - 1u - k;
-            if (e & 1u) part = gf_mul_warp<true>(part, S->tab[tab_pow_32k(static_cast<int>(seg_steps))], static_cast<int>(lane));
-#pragma unroll
-            for (int b = 1; b < 6; ++b)
-                if (e & (1u << b)) part = gf_mul_warp<true>(part, L.h.join_pow + 512 * (b - 1), static_cast<int>(lane));
-        }
-        __threadfence();
-        __syncwarp();
-        uint32_t last = 0;
-        if (lane == 0) {
-            L.h.partials[w] = part;
-            __threadfence();
-            last = atomicAdd(&L.h.counters[r], 1u) == nseg - 1 ? 1u : 0u;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
-        uint4 acc = zero4();
-        if (prescaled) {
-            uint4 v = zero4();
-            for (uint32_t q = lane; q < nseg; q += 32) v = xor4(v, __ldcg(&L.h.partials[r * nseg + q]));
-            acc = warp_xor_reduce(v);
-        }
-        const uint32_t first = nseg - (nseg - 1) / 32 * 32;
-        for (uint32_t k0 = 0; !prescaled && k0 < nseg;) {
-            const uint32_t cnt = k0 == 0 ? first : 32;
-            const uint32_t pad = 32 - cnt;
-            uint4 v = lane >= pad ? __ldcg(&L.h.partials[r * nseg + k0 + lane - pad]) : zero4();
-#pragma unroll
-            for (int b = 0; b < 5; ++b) {
-                const uint4 left = shfl_up4(v, 1u << b);
-                const uint32_t grp = (2u << b) - 1u;
-                const uint4* tb = b == 0 ? S->tab[tab_pow_32k(static_cast<int>(seg_steps))] : L.h.join_pow + 512 * (b - 1);
-                if ((lane & grp) == grp) v = xor4(gf_mul_table<1, true>(left, tb, 0), v);
-            }
-            v = make_uint4(__shfl_sync(0xffffffffu, v.x, 31), __shfl_sync(0xffffffffu, v.y, 31),
-                           __shfl_sync(0xffffffffu, v.z, 31), __shfl_sync(0xffffffffu, v.w, 31));
-            acc = k0 == 0 ? v : xor4(gf_mul_warp<true>(acc, L.h.join_pow + 4 * 512, lane), v);
-            k0 += cnt;
-        }
-        uint32_t ivr[4];
-        layer_iv(L.h.iv0, L.rec[r].ticket, ivr);
-        const uint4 mask = aes128_encrypt_t4(j0_block_le(ivr), T, rk_s);
-        const bool ok = equal4(xor4(acc, mask), ldg16(in + tag_off));
-        if (lane == 0) {
-            L.h.status[r] = ok ? 1u : 0u;
-            L.h.counters[r] = 0u;
-        }
-        if (!ok) {
-            for (uint64_t off = static_cast<uint64_t>(lane) * 16u; off < count; off += 512u)
-                store_block(out + off, zero4(), count - off, true);
-        }
-    }
-}
-
 // ----------------------------------------------------------------------------
 // Writeback quantisation (transport_codec.py:22-42), one thread per group.
 // ----------------------------------------------------------------------------
@@ -2337,23 +2083,6 @@ int launch_layer_verify_inline(const LayerHeader& h, const LayerRec* rec, cudaSt
                                             rec, kInlineThreads, kInlineSmem, grid, set_small[dev & 63], stream, 1);
     return layer_launch<kLayerCapLarge>(kKernLayerVerifyInline, gcm_layer_verify_inline_kernel<kLayerCapLarge>, h, rec,
                                         kInlineThreads, kInlineSmem, grid, set_large[dev & 63], stream, 1);
-}
-
-int launch_layer_verify_ws(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)
-{
-    if (h.n == 0) return cudaSuccess;
-    if (h.n > static_cast<uint32_t>(kLayerCapLarge) || h.join_pow == nullptr || h.seg_steps < 1 ||
-        h.seg_steps > static_cast<uint32_t>(kMaxWarpSegSteps) || h.unaligned || h.codec.bits)
-        return cudaErrorInvalidValue;
-    static bool set_small[64], set_large[64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const uint32_t grid = (h.nseg * h.n + kWsGroups - 1) / kWsGroups;
-    if (h.n <= static_cast<uint32_t>(kLayerCapSmall))
-        return layer_launch<kLayerCapSmall>(kKernLayerVerifyInline, gcm_layer_verify_ws_kernel<kLayerCapSmall>, h, rec,
-                                            kWsThreads, kWsSmem, grid, set_small[dev & 63], stream, 1);
-    return layer_launch<kLayerCapLarge>(kKernLayerVerifyInline, gcm_layer_verify_ws_kernel<kLayerCapLarge>, h, rec,
-                                        kWsThreads, kWsSmem, grid, set_large[dev & 63], stream, 1);
 }
 
 int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream)

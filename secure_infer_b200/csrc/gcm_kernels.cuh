@@ -152,9 +152,6 @@ int launch_layer_encrypt(const LayerHeader& h, const LayerRec* rec, cudaStream_t
 // Fused verify with the AES keystream computed in the kernel (h.ks unused):
 // raw payloads (codec.bits 0), 16-byte aligned records and destinations.
 int launch_layer_verify_inline(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
-// The same request on the warp-specialised kernel (AES producer warps feed a
-// shared-memory keystream ring read by GHASH consumer warps).
-int launch_layer_verify_ws(const LayerHeader& h, const LayerRec* rec, cudaStream_t stream);
 
 // Kernel profile: while enabled, every launch below is bracketed by timing
 // events on its stream; collect() sums device time and launches per kind.

@@ -768,14 +768,6 @@ int keystream_records_locked(const uint64_t* tickets, uint32_t n, uint64_t count
     return 0;
 }
 
-// Keystream-less raw reloads run the warp-specialised kernel unless
-// SECURE_INFER_FUSED_VERIFY=inline selects the single-role one (read per call).
-bool fused_verify_ws()
-{
-    const char* v = std::getenv("SECURE_INFER_FUSED_VERIFY");
-    return v == nullptr || std::strcmp(v, "inline") != 0;
-}
-
 // Fused verify / XOR / (dequant) / scatter over n device-resident records.
 // Raw records with a keystream run on the layer kernel (descriptors in kernel
 // parameters); codec records and keystream-less requests use the CTA-segment
@@ -868,9 +860,7 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
             h.seg_steps = seg_steps;
             h.join_pow = sib::join_tables_for(g_s.join_tabs, seg_steps);
             for (uint32_t i = 0; i < m; ++i) recs[i] = LayerRec{static_cast<uint8_t*>(dsts[first + i]), tickets[first + i]};
-            if ((fused_verify_ws() ? launch_layer_verify_ws(h, recs.data(), stream)
-                                   : launch_layer_verify_inline(h, recs.data(), stream)) != cudaSuccess)
-                return -1;
+            if (launch_layer_verify_inline(h, recs.data(), stream) != cudaSuccess) return -1;
             cudaEventRecord(slot.free_ev, stream);
             slot.used = true;
         }
