@@ -1062,6 +1062,20 @@ struct PrepPool {
     uint64_t held = 0;                                // bytes of all pinned buffers
     std::thread worker;
     bool stop = false;
+
+    ~PrepPool()
+    {
+        // Process exit without secure_infer_session_shutdown(): stop the
+        // encryption thread and let it go (it may be inside OpenSSL).
+        if (worker.joinable()) {
+            {
+                std::lock_guard<std::mutex> lock(mu);
+                stop = true;
+            }
+            cv.notify_all();
+            worker.detach();
+        }
+    }
 } g_prep;
 
 uint64_t prep_pool_cap()
@@ -1727,6 +1741,13 @@ struct AsyncReload {
     std::vector<uint8_t> state;             // per layer: 0 pending, 1 submitted, 2 failed
     int rc = 0;
     std::thread worker;
+
+    // A request that was never joined (process exit) lets its thread go; the
+    // last owner may be that thread itself.
+    ~AsyncReload()
+    {
+        if (worker.joinable()) worker.detach();
+    }
 };
 std::mutex g_async_mu;
 std::condition_variable g_async_cv;

@@ -182,3 +182,28 @@ def test_prepare_pool_cap():
     env = dict(os.environ, SECURE_INFER_PREPARE_POOL_BYTES=str(1 << 20))
     r = subprocess.run([sys.executable, "-c", CHILD, str(ROOT)], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "cap ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_process_exit_without_shutdown_is_clean(nl):
+    """A process that announced a reload (starting the lookahead encryption
+    thread) and exits without secure_infer_session_shutdown ends normally,
+    instead of std::terminate from a joinable library thread."""
+    import subprocess
+    import sys
+    import textwrap
+    from conftest import ROOT
+    code = textwrap.dedent("""
+        import torch
+        from secure_infer_b200 import native_layerwise as nl
+        s = nl.Session(0, bytes(range(16)), bytes(4))
+        host = torch.zeros((4, 128, 1, 128), dtype=torch.bfloat16).pin_memory()
+        nl.register_host_range(host, 3, 0)
+        mapping = torch.tensor([[0, 0], [1, 1]])
+        t = nl.NativeTransfer("none", layers=4, heads=1)
+        assert t.prepare_layer(([host, host], mapping), 1, layer=3)
+        print("exiting")
+    """)
+    out = subprocess.run([sys.executable, "-c", code], cwd=str(ROOT), capture_output=True, text=True, timeout=300,
+                         env={**__import__("os").environ, "PYTHONPATH": str(ROOT)})
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "exiting" in out.stdout
