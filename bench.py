@@ -547,7 +547,9 @@ def attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, suffix:
 
     events = [torch.cuda.Event() for _ in range(L)]
     names = [f"model.layers.{layer}.self_attn.attn" for layer in range(L)]
-    reloader = LayerwiseReloader(names, cache, payload, mode=cfg["codec"])
+    reloaders = {gate: LayerwiseReloader(names, cache, payload, mode=cfg["codec"], host_gate=gate == "host")
+                 for gate in ("host", "device")}
+    reloader = reloaders["host"]
     requests = itertools.count()
     src_blocks, dst_blocks = list(range(B)), list(perm[:B])
 
@@ -555,15 +557,17 @@ def attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, suffix:
         for layer in range(L):
             dev_reload(layer, lsp)
 
-    def connector_run(fn):
+    def connector_run(fn, gate="host"):
+        rl = reloaders[gate]
+
         def enqueue():
             with torch.cuda.stream(cs):
-                reloader.start_load(next(requests), src_blocks, dst_blocks)
+                rl.start_load(next(requests), src_blocks, dst_blocks)
                 for layer in range(L):
-                    reloader.wait_for_layer_load(names[layer])
+                    rl.wait_for_layer_load(names[layer])
                     if fn is not None:
                         fn(layer)
-            reloader.get_finished()
+            rl.get_finished()
         return enqueue
 
     out = {"suffix_tokens": S, "prefix_tokens": P, "layers": L,
@@ -572,7 +576,8 @@ def attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, suffix:
                        f"SwiGLU MLP ({hid} -> {ffn} -> {hid}) GEMMs",
            "gate": "device-resident: CUDA event per layer after secure_infer_reload_records; e2e: "
                    "LayerwiseReloader.wait_for_layer_load (host-observed authentication, then a device-side "
-                   "wait on the layer's event)"}
+                   "wait on the layer's event); e2e_reload_device_gate: the same connector with host_gate=False "
+                   "(released once submitted; failed records are zero when the layer's event fires)"}
     # Warm up every piece (kernels, SDPA backend, cuBLAS heuristics, connector threads).
     for fn in (attention, full_layer):
         with torch.cuda.stream(cs):
@@ -599,6 +604,7 @@ def attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, suffix:
         compute_host_ms = median(lambda: timed(compute_all, 0))
         dev_ms = median(lambda: timed(dev_overlap))
         e2e_ms = median(lambda: timed(connector_run(fn), 0))
+        e2e_dev_gate_ms = median(lambda: timed(connector_run(fn, "device"), 0))
 
         def row(load_ms, both_ms, compute_ms):
             finish = max(load_ms + compute_ms / L, compute_ms + load_ms / L)
@@ -609,8 +615,10 @@ def attention_overlap(torch, lib, cfg, cache, perm, payload, dev_reload, suffix:
 
         out[name] = {"compute_us_per_layer": round(compute_dev_ms * 1e3 / L, 2),
                      "device_resident_reload": row(reload_dev_ms, dev_ms, compute_dev_ms),
-                     "e2e_reload": row(reload_e2e_ms, e2e_ms, compute_host_ms)}
-    reloader.close()
+                     "e2e_reload": row(reload_e2e_ms, e2e_ms, compute_host_ms),
+                     "e2e_reload_device_gate": row(reload_e2e_ms, e2e_dev_gate_ms, compute_host_ms)}
+    for rl in reloaders.values():
+        rl.close()
     return out
 
 

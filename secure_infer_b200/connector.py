@@ -46,7 +46,7 @@ class LayerwiseReloader:
     _jobs = itertools.count(1)
 
     def __init__(self, names, kv_caches, cpu_tensors, mode: str | None = None, lookahead: bool = True,
-                 timeout: float = 120.0, native_loop: bool = True):
+                 timeout: float = 120.0, native_loop: bool = False, host_gate: bool = True):
         if not (len(names) == len(kv_caches) == len(cpu_tensors)):
             raise ValueError("names, kv_caches and cpu_tensors differ in length")
         self.lib = _native.lib()
@@ -56,9 +56,18 @@ class LayerwiseReloader:
         self.mode = mode if mode is not None else settings()[0]
         self.lookahead = lookahead
         self.timeout = timeout
-        # Run each request's layer loop on a library thread when the library
-        # has secure_infer_h2d_reload_layers_async (otherwise in the fetch thread).
+        # native_loop: run each request's layer loop on a library thread
+        # (secure_infer_h2d_reload_layers_async) instead of the fetch thread.
+        # Measured with an attention stand-in, the fetch thread's loop
+        # overlapped better, so it is the default.
         self.native_loop = native_loop
+        # host_gate: wait_for_layer_load returns only once the layer's
+        # authentication is known on the host, as the reference does.  With
+        # host_gate=False it returns once the layer is submitted and gates the
+        # compute stream on the device alone: records that fail verification
+        # are already zero when the layer's event fires, and the failure is
+        # raised by a later wait, get_finished() or the last layer.
+        self.host_gate = host_gate
         self.device = kv_caches[0][0].device
         self.heads = kv_caches[0][0].shape[2]
         # High priority: attention waits on this stream's reloads, so their
@@ -219,14 +228,18 @@ class LayerwiseReloader:
 
     # ----------------------------------------------------------------- wait
     def wait_for_layer_load(self, name) -> None:
-        """Every request being consumed has authenticated KV for this layer
-        before attention runs; the current stream waits on the layer's event."""
+        """Every request being consumed has its KV for this layer before
+        attention runs: with the host gate (the reference's behaviour) the
+        layer's authentication is known on the host first; in both modes the
+        current stream then waits on the layer's event, by which time any
+        record that failed verification has been zeroed."""
         layer = self.names.index(name)
         stream = torch.cuda.current_stream(self.device)
         deadline = time.monotonic() + self.timeout
+        gate = "authenticated" if self.host_gate else "submitted"
         for state in list(self.consuming.values()):
             with self.lock:
-                while not state["authenticated"][layer] and not state["error"]:
+                while not state[gate][layer] and not state["error"]:
                     if not self.lock.wait(timeout=max(0.0, deadline - time.monotonic())):
                         if time.monotonic() >= deadline:
                             raise RuntimeError(f"layer {layer} not authenticated within {self.timeout} s")

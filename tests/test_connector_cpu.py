@@ -117,7 +117,7 @@ class FakeTransfer:
 def make(monkeypatch):
     from secure_infer_b200 import connector
 
-    def build(lib, timeout=5.0, raise_on_layer=None):
+    def build(lib, timeout=5.0, raise_on_layer=None, host_gate=True):
         fake_torch = types.SimpleNamespace(cuda=FakeCuda(), from_numpy=torch.from_numpy)
         monkeypatch.setattr(connector, "torch", fake_torch)
         monkeypatch.setattr(connector._native, "lib", lambda: lib)
@@ -127,7 +127,8 @@ def make(monkeypatch):
         caches = [[torch.zeros((8, 4, 1, 4)) for _ in range(2)] for _ in range(LAYERS)]
         cpu = [[torch.zeros((8, 4, 1, 4)) for _ in range(2)] for _ in range(LAYERS)]
         names = [f"layers.{i}" for i in range(LAYERS)]
-        return connector.LayerwiseReloader(names, caches, cpu, mode="none", timeout=timeout), names, fake_torch
+        return (connector.LayerwiseReloader(names, caches, cpu, mode="none", timeout=timeout, host_gate=host_gate),
+                names, fake_torch)
     return build
 
 
@@ -194,3 +195,20 @@ def test_block_indices_checked(make):
         r.start_load("a", [8], [0])
     with pytest.raises(ValueError):
         r.start_load("a", [0, 1], [0])
+
+
+def test_device_gate_releases_layers_before_host_authentication(make):
+    """host_gate=False: a layer is released to the compute stream once it is
+    submitted, while its authentication is still pending on the host; the
+    last layer still joins the request and reports its outcome."""
+    lib = FakeLib(hang_layer=1)
+    r, names, ft = make(lib, host_gate=False)
+    r.start_load("a", [0], [0])
+    t0 = time.monotonic()
+    for name in names[:-1]:
+        r.wait_for_layer_load(name)              # layer 1's authentication is still pending
+    assert time.monotonic() - t0 < 3.0
+    assert len(ft.cuda.current.waited) == LAYERS - 1
+    lib.release.set()
+    r.wait_for_layer_load(names[-1])
+    assert r.get_finished() == {"a"}

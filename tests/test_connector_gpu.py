@@ -33,12 +33,13 @@ def env():
     s.close()
 
 
-def make_reloader(cpu, mode="none", native_loop=True):
+def make_reloader(cpu, mode="none", native_loop=False, host_gate=True):
     from secure_infer_b200.connector import LayerwiseReloader
     caches = [[torch.zeros((CACHE, 128, HEADS, 128), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
               for _ in range(LAYERS)]
     names = [f"model.layers.{i}.self_attn" for i in range(LAYERS)]
-    return LayerwiseReloader(names, caches, cpu, mode=mode, native_loop=native_loop), caches, names
+    return (LayerwiseReloader(names, caches, cpu, mode=mode, native_loop=native_loop, host_gate=host_gate), caches,
+            names)
 
 
 def run_model(reloader, names, caches, dest):
@@ -56,12 +57,13 @@ def expected(cpu, src):
                         for layer in range(LAYERS)])
 
 
-@pytest.mark.parametrize("native_loop", [True, False])
-def test_two_requests_reload_all_layers(env, native_loop):
-    """The layer loop on the library's thread (secure_infer_h2d_reload_layers_async)
-    or in the connector's fetch thread: the same blocks land either way."""
+@pytest.mark.parametrize("native_loop,host_gate", [(False, True), (True, True), (False, False), (True, False)])
+def test_two_requests_reload_all_layers(env, native_loop, host_gate):
+    """The layer loop in the connector's fetch thread or on the library's
+    thread (secure_infer_h2d_reload_layers_async), attention gated after host
+    authentication or on the device alone: the same blocks land either way."""
     nl, cpu = env
-    reloader, caches, names = make_reloader(cpu, native_loop=native_loop)
+    reloader, caches, names = make_reloader(cpu, native_loop=native_loop, host_gate=host_gate)
     for req, (src, dst) in enumerate([([3, 0, 7, 5], [10, 2, 4, 9]), ([11, 1], [0, 15])]):
         before = nl.prefetch_stats()
         reloader.start_load(f"req-{req}", src, dst)
