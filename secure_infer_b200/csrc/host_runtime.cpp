@@ -533,6 +533,7 @@ struct Session {
 };
 
 std::recursive_mutex g_mu;      // H2D path + session state
+std::mutex g_events_mu;         // g_s.last_event / last_batch (device-side layer release)
 bool host_only_session = false;
 std::mutex g_d2h_mu;            // D2H completion state
 Session g_s;
@@ -1277,6 +1278,19 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
         if (!g_s.ready) return nullptr;
     }
     StageSlot& slot = *pick;
+    // The slot's previous batch must finish before its buffers are reused;
+    // with the lock released, reserved against other submissions, while the
+    // GPU gets there.  The batch (slot.owner) keeps its event alive.
+    if (held != nullptr && slot.done != nullptr && cudaEventQuery(slot.done) == cudaErrorNotReady) {
+        const cudaEvent_t prev = slot.done;
+        slot.encrypting = true;
+        held->unlock();
+        cudaEventSynchronize(prev);
+        held->lock();
+        slot.encrypting = false;
+        g_slot_cv.notify_all();
+        if (!g_s.ready) return nullptr;
+    }
     if (slot.owner) harvest(*slot.owner);   // statuses leave the slot before reuse
     if (!ensure_stage(slot, stride * n, layer_ks_stride(count) * n, n, 0, true)) return nullptr;
     if (slot.done) cudaEventSynchronize(slot.done);
@@ -1374,6 +1388,7 @@ std::shared_ptr<LayerBatch> submit_layer_locked(uint32_t layer, const void* cons
 void register_batch_locked(const std::shared_ptr<LayerBatch>& b)
 {
     g_s.pending[b->layer].push_back(b);
+    std::lock_guard<std::mutex> ev(g_events_mu);
     g_s.last_event[b->layer] = b->done;
     g_s.last_batch[b->layer] = b;
 }
@@ -1657,8 +1672,11 @@ void shutdown_locked()
     for (auto& kv : g_s.pending)
         for (auto& b : kv.second) harvest(*b);
     g_s.pending.clear();
-    g_s.last_event.clear();
-    g_s.last_batch.clear();
+    {
+        std::lock_guard<std::mutex> ev(g_events_mu);
+        g_s.last_event.clear();
+        g_s.last_batch.clear();
+    }
     for (auto& s : g_s.h2d) {
         s.owner.reset();
         free_stage(s);
@@ -2198,7 +2216,8 @@ SI_EXPORT int secure_infer_h2d_prepare_layer(uint32_t layer, const void* const* 
 SI_EXPORT int secure_infer_layer_ready_wait(uint32_t layer, void* stream)
 {
     if (!await_async_layer(layer)) return -1;
-    std::lock_guard<std::recursive_mutex> lock(g_mu);
+    // Not the session lock: a submission may hold that across its GPU waits.
+    std::lock_guard<std::mutex> lock(g_events_mu);
     auto it = g_s.last_event.find(layer);
     if (it == g_s.last_event.end()) return -1;
     return CUDA_OK(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), it->second, 0)) ? 0 : -1;
@@ -2269,6 +2288,7 @@ SI_EXPORT int secure_infer_recovery_wait_layer_authentication(uint32_t layer)
         for (uint32_t i = 0; i < r->n; ++i) {
             if (r->status[i] == 1u) ++g_verified; else { ++g_rejected; ok = false; }
         }
+        std::lock_guard<std::mutex> ev(g_events_mu);
         g_s.last_event[b->layer] = r->done;
         g_s.last_batch[b->layer] = r;
     }
