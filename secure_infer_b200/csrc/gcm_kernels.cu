@@ -662,7 +662,7 @@ __device__ __forceinline__ void layer_iv(uint32_t iv0, uint64_t ticket, uint32_t
 // columns 1 and 0 alone.  So round 1 is t0 = a0 ^ Te3[byte 15],
 // t1 = a1 ^ Te2[byte 14], t2 = a2, t3 = a3, and round 2 needs the eight
 // lookups of t0 and t1 beside the constants b0..b3 (Bernstein and Schwabe's
-// counter-mode caching for table AES): 138 lookups per block instead of 176.
+// counter-mode caching for table AES): 138 lookups per block instead of 160.
 struct CtrCache {
     uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
 };
