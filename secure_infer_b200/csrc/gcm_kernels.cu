@@ -923,6 +923,27 @@ __device__ __forceinline__ void layer_dequant(uint4 p, uint64_t c, const CodecPa
     }
 }
 
+// Publishes a warp's segment partial and counts it; true in the warp that
+// completes record r.  The warp's output stores are ordered before the count
+// by the warp barrier and one device-scope fence in lane 0 (the ordering the
+// fail-closed zeroing of the completing warp relies on), and that warp's lane
+// 0 fences again before its lanes read the other partials.
+__device__ __forceinline__ bool publish_partial(uint4* partials, uint32_t* counters, uint32_t w, uint32_t r,
+                                                uint32_t nseg, uint4 part, uint32_t lane)
+{
+    __syncwarp();
+    uint32_t last = 0;
+    if (lane == 0) {
+        partials[w] = part;
+        __threadfence();
+        last = atomicAdd(&counters[r], 1u) == nseg - 1 ? 1u : 0u;
+        if (last) __threadfence();
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
+    return last != 0;
+}
+
 template <int kCap, int kMode>
 __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kernel(const __grid_constant__ LayerLaunch<kCap> L)
 {
@@ -1155,17 +1176,7 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
             if (e & 32u) part = gf_mul_warp<true>(part, L.h.join_pow + 4 * 512, static_cast<int>(lane));
         }
 
-        __threadfence();
-        __syncwarp();
-        uint32_t last = 0;
-        if (lane == 0) {
-            L.h.partials[w] = part;
-            __threadfence();
-            last = atomicAdd(&L.h.counters[r], 1u) == nseg - 1 ? 1u : 0u;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
+        if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) continue;
         uint4 acc = zero4();
         if (prescaled) {
             uint4 v = zero4();
@@ -1221,18 +1232,27 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
 
 // Fused verify with the keystream computed inside the kernel, for raw,
 // 16-byte aligned records already in device memory (nothing to overlap a
-// keystream prefetch with).  Shared memory holds what the main loop reads:
-// the four AES T-table replicas and round keys (128 KiB, as the keystream
-// kernel) and the H^32 byte tables (64 KiB); the lane, quarter and join
-// tables of the segment combine are read through L1 from the schedule, once
-// per segment.  Segments, lanes and the combine are those of
-// gcm_layer_verify_kernel.  An interior step of a warp loads 16 bytes of
-// ciphertext per lane two steps ahead, encrypts the lane's counter block,
+// keystream prefetch with).  During the main loop shared memory holds what
+// the loop reads: the four AES T-table replicas and round keys (128 KiB, as
+// the keystream kernel) and the H^32 byte tables (64 KiB).  Segments and lanes
+// are those of gcm_layer_verify_kernel.  An interior step of a warp loads 16
+// bytes of ciphertext per lane two steps ahead, encrypts the lane's counter
+// block (with the record's counter-mode constants, as the keystream kernel),
 // XORs, stores and takes one Horner step; the AES lookups of one warp fill
-// the load latency of the others, and no keystream crosses HBM.  The warp
-// that joins a record's partials computes E_K(J0) itself.
+// the load latency of the others, and no keystream crosses HBM.
+//
+// When every warp holds at most one segment and a record has at most 64 of
+// them (the usual layer), the launch is a single pass: once all warps of the
+// CTA are through their main loops, the lane, quarter and join tables (128
+// KiB) replace the T-tables by one bulk copy, so the segment combine runs on
+// conflict-free shared-memory tables as in gcm_layer_verify_kernel, and the
+// first warp of each record folds E_K(J0) into its partial, so the XOR of a
+// record's partials is its tag.  Otherwise (longer layers) each warp combines
+// its segments through L1 from the schedule and the warp that completes a
+// record computes E_K(J0) itself.
 constexpr uint32_t kInlineThreads = 512;
 constexpr size_t kInlineSmem = kCtrTableBytes + 256 + kGhashSmem;
+static_assert(kCtrTableBytes == 2 * kGhashSmem, "the combine tables take the T-tables' place");
 
 template <int kCap>
 __global__ void __launch_bounds__(kInlineThreads, 1)
@@ -1240,10 +1260,15 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     uint4* gtab = reinterpret_cast<uint4*>(smem + kCtrTableBytes + 256);
+    // Single pass, after the main loops: the combine tables in the T-tables'
+    // place (lane8 64 KiB, H^8/16/24 24 KiB, H^(L 2^b) for b = 0..4 40 KiB).
+    uint4* ltab = reinterpret_cast<uint4*>(smem);
+    uint4* qtab = reinterpret_cast<uint4*>(smem + kGhashSmem);
+    uint4* jtab = qtab + 3 * 512;
     const GcmSchedule* __restrict__ S = L.h.sched;
     const uint32_t tid = threadIdx.x, lane = tid & 31u, rep = lane & 7u, quarter = lane >> 3;
     const uint32_t seg_steps = L.h.seg_steps;
-    __shared__ __align__(8) uint64_t gtab_bar;
+    __shared__ __align__(8) uint64_t gtab_bar, comb_bar;
     if (tid == 0) {
         mbar_init_expect(&gtab_bar, 65536u);
         bulk_g2s(gtab, S->byte32, 65536u, &gtab_bar);
@@ -1254,7 +1279,7 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
     // the stream has completed.
     allow_dependent_launch();
     grid_dependency_wait();
-    // If the table copy never completes, every partial is poisoned and the
+    // If a table copy never completes, the partials are poisoned and the
     // records fail closed (status 0, output zeroed) instead of hanging.
     const bool gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
     const uint32_t* rk = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
@@ -1272,14 +1297,18 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
     const uint4 len_blk = len_block_le(64, count);
     constexpr uint32_t kWarps = kInlineThreads / 32;
     constexpr int kPf = 2;
+    const bool cached = n_blk + 2 <= 65536;
 
-    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * kWarps) {
-        const uint32_t r = w / nseg, k = w - r * nseg;
+    // Horner partial of segment k of record r (lane l: blocks base + l + 32 j,
+    // stride H^32), with the record's plaintext written out.
+    auto hash_segment = [&](uint32_t r, uint32_t k) -> uint4 {
         const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
         const uint8_t* aad = in + tag_off + 32;
         uint8_t* out = L.rec[r].dst;
         uint32_t iv[4];
         layer_iv(L.h.iv0, L.rec[r].ticket, iv);
+        // Counter-mode constants of the record (counters below 2^16).
+        const CtrCache K = cached ? ctr_cache(iv, T, rk) : CtrCache{};
         const int64_t seg_end = len0 + static_cast<int64_t>(k) * seg_blocks;
         const int64_t seg_len = k == 0 ? len0 : seg_blocks;
         const int J = static_cast<int>((seg_len + 31) / 32);
@@ -1315,8 +1344,6 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
             Y = xor4(gf_mul_byte8(Y, gtab, rep), x);
         };
 
-        if (lane == 0 && hi > lo)
-            l2_prefetch_bulk(in + (base - a_blk) * 16 + 512ll * lo, static_cast<uint32_t>(hi - lo) * 512u);
         uint4 xq[kPf];
 #pragma unroll
         for (int u = 0; u < kPf; ++u)
@@ -1332,16 +1359,88 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
                 const uint4 x0 = xq[u];
                 if (j + kPf < hi) xq[u] = ldg16(in + static_cast<uint64_t>(c0 + 32ll * (j + kPf)) * 16u);
                 const uint64_t c = static_cast<uint64_t>(c0 + 32ll * j);
-                const uint4 ks = aes128_encrypt_t4(ctr_block_le(iv, c), T, rk);
+                const uint4 ks = cached ? aes128_ctr_cached(2u + static_cast<uint32_t>(c), K, T, rk)
+                                        : aes128_encrypt_t4(ctr_block_le(iv, c), T, rk);
                 *reinterpret_cast<uint4*>(out + c * 16u) = xor4(x0, ks);
                 Y = xor4(gf_mul_byte8(Y, gtab, rep), x0);
             }
         }
 #pragma unroll 1
         for (int j = hi; j < J; ++j) general(j);
-
-        // Two-stage lane combine (tables through L1).
         if (!gtab_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
+        return Y;
+    };
+
+    // Tag check of record r by the warp that completed it: status, and on a
+    // mismatch the record's plaintext zeroed.
+    auto finish_record = [&](uint32_t r, uint4 tag) {
+        const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
+        const bool ok = equal4(tag, ldg16(in + tag_off));
+        if (lane == 0) {
+            L.h.status[r] = ok ? 1u : 0u;
+            L.h.counters[r] = 0u;
+        }
+        if (!ok) {
+            uint8_t* out = L.rec[r].dst;
+            for (uint64_t off = static_cast<uint64_t>(lane) * 16u; off < count; off += 512u)
+                store_block(out + off, zero4(), count - off, true);
+        }
+    };
+
+    if (total <= gridDim.x * kWarps && nseg <= 64u) {
+        const uint32_t w = blockIdx.x + gridDim.x * (tid >> 5);
+        const bool has = w < total;
+        const uint32_t r = has ? w / nseg : 0u, k = has ? w - r * nseg : 0u;
+        uint4 Y = zero4(), mask = zero4();
+        if (has) {
+            Y = hash_segment(r, k);
+            if (k == 0) {
+                uint32_t iv[4];
+                layer_iv(L.h.iv0, L.rec[r].ticket, iv);
+                mask = aes128_encrypt_t4(j0_block_le(iv), T, rk);
+            }
+        }
+        // Every warp of the CTA is through its T-table lookups.
+        __syncthreads();
+        if (tid == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_init_expect(&comb_bar, 65536u + 8u * 8192u);
+            bulk_g2s(ltab, S->lane8, 65536u, &comb_bar);
+            bulk_g2s(qtab, S->tab[tab_pow_small(8)], 8192u, &comb_bar);
+            bulk_g2s(qtab + 512, S->tab[tab_pow_small(16)], 8192u, &comb_bar);
+            bulk_g2s(qtab + 1024, S->tab[tab_pow_small(24)], 8192u, &comb_bar);
+            bulk_g2s(jtab, S->tab[tab_pow_32k(static_cast<int>(seg_steps))], 8192u, &comb_bar);
+            bulk_g2s(jtab + 512, L.h.join_pow, 4u * 8192u, &comb_bar);
+        }
+        __syncthreads();
+        const bool comb_ready = mbar_wait_bounded(&comb_bar, 0);
+        if (!has) return;
+        if (!comb_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
+        Y = gf_mul_table<8, false>(Y, ltab, rep);                       // * H^(8 - r)
+        Y = xor4(Y, shfl_xor4(Y, 1));
+        Y = xor4(Y, shfl_xor4(Y, 2));
+        Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
+        if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
+        Y = xor4(Y, shfl_xor4(Y, 8));
+        uint4 part = xor4(Y, shfl_xor4(Y, 16));
+        // Pre-scaled by H^(L e), e = nseg - 1 - k; segment 0 adds E_K(J0).
+        const uint32_t e = nseg - 1u - k;
+#pragma unroll
+        for (int b = 0; b < 5; ++b)
+            if (e & (1u << b)) part = gf_mul_warp<false>(part, jtab + 512 * b, static_cast<int>(lane));
+        if (e & 32u) part = gf_mul_warp<true>(part, L.h.join_pow + 4 * 512, static_cast<int>(lane));
+        part = xor4(part, mask);
+        if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) return;
+        uint4 v = zero4();
+        for (uint32_t i = lane; i < nseg; i += 32) v = xor4(v, __ldcg(&L.h.partials[r * nseg + i]));
+        finish_record(r, warp_xor_reduce(v));
+        return;
+    }
+
+    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * kWarps) {
+        const uint32_t r = w / nseg, k = w - r * nseg;
+        uint4 Y = hash_segment(r, k);
+        // Two-stage lane combine (tables through L1).
         Y = gf_mul_table<8, true>(Y, S->lane8, rep);                    // * H^(8 - r)
         Y = xor4(Y, shfl_xor4(Y, 1));
         Y = xor4(Y, shfl_xor4(Y, 2));
@@ -1359,18 +1458,7 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
             for (int b = 1; b < 6; ++b)
                 if (e & (1u << b)) part = gf_mul_warp<true>(part, L.h.join_pow + 512 * (b - 1), static_cast<int>(lane));
         }
-
-        __threadfence();
-        __syncwarp();
-        uint32_t last = 0;
-        if (lane == 0) {
-            L.h.partials[w] = part;
-            __threadfence();
-            last = atomicAdd(&L.h.counters[r], 1u) == nseg - 1 ? 1u : 0u;
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
+        if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) continue;
         uint4 acc = zero4();
         if (prescaled) {
             uint4 v = zero4();
@@ -1398,16 +1486,9 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
             acc = k0 == 0 ? v : xor4(gf_mul_warp<true>(acc, L.h.join_pow + 4 * 512, lane), v);
             k0 += cnt;
         }
-        const uint4 mask = aes128_encrypt_t4(j0_block_le(iv), T, rk);
-        const bool ok = equal4(xor4(acc, mask), ldg16(in + tag_off));
-        if (lane == 0) {
-            L.h.status[r] = ok ? 1u : 0u;
-            L.h.counters[r] = 0u;
-        }
-        if (!ok) {
-            for (uint64_t off = static_cast<uint64_t>(lane) * 16u; off < count; off += 512u)
-                store_block(out + off, zero4(), count - off, true);
-        }
+        uint32_t iv[4];
+        layer_iv(L.h.iv0, L.rec[r].ticket, iv);
+        finish_record(r, xor4(acc, aes128_encrypt_t4(j0_block_le(iv), T, rk)));
     }
 }
 
