@@ -26,6 +26,7 @@
 #include <cuda_bf16.h>
 
 #include <atomic>
+#include <cstddef>
 #include <mutex>
 #include <vector>
 
@@ -351,6 +352,13 @@ __device__ __forceinline__ uint4 aes128_rounds_from(uint4 s, int first, const Ae
 __device__ __forceinline__ uint4 aes128_encrypt_t4(uint4 in, const Aes4Tables& T, const uint32_t* __restrict__ rk)
 {
     return aes128_rounds_from(make_uint4(in.x ^ rk[0], in.y ^ rk[1], in.z ^ rk[2], in.w ^ rk[3]), 1, T, rk);
+}
+
+// The same AES as a call, for rare blocks (general-path steps, tag masks), so
+// a kernel carries one copy of it besides its unrolled main loop.
+__device__ __noinline__ uint4 aes128_encrypt_t4_call(uint4 in, const Aes4Tables T, const uint32_t* rk)
+{
+    return aes128_encrypt_t4(in, T, rk);
 }
 
 __device__ __forceinline__ void fill_aes4_smem(uint8_t* smem, const GcmSchedule* S)
@@ -1250,6 +1258,7 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
 // record's partials is its tag.  Otherwise (longer layers) each warp combines
 // its segments through L1 from the schedule and the warp that completes a
 // record computes E_K(J0) itself.
+static_assert(offsetof(GcmSchedule, rk) == 0, "the host copies the round keys from the schedule's start");
 constexpr uint32_t kInlineThreads = 512;
 constexpr size_t kInlineSmem = kCtrTableBytes + 256 + kGhashSmem;
 static_assert(kCtrTableBytes == 2 * kGhashSmem, "the combine tables take the T-tables' place");
@@ -1282,7 +1291,8 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
     // If a table copy never completes, the partials are poisoned and the
     // records fail closed (status 0, output zeroed) instead of hanging.
     const bool gtab_ready = mbar_wait_bounded(&gtab_bar, 0);
-    const uint32_t* rk = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);
+    const uint32_t* rk = L.h.rk;   // constant bank
+    const uint32_t* rk_smem = reinterpret_cast<const uint32_t*>(smem + kCtrTableBytes);   // for the AES calls
     const Aes4Tables T = aes4_view(smem);
 
     const uint64_t count = L.h.count;
@@ -1322,51 +1332,51 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
         const int hi = j_hi > lo ? j_hi : lo;
         const int64_t c0 = base + lane - a_blk;   // payload block of step 0 (negative on the AAD)
         uint4 Y = zero4();
-
-        // Any step through the general path: AAD, payload, partial and length
-        // blocks in any mix.
-        auto general = [&](int j) {
+        uint4 xq[kPf];
+#pragma unroll
+        for (int u = 0; u < kPf; ++u)
+            if (lo + u < hi) xq[u] = ldg16(in + static_cast<uint64_t>(c0 + 32ll * (lo + u)) * 16u);
+        // Steps outside [lo, hi) take the general path (AAD, payload, partial
+        // and length blocks in any mix, AES by call); the interior runs the
+        // unrolled loop.
+#pragma unroll 1
+        for (int j = 0; j < J; ++j) {
+            if (j == lo && lo < hi) {
+#pragma unroll 1
+                for (int j0 = lo; j0 < hi; j0 += kPf) {
+#pragma unroll
+                    for (int u = 0; u < kPf; ++u) {
+                        const int jj = j0 + u;
+                        if (jj >= hi) break;
+                        const uint4 x0 = xq[u];
+                        if (jj + kPf < hi) xq[u] = ldg16(in + static_cast<uint64_t>(c0 + 32ll * (jj + kPf)) * 16u);
+                        const uint64_t c = static_cast<uint64_t>(c0 + 32ll * jj);
+                        const uint4 ks = cached ? aes128_ctr_cached(2u + static_cast<uint32_t>(c), K, T, rk)
+                                                : aes128_encrypt_t4(ctr_block_le(iv, c), T, rk);
+                        *reinterpret_cast<uint4*>(out + c * 16u) = xor4(x0, ks);
+                        Y = xor4(gf_mul_byte8(Y, gtab, rep), x0);
+                    }
+                }
+                j = hi - 1;
+                continue;
+            }
             const int64_t i = base + lane + 32 * static_cast<int64_t>(j);
             uint4 x = zero4();
-            if (j < J && i >= 0) {
+            if (i >= 0) {
                 if (i < a_blk) {
                     x = ldg16(aad + 16 * i);
                 } else if (i < a_blk + n_blk) {
                     const uint64_t off = static_cast<uint64_t>(i - a_blk) * 16u;
                     const uint64_t avail = count - off;
                     x = avail >= 16 ? ldg16(in + off) : load_partial16(in + off, avail);
-                    const uint4 ks = aes128_encrypt_t4(ctr_block_le(iv, static_cast<uint64_t>(i - a_blk)), T, rk);
+                    const uint4 ks = aes128_encrypt_t4_call(ctr_block_le(iv, static_cast<uint64_t>(i - a_blk)), T, rk_smem);
                     store_block(out + off, xor4(x, ks), avail, true);
                 } else {
                     x = len_blk;
                 }
             }
             Y = xor4(gf_mul_byte8(Y, gtab, rep), x);
-        };
-
-        uint4 xq[kPf];
-#pragma unroll
-        for (int u = 0; u < kPf; ++u)
-            if (lo + u < hi) xq[u] = ldg16(in + static_cast<uint64_t>(c0 + 32ll * (lo + u)) * 16u);
-#pragma unroll 1
-        for (int j = 0; j < lo; ++j) general(j);
-#pragma unroll 1
-        for (int j0 = lo; j0 < hi; j0 += kPf) {
-#pragma unroll
-            for (int u = 0; u < kPf; ++u) {
-                const int j = j0 + u;
-                if (j >= hi) break;
-                const uint4 x0 = xq[u];
-                if (j + kPf < hi) xq[u] = ldg16(in + static_cast<uint64_t>(c0 + 32ll * (j + kPf)) * 16u);
-                const uint64_t c = static_cast<uint64_t>(c0 + 32ll * j);
-                const uint4 ks = cached ? aes128_ctr_cached(2u + static_cast<uint32_t>(c), K, T, rk)
-                                        : aes128_encrypt_t4(ctr_block_le(iv, c), T, rk);
-                *reinterpret_cast<uint4*>(out + c * 16u) = xor4(x0, ks);
-                Y = xor4(gf_mul_byte8(Y, gtab, rep), x0);
-            }
         }
-#pragma unroll 1
-        for (int j = hi; j < J; ++j) general(j);
         if (!gtab_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
         return Y;
     };
@@ -1387,60 +1397,56 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
         }
     };
 
-    if (total <= gridDim.x * kWarps && nseg <= 64u) {
-        const uint32_t w = blockIdx.x + gridDim.x * (tid >> 5);
+    const bool single = total <= gridDim.x * kWarps && nseg <= 64u;
+    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5);; w += gridDim.x * kWarps) {
         const bool has = w < total;
+        if (!single && !has) return;
         const uint32_t r = has ? w / nseg : 0u, k = has ? w - r * nseg : 0u;
         uint4 Y = zero4(), mask = zero4();
-        if (has) {
-            Y = hash_segment(r, k);
-            if (k == 0) {
-                uint32_t iv[4];
-                layer_iv(L.h.iv0, L.rec[r].ticket, iv);
-                mask = aes128_encrypt_t4(j0_block_le(iv), T, rk);
+        uint32_t iv[4];
+        layer_iv(L.h.iv0, has ? L.rec[r].ticket : 0ull, iv);
+        if (has) Y = hash_segment(r, k);
+        if (has && (!single || k == 0)) mask = aes128_encrypt_t4_call(j0_block_le(iv), T, rk_smem);
+        if (single) {
+            // Every warp of the CTA is through its T-table lookups.
+            __syncthreads();
+            if (tid == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_init_expect(&comb_bar, 65536u + 8u * 8192u);
+                bulk_g2s(ltab, S->lane8, 65536u, &comb_bar);
+                bulk_g2s(qtab, S->tab[tab_pow_small(8)], 8192u, &comb_bar);
+                bulk_g2s(qtab + 512, S->tab[tab_pow_small(16)], 8192u, &comb_bar);
+                bulk_g2s(qtab + 1024, S->tab[tab_pow_small(24)], 8192u, &comb_bar);
+                bulk_g2s(jtab, S->tab[tab_pow_32k(static_cast<int>(seg_steps))], 8192u, &comb_bar);
+                bulk_g2s(jtab + 512, L.h.join_pow, 4u * 8192u, &comb_bar);
             }
-        }
-        // Every warp of the CTA is through its T-table lookups.
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_init_expect(&comb_bar, 65536u + 8u * 8192u);
-            bulk_g2s(ltab, S->lane8, 65536u, &comb_bar);
-            bulk_g2s(qtab, S->tab[tab_pow_small(8)], 8192u, &comb_bar);
-            bulk_g2s(qtab + 512, S->tab[tab_pow_small(16)], 8192u, &comb_bar);
-            bulk_g2s(qtab + 1024, S->tab[tab_pow_small(24)], 8192u, &comb_bar);
-            bulk_g2s(jtab, S->tab[tab_pow_32k(static_cast<int>(seg_steps))], 8192u, &comb_bar);
-            bulk_g2s(jtab + 512, L.h.join_pow, 4u * 8192u, &comb_bar);
-        }
-        __syncthreads();
-        const bool comb_ready = mbar_wait_bounded(&comb_bar, 0);
-        if (!has) return;
-        if (!comb_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
-        Y = gf_mul_table<8, false>(Y, ltab, rep);                       // * H^(8 - r)
-        Y = xor4(Y, shfl_xor4(Y, 1));
-        Y = xor4(Y, shfl_xor4(Y, 2));
-        Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
-        if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
-        Y = xor4(Y, shfl_xor4(Y, 8));
-        uint4 part = xor4(Y, shfl_xor4(Y, 16));
-        // Pre-scaled by H^(L e), e = nseg - 1 - k; segment 0 adds E_K(J0).
-        const uint32_t e = nseg - 1u - k;
+            __syncthreads();
+            const bool comb_ready = mbar_wait_bounded(&comb_bar, 0);
+            if (!has) return;
+            if (!comb_ready) Y = make_uint4(~0u, ~0u, ~0u, ~0u);
+            Y = gf_mul_table<8, false>(Y, ltab, rep);                       // * H^(8 - r)
+            Y = xor4(Y, shfl_xor4(Y, 1));
+            Y = xor4(Y, shfl_xor4(Y, 2));
+            Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
+            if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
+            Y = xor4(Y, shfl_xor4(Y, 8));
+            uint4 part = xor4(Y, shfl_xor4(Y, 16));
+            // Pre-scaled by H^(L e), e = nseg - 1 - k; segment 0 adds E_K(J0),
+            // so the XOR of the record's partials is its tag.
+            const uint32_t e = nseg - 1u - k;
 #pragma unroll
-        for (int b = 0; b < 5; ++b)
-            if (e & (1u << b)) part = gf_mul_warp<false>(part, jtab + 512 * b, static_cast<int>(lane));
-        if (e & 32u) part = gf_mul_warp<true>(part, L.h.join_pow + 4 * 512, static_cast<int>(lane));
-        part = xor4(part, mask);
-        if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) return;
-        uint4 v = zero4();
-        for (uint32_t i = lane; i < nseg; i += 32) v = xor4(v, __ldcg(&L.h.partials[r * nseg + i]));
-        finish_record(r, warp_xor_reduce(v));
-        return;
-    }
-
-    for (uint32_t w = blockIdx.x + gridDim.x * (tid >> 5); w < total; w += gridDim.x * kWarps) {
-        const uint32_t r = w / nseg, k = w - r * nseg;
-        uint4 Y = hash_segment(r, k);
-        // Two-stage lane combine (tables through L1).
+            for (int b = 0; b < 5; ++b)
+                if (e & (1u << b)) part = gf_mul_warp<false>(part, jtab + 512 * b, static_cast<int>(lane));
+            if (e & 32u) part = gf_mul_warp<true>(part, L.h.join_pow + 4 * 512, static_cast<int>(lane));
+            part = xor4(part, mask);
+            if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) return;
+            uint4 v = zero4();
+            for (uint32_t i = lane; i < nseg; i += 32) v = xor4(v, __ldcg(&L.h.partials[r * nseg + i]));
+            finish_record(r, warp_xor_reduce(v));
+            return;
+        }
+        // Several segments per warp: two-stage lane combine with the tables
+        // read through L1.
         Y = gf_mul_table<8, true>(Y, S->lane8, rep);                    // * H^(8 - r)
         Y = xor4(Y, shfl_xor4(Y, 1));
         Y = xor4(Y, shfl_xor4(Y, 2));
@@ -1486,9 +1492,7 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
             acc = k0 == 0 ? v : xor4(gf_mul_warp<true>(acc, L.h.join_pow + 4 * 512, lane), v);
             k0 += cnt;
         }
-        uint32_t iv[4];
-        layer_iv(L.h.iv0, L.rec[r].ticket, iv);
-        finish_record(r, xor4(acc, aes128_encrypt_t4(j0_block_le(iv), T, rk)));
+        finish_record(r, xor4(acc, mask));
     }
 }
 

@@ -126,6 +126,10 @@ struct LayerHeader {
     uint32_t v_first;       // codec: records r >= v_first decode as V packets, the rest as K
     const uint8_t* aad;     // encrypt: AAD of record r at aad + 64 r (records are the output)
     const uint4* join_pow;  // H^(32 seg_steps 2^b) nibble tables, b = 1..5 (join_tables_for)
+    // AES-128 round keys (LE words, as GcmSchedule::rk): read by the layer
+    // kernels from the kernel parameters, i.e. the constant bank, so a round
+    // key costs no shared-memory load and no register.
+    uint32_t rk[44];
 };
 
 template <int kCap>

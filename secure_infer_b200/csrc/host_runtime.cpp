@@ -474,6 +474,7 @@ struct Session {
     uint8_t key[16] = {};
     uint8_t salt[4] = {};
     GcmSchedule* sched = nullptr;
+    uint32_t rk[44] = {};             // the schedule's round keys, for the layer kernels' parameters
     void* join_tabs = nullptr;        // segment join tables of the layer kernels
     cudaStream_t producer = nullptr;
     cudaStream_t copier = nullptr;    // staged H2D record copies
@@ -754,6 +755,7 @@ int keystream_records_locked(const uint64_t* tickets, uint32_t n, uint64_t count
     for (uint32_t first = 0; first < n; first += kLayerCapLarge) {
         const uint32_t m = std::min<uint32_t>(n - first, kLayerCapLarge);
         LayerHeader h{};
+        std::memcpy(h.rk, g_s.rk, sizeof(h.rk));
         h.sched = g_s.sched;
         h.count = count;
         h.ks = keystream + first * ks_stride;
@@ -799,6 +801,8 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
             g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
             if (!ensure_launch_slot(slot, m, nseg * m)) return -1;
             LayerHeader h{};
+            std::memcpy(h.rk, g_s.rk, sizeof(h.rk));
+        std::memcpy(h.rk, g_s.rk, sizeof(h.rk));
             h.sched = g_s.sched;
             h.records = records + first * stride;
             h.stride = stride;
@@ -848,6 +852,8 @@ int verify_records_locked(const uint8_t* records, uint64_t stride, uint64_t coun
             g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
             if (!ensure_launch_slot(slot, m, nseg * m)) return -1;
             LayerHeader h{};
+            std::memcpy(h.rk, g_s.rk, sizeof(h.rk));
+        std::memcpy(h.rk, g_s.rk, sizeof(h.rk));
             h.sched = g_s.sched;
             h.records = records + first * stride;
             h.stride = stride;
@@ -1531,6 +1537,7 @@ int writeback_device_locked(const void* const* srcs, void* const* host_dsts, uin
         g_s.launch_next = (g_s.launch_next + 1) % g_s.launch.size();
         if (!ensure_launch_slot(ls, m, nseg * m)) return -1;
         LayerHeader h{};
+        std::memcpy(h.rk, g_s.rk, sizeof(h.rk));
         h.sched = g_s.sched;
         h.records = records + first * stride;
         h.stride = stride;
@@ -1724,6 +1731,8 @@ void shutdown_locked()
     if (g_s.consumed_ev) cudaEventDestroy(g_s.consumed_ev);
     if (g_s.produced_ev) cudaEventDestroy(g_s.produced_ev);
     g_s.consumed_ev = g_s.produced_ev = nullptr;
+    OPENSSL_cleanse(g_s.key, sizeof(g_s.key));
+    OPENSSL_cleanse(g_s.rk, sizeof(g_s.rk));
     g_s.ready = false;
 }
 
@@ -1987,7 +1996,8 @@ int session_init_locked(int device, const uint8_t* key16, const uint8_t* iv_salt
     const bool ok = launch_schedule(g_s.sched, dkey, nullptr, true, g_s.producer) == cudaSuccess &&
                     CUDA_OK(cudaMemsetAsync(dkey, 0, 16, g_s.producer)) &&
                     sib::launch_join_tables(g_s.sched, g_s.join_tabs, g_s.producer) == cudaSuccess &&
-                    CUDA_OK(cudaStreamSynchronize(g_s.producer));
+                    CUDA_OK(cudaStreamSynchronize(g_s.producer)) &&
+                    CUDA_OK(cudaMemcpy(g_s.rk, g_s.sched, sizeof(g_s.rk), cudaMemcpyDeviceToHost));   // rk leads the schedule
     cudaFree(dkey);
     if (!ok) return -1;
     g_s.launch.resize(kLaunchSlots);

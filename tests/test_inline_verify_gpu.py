@@ -51,7 +51,13 @@ def reload(nl, drecs, stride, count, tk, dest, order, keystream):
     return status.cpu().tolist()
 
 
-@pytest.mark.parametrize("count,n", [(262144, 96), (262144 + 16, 5), (1000, 9), (16, 40), (4097, 1030)])
+# (262144, 96) is a c2 layer: one segment per warp, partials pre-scaled (the
+# single pass that swaps the combine tables into shared memory).  (65536,
+# 1100) gives the first launch of 1024 records several segments per warp with
+# pre-scaled partials; (4 MiB + 16, 12) gives records of more than 64 segments
+# (tree join by the completing warp).
+@pytest.mark.parametrize("count,n", [(262144, 96), (262144 + 16, 5), (1000, 9), (16, 40), (4097, 1030),
+                                     (65536, 1100), ((4 << 20) + 16, 12)])
 def test_inline_keystream_reload_matches_plaintext_and_prefetched_path(nl, count, n):
     g = torch.Generator().manual_seed(count * 7 + n)
     plain = torch.randint(0, 256, (n, count), dtype=torch.uint8, generator=g).pin_memory()
@@ -71,11 +77,13 @@ def test_inline_keystream_reload_matches_plaintext_and_prefetched_path(nl, count
     assert torch.equal(outs[0], outs[1])
 
 
-def test_inline_keystream_reload_rejects_tampering(nl):
+@pytest.mark.parametrize("count", [262144 + 5, (4 << 20) + 5])
+def test_inline_keystream_reload_rejects_tampering(nl, count):
     """Flip one bit of record 1's ciphertext (first block), record 3's tag,
     record 4's AAD and record 6's last payload byte: those records fail closed
-    (status 0, destination zeroed), the others land."""
-    n, count = 8, 262144 + 5
+    (status 0, destination zeroed), the others land.  The second size gives
+    records of more than 64 segments (joined by the completing warp)."""
+    n = 8
     g = torch.Generator().manual_seed(99)
     plain = torch.randint(0, 256, (n, count), dtype=torch.uint8, generator=g).pin_memory()
     recs, tk, stride = encrypt(nl, plain)
