@@ -118,9 +118,9 @@ NCU_TRAFFIC_BYTES = {
 # binding pipe), one conflict-free wavefront per warp-wide lookup: GHASH with
 # byte tables = 16 LDS.128 per lane per block = 2 wavefronts; AES-128 with
 # T-tables = 16 lookups in each of rounds 1-9 and 16 in the final round = 160
-# per 32 blocks = 5.0, and 138 (4.3125) with the keystream kernel's counter-mode
-# caching (records of fewer than 2^16 - 2 blocks: round 1 needs 2 lookups,
-# round 2 needs 8).
+# per 32 blocks = 5.0, and 138 (4.3125) with the counter-mode caching of the
+# keystream and inline kernels (records of fewer than 2^16 - 2 blocks: round 1
+# needs 2 lookups, round 2 needs 8).
 GHASH_WAVEFRONTS_PER_BLOCK = 2.0
 AES_WAVEFRONTS_PER_BLOCK = 160 / 32
 AES_CACHED_WAVEFRONTS_PER_BLOCK = 138 / 32
@@ -879,7 +879,7 @@ def run_gpu(args, cfg):
         wavefronts = {"gcm_layer_verify_kernel": GHASH_WAVEFRONTS_PER_BLOCK * (payload_blocks + 5 * n),
                       "gcm_layer_ctr_kernel": aes_ctr * (payload_blocks + n),
                       "gcm_layer_verify_inline_kernel": GHASH_WAVEFRONTS_PER_BLOCK * (payload_blocks + 5 * n)
-                      + AES_WAVEFRONTS_PER_BLOCK * (payload_blocks + n)}
+                      + aes_ctr * (payload_blocks + n)}
         smem = {name: round(wavefronts[name] / (us * 1e-6 * sms * sm_hz), 4) for name, us in per_kernel.items()
                 if name in wavefronts}
         result = {
@@ -936,8 +936,8 @@ def run_gpu(args, cfg):
                                  "kernel's time on the path that gave `value`; peak = measured HBM copy bandwidth "
                                  "(of measured). The binding resource is the shared-memory pipe (AES T-tables, "
                                  "GHASH byte tables): smem_pipe_frac = algorithmic wavefronts (GHASH 2 per 16-byte "
-                                 "block; AES 5.0, or 4.3125 with the keystream kernel's counter-mode caching; the "
-                                 "inline kernel both, uncached) / (kernel time x SMs x sampled SM clock), 1 "
+                                 "block; AES 5.0, or 4.3125 with counter-mode caching (records below 2^16 blocks); "
+                                 "the inline kernel both) / (kernel time x SMs x sampled SM clock), 1 "
                                  "wavefront per SM per clock peak."},
             "clocks": clocks.summary(),
         }

@@ -41,6 +41,31 @@ __device__ __forceinline__ uint4 shfl_xor4(uint4 v, int m)
                       __shfl_xor_sync(0xffffffffu, v.z, m), __shfl_xor_sync(0xffffffffu, v.w, m));
 }
 
+// Quarter stage of the segment combine: every lane of an active quarter holds
+// the quarter sum V, and the quarter returns V * M (M's nibble table tab,
+// entry p * 16 + v) in all its lanes.  Lane r of the quarter looks up nibbles
+// 4 r .. 4 r + 3 and the quarter XOR-reduces: 4 LDS.128 per lane instead of 32
+// for a lane-by-lane product.  Every lane must call it (the reduction
+// shuffles); lanes of an inactive quarter return zero.
+__device__ __forceinline__ uint4 gf_mul_quarter(uint4 v, const uint4* __restrict__ tab, uint32_t rep, bool active)
+{
+    const uint32_t wi = rep >> 1;
+    const uint32_t w = wi == 0 ? v.x : wi == 1 ? v.y : wi == 2 ? v.z : v.w;
+    const uint32_t half = (rep & 1u) * 16u;
+    uint4 acc = zero4();
+    if (active) {
+#pragma unroll
+        for (uint32_t i = 0; i < 4; ++i) {
+            // nibble p = 4 r + i: byte 2 r + i / 2, high nibble for even p.
+            const uint32_t shift = half + (i >> 1) * 8u + ((i & 1u) ? 0u : 4u);
+            acc = xor4(acc, tab[(4u * rep + i) * 16u + ((w >> shift) & 0xfu)]);
+        }
+    }
+    acc = xor4(acc, shfl_xor4(acc, 1));
+    acc = xor4(acc, shfl_xor4(acc, 2));
+    return xor4(acc, shfl_xor4(acc, 4));
+}
+
 __device__ __forceinline__ uint4 shfl_up4(uint4 v, uint32_t d)
 {
     return make_uint4(__shfl_up_sync(0xffffffffu, v.x, d), __shfl_up_sync(0xffffffffu, v.y, d),
@@ -1167,7 +1192,10 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
         Y = xor4(Y, shfl_xor4(Y, 1));
         Y = xor4(Y, shfl_xor4(Y, 2));
         Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
-        if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
+        {
+            const uint4 Yq = gf_mul_quarter(Y, qtab + 512 * (quarter < 3 ? 2 - quarter : 0), rep, quarter != 3);
+            if (quarter != 3) Y = Yq;                                    // * H^(24 - 8 q)
+        }
         Y = xor4(Y, shfl_xor4(Y, 8));
         uint4 part = xor4(Y, shfl_xor4(Y, 16));
         // The record's GHASH is S = sum_k p_k H^(L (nseg - 1 - k)), L = 32
@@ -1184,6 +1212,9 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
             if (e & 32u) part = gf_mul_warp<true>(part, L.h.join_pow + 4 * 512, static_cast<int>(lane));
         }
 
+        // The record's tag, loaded before the count so that the warp that
+        // completes the record does not wait for it afterwards.
+        const uint4 tag_in = kEncrypt ? zero4() : load_partial16(in + tag_off, 16);
         if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) continue;
         uint4 acc = zero4();
         if (prescaled) {
@@ -1226,7 +1257,7 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
             }
             continue;
         }
-        const bool ok = equal4(xor4(acc, mask), load_partial16(in + tag_off, 16));
+        const bool ok = equal4(xor4(acc, mask), tag_in);
         if (lane == 0) {
             L.h.status[r] = ok ? 1u : 0u;
             L.h.counters[r] = 0u;
@@ -1383,9 +1414,8 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
 
     // Tag check of record r by the warp that completed it: status, and on a
     // mismatch the record's plaintext zeroed.
-    auto finish_record = [&](uint32_t r, uint4 tag) {
-        const uint8_t* in = L.h.records + static_cast<uint64_t>(r) * L.h.stride;
-        const bool ok = equal4(tag, ldg16(in + tag_off));
+    auto finish_record = [&](uint32_t r, uint4 tag, uint4 tag_in) {
+        const bool ok = equal4(tag, tag_in);
         if (lane == 0) {
             L.h.status[r] = ok ? 1u : 0u;
             L.h.counters[r] = 0u;
@@ -1428,7 +1458,10 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
             Y = xor4(Y, shfl_xor4(Y, 1));
             Y = xor4(Y, shfl_xor4(Y, 2));
             Y = xor4(Y, shfl_xor4(Y, 4));                                   // quarter sum
-            if (quarter != 3) Y = gf_mul_table<1, false>(Y, qtab + 512 * (2 - quarter), 0);   // * H^(24 - 8 q)
+            {
+                const uint4 Yq = gf_mul_quarter(Y, qtab + 512 * (quarter < 3 ? 2 - quarter : 0), rep, quarter != 3);
+                if (quarter != 3) Y = Yq;                                    // * H^(24 - 8 q)
+            }
             Y = xor4(Y, shfl_xor4(Y, 8));
             uint4 part = xor4(Y, shfl_xor4(Y, 16));
             // Pre-scaled by H^(L e), e = nseg - 1 - k; segment 0 adds E_K(J0),
@@ -1439,10 +1472,11 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
                 if (e & (1u << b)) part = gf_mul_warp<false>(part, jtab + 512 * b, static_cast<int>(lane));
             if (e & 32u) part = gf_mul_warp<true>(part, L.h.join_pow + 4 * 512, static_cast<int>(lane));
             part = xor4(part, mask);
+            const uint4 tag_in = ldg16(L.h.records + static_cast<uint64_t>(r) * L.h.stride + tag_off);
             if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) return;
             uint4 v = zero4();
             for (uint32_t i = lane; i < nseg; i += 32) v = xor4(v, __ldcg(&L.h.partials[r * nseg + i]));
-            finish_record(r, warp_xor_reduce(v));
+            finish_record(r, warp_xor_reduce(v), tag_in);
             return;
         }
         // Several segments per warp: two-stage lane combine with the tables
@@ -1464,6 +1498,7 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
             for (int b = 1; b < 6; ++b)
                 if (e & (1u << b)) part = gf_mul_warp<true>(part, L.h.join_pow + 512 * (b - 1), static_cast<int>(lane));
         }
+        const uint4 tag_in = ldg16(L.h.records + static_cast<uint64_t>(r) * L.h.stride + tag_off);
         if (!publish_partial(L.h.partials, L.h.counters, w, r, nseg, part, lane)) continue;
         uint4 acc = zero4();
         if (prescaled) {
@@ -1492,7 +1527,7 @@ __global__ void __launch_bounds__(kInlineThreads, 1)
             acc = k0 == 0 ? v : xor4(gf_mul_warp<true>(acc, L.h.join_pow + 4 * 512, lane), v);
             k0 += cnt;
         }
-        finish_record(r, xor4(acc, mask));
+        finish_record(r, xor4(acc, mask), tag_in);
     }
 }
 
