@@ -106,6 +106,9 @@ NCU_TRAFFIC_BYTES = {
     # one c2 layer of keystream: written into L2 and read from there by the
     # verify kernel, so almost nothing reaches DRAM
     ("c2", 8, "gcm_layer_ctr_kernel"): 22_784 + 4_096,
+    # one c2 layer through the inline kernel: the ciphertext only (no keystream
+    # crosses HBM; the bf16 output is still in L2 when the kernel ends)
+    ("c2", 8, "gcm_layer_verify_inline_kernel"): 25_469_184 + 1_792,
     # one c5 layer (128 records x 10256 B, K+V in one launch)
     ("c5", 1, "gcm_layer_verify_kernel"): 2_939_392,
     # one c4 layer (128 blocks of 8 heads): bf16 read; packets stay in L2
