@@ -1136,9 +1136,12 @@ __global__ void __launch_bounds__(layer_threads(kMode), 1) gcm_layer_verify_kern
             // block, partial last block).  Interior segments are all interior.
             const int lo = j_lo < J ? j_lo : J;
             const int hi = j_hi > lo ? j_hi : lo;
-            // The warp's interior is one contiguous range of the input and of
-            // the keystream: stream both into L2 ahead of the loads below.
-            if (lane == 0 && hi > lo) {
+            // Encrypt: the warp's interior is one contiguous range of the
+            // plaintext and of the keystream, streamed into L2 ahead of the
+            // loads below.  Raw verify loads without it (measured 2 % faster
+            // per c2 layer: the bulk requests of every warp at once queue
+            // ahead of the first steps' loads).
+            if (kEncrypt && lane == 0 && hi > lo) {
                 const uint64_t off = static_cast<uint64_t>((base - a_blk) * 16 + 512ll * lo);
                 const uint32_t bytes = static_cast<uint32_t>(hi - lo) * 512u;
                 l2_prefetch_bulk(in + off, bytes);
