@@ -106,3 +106,25 @@ def test_inline_keystream_reload_rejects_tampering(nl, count):
                 assert not got[i].any(), i
             else:
                 assert torch.equal(got[i], plain[i]), i
+
+
+def test_fail_closed_zeroing_is_never_overtaken_by_late_plaintext(nl):
+    """Every record's tag is wrong: the warp that completes a record zeroes its
+    destination after every segment's plaintext stores (each warp counts its
+    segment only after a warp barrier and a device-scope fence).  Many small
+    records and repeated launches give a late store many chances to land after
+    the zeroing; not one destination byte may survive."""
+    n, count = 1024, 4097
+    g = torch.Generator().manual_seed(7)
+    plain = torch.randint(1, 256, (n, count), dtype=torch.uint8, generator=g).pin_memory()
+    recs, tk, stride = encrypt(nl, plain)
+    aligned = (count + 31) // 32 * 32
+    recs[:, aligned] ^= 1                      # every tag
+    drecs = recs.cuda()
+    order = list(range(n))
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
+    for rep in range(4):
+        for keystream in (None, ks.data_ptr()):
+            dest = torch.full((n, count), 0x5A, dtype=torch.uint8, device="cuda")
+            assert reload(nl, drecs, stride, count, tk, dest, order, keystream) == [0] * n
+            assert int(dest.count_nonzero().item()) == 0, (rep, keystream)
