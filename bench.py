@@ -665,6 +665,7 @@ def run_gpu(args, cfg):
         dstride = cache[layer][0].stride(0) * 2
         dsts.append([cache[layer][k].data_ptr() + perm[i] * dstride for k in range(2) for i in range(B)])
     ks = torch.empty(max_ks, dtype=torch.uint8, device="cuda")
+    ks2 = torch.empty(max_ks, dtype=torch.uint8, device="cuda")   # the second stream's keystream buffer
     status = torch.zeros((L, n), dtype=torch.int32, device="cuda")
     torch.cuda.synchronize()
     # ctypes argument arrays are built once, outside every timed region, so the
@@ -718,6 +719,22 @@ def run_gpu(args, cfg):
         stream.wait_event(join_ev)
         return L
 
+    ks2_ptr = ks2.data_ptr()
+
+    def device_step_two_streams():
+        """The two-kernel path with consecutive layers alternating between two
+        streams, each stream with its own keystream buffer."""
+        fork_ev.record(stream)
+        stream2.wait_event(fork_ev)
+        for layer in range(L):
+            lsp, lks = (sp, ks_ptr) if layer % 2 == 0 else (sp2, ks2_ptr)
+            assert lib.secure_infer_reload_records(layer, rec_ptr[layer], strides[layer], count[layer], n,
+                                                   tickets[layer], dst_all[layer], lks, st_ptr[layer],
+                                                   codec_arg[layer], lsp, lsp) == 0
+        join_ev.record(stream2)
+        stream.wait_event(join_ev)
+        return 2 * L
+
     def barrier():
         if dist is not None:
             dist.barrier()
@@ -753,7 +770,7 @@ def run_gpu(args, cfg):
         assert int(status.min().item()) == 1
         return ms / args.steps, launches, clk
 
-    paths = {"prefetched_keystream": device_step}
+    paths = {"prefetched_keystream": device_step, "prefetched_keystream_two_streams": device_step_two_streams}
     if all(b == 0 for b in bits):
         paths["inline_keystream"] = device_step_inline
         paths["inline_keystream_two_streams"] = device_step_inline_two_streams
