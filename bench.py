@@ -268,6 +268,22 @@ def kernel_profile(lib, torch, enqueue_step, layers):
     return out
 
 
+def with_sm_share(lib, torch, device, step, streams):
+    """`step` (whose layers alternate between `streams` streams) run with each
+    layer launch limited to SMs / streams (secure_infer_set_layer_sm_limit),
+    so the streams' launches run side by side; the limit is restored after
+    the step's calls (launches read it when they are made)."""
+    share = torch.cuda.get_device_properties(device).multi_processor_count // streams
+
+    def run():
+        prev = lib.secure_infer_set_layer_sm_limit(share)
+        try:
+            return step()
+        finally:
+            lib.secure_infer_set_layer_sm_limit(prev)
+    return run
+
+
 def link_gbs(torch, stream, direction="h2d", nbytes=256 << 20, reps=5, write_combined=False):
     """Measured pinned-host <-> device copy bandwidth (GB/s), best of `reps`
     one-shot copies of `nbytes` on `stream` (CUDA events).  write_combined:
@@ -700,9 +716,10 @@ def run_gpu(args, cfg):
 
     # Consecutive layers alternate between two streams: the layers are
     # independent (own records, destinations, status and launch slot, no
-    # keystream buffer), so one layer's launch ramp and tail overlap the
-    # other stream's kernel.  The timed events stay on `stream`, which forks
-    # to and joins the second stream every step.
+    # keystream buffer), and with each launch limited to half the SMs
+    # (with_sm_share) the two streams' kernels run side by side.  The timed
+    # events stay on `stream`, which forks to and joins the second stream
+    # every step.
     stream2 = torch.cuda.Stream()
     sp2 = ct.c_void_p(stream2.cuda_stream)
     fork_ev, join_ev = torch.cuda.Event(), torch.cuda.Event()
@@ -770,10 +787,11 @@ def run_gpu(args, cfg):
         assert int(status.min().item()) == 1
         return ms / args.steps, launches, clk
 
-    paths = {"prefetched_keystream": device_step, "prefetched_keystream_two_streams": device_step_two_streams}
+    paths = {"prefetched_keystream": device_step,
+             "prefetched_keystream_two_streams": with_sm_share(lib, torch, local, device_step_two_streams, 2)}
     if all(b == 0 for b in bits):
         paths["inline_keystream"] = device_step_inline
-        paths["inline_keystream_two_streams"] = device_step_inline_two_streams
+        paths["inline_keystream_two_streams"] = with_sm_share(lib, torch, local, device_step_inline_two_streams, 2)
     timings = {name: timed_steps(fn) for name, fn in paths.items()}
     best = min(timings, key=lambda name: timings[name][0])
     ms_per_step, launches, clocks = timings[best]
@@ -1105,7 +1123,7 @@ def run_gpu_writeback(args, cfg):
         barrier()
         return max_over_ranks(start.elapsed_time(end), dist) / args.steps, launches, clk
 
-    paths = {"one_stream": device_step, "two_streams": device_step_two_streams}
+    paths = {"one_stream": device_step, "two_streams": with_sm_share(lib, torch, local, device_step_two_streams, 2)}
     timings = {name: timed_steps(fn) for name, fn in paths.items()}
     best = min(timings, key=lambda name: timings[name][0])
     ms_per_step, launches, clocks = timings[best]

@@ -50,6 +50,7 @@ HOST_SIGNATURES: dict[str, tuple[list, object]] = {
     "secure_infer_register_host_range_ex": ([P, SZ, U32, U32, SZ], None),
     "secure_infer_is_registered_host_range": ([P, SZ], I32),
     "secure_infer_host_pool_info": ([ct.POINTER(U32), ct.POINTER(I32), U32, ct.POINTER(U32)], I32),
+    "secure_infer_set_layer_sm_limit": ([U32], U32),
     "secure_infer_new_transfer_ticket": ([], U64),
     "secure_infer_derive_transfer_iv": ([P, U64, U64, P], I32),
     "secure_infer_build_gcm_aad": ([P, SZ, ct.c_uint8, U64, U64, P], I32),

@@ -1858,6 +1858,18 @@ DeviceInfo& device_info(int dev)
     return d;
 }
 
+// SMs a layer launch may occupy (0: all).  A caller that alternates
+// consecutive layers between streams sets it to a share of the GPU so the
+// launches of different streams run side by side instead of queueing for the
+// same SMs.
+std::atomic<uint32_t> g_layer_sm_limit{0};
+
+int layer_sms(const DeviceInfo& d)
+{
+    const uint32_t lim = g_layer_sm_limit.load(std::memory_order_relaxed);
+    return lim != 0 && static_cast<int>(lim) < d.sms ? static_cast<int>(lim) : d.sms;
+}
+
 // ---------------------------------------------------------------- profile
 struct ProfileRec {
     uint32_t kind;
@@ -1940,6 +1952,8 @@ int segment_launch_impl(const SegmentLaunch& args, size_t smem, int variant, cud
 }
 
 }  // namespace
+
+uint32_t set_layer_sm_limit(uint32_t sms) { return g_layer_sm_limit.exchange(sms); }
 
 void profile_enable(bool on) { g_prof_on.store(on); }
 
@@ -2063,7 +2077,7 @@ void layer_segments_for(uint64_t count, uint32_t n, uint32_t codec_bits, uint32_
     cudaGetDevice(&dev);
     {
         std::lock_guard<std::mutex> lock(g_dev_mu);
-        sms = device_info(dev).sms;
+        sms = layer_sms(device_info(dev));
     }
     const uint64_t m = 4u + (count + 15u) / 16u + 1u;
     const uint64_t warps = static_cast<uint64_t>(sms) * kLayerWarps;
@@ -2084,7 +2098,7 @@ int layer_launch(uint32_t kind, Kernel kernel, const LayerHeader& h, const Layer
     int sms;
     {
         std::lock_guard<std::mutex> lock(g_dev_mu);
-        sms = device_info(dev).sms;
+        sms = layer_sms(device_info(dev));
         if (!attr_set) {
             cudaError_t e =
                 cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

@@ -144,6 +144,9 @@ constexpr int kLayerCapLarge = 1024;
 inline uint64_t layer_ks_stride(uint64_t count) { return ((count + 15) & ~uint64_t(15)) + 16; }
 // Segment length (seg_steps) and count (nseg) per record for a launch of n records.
 void layer_segments_for(uint64_t count, uint32_t n, uint32_t codec_bits, uint32_t* seg_steps, uint32_t* nseg);
+// SMs a layer launch may occupy from now on (0: all of them); returns the
+// previous limit.
+uint32_t set_layer_sm_limit(uint32_t sms);
 
 // Keystream (+ tag masks) and fused verify/XOR/scatter for up to
 // kLayerCapLarge records; rec points at n LayerRec entries.  The encrypt

@@ -2389,6 +2389,8 @@ SI_EXPORT int secure_infer_d2h_writeback_layer(const void* const* src_blocks, vo
 
 SI_EXPORT int secure_infer_d2h_wait(void) { return d2h_join(0, false); }
 
+SI_EXPORT uint32_t secure_infer_set_layer_sm_limit(uint32_t sms) { return sib::set_layer_sm_limit(sms); }
+
 SI_EXPORT int secure_infer_kernel_profile_enable(int on)
 {
     sib::profile_enable(on != 0);

@@ -128,3 +128,30 @@ def test_fail_closed_zeroing_is_never_overtaken_by_late_plaintext(nl):
             dest = torch.full((n, count), 0x5A, dtype=torch.uint8, device="cuda")
             assert reload(nl, drecs, stride, count, tk, dest, order, keystream) == [0] * n
             assert int(dest.count_nonzero().item()) == 0, (rep, keystream)
+
+
+def test_layer_sm_limit_keeps_both_paths_exact(nl):
+    """With each layer launch limited to a few SMs (segments sized for them),
+    the fused and the two-kernel reload still land the plaintext and reject a
+    tampered record; the limit is process-wide and restored afterwards."""
+    lib = nl._native.lib()
+    n, count = 96, 32768
+    g = torch.Generator().manual_seed(11)
+    plain = torch.randint(0, 256, (n, count), dtype=torch.uint8, generator=g).pin_memory()
+    recs, tk, stride = encrypt(nl, plain)
+    recs[5, count // 2] ^= 2
+    drecs = recs.cuda()
+    order = torch.randperm(n + 4, generator=g)[:n].tolist()
+    ks = torch.empty(n * ((count + 15) // 16 * 16 + 16), dtype=torch.uint8, device="cuda")
+    for sms in (7, 74):
+        prev = lib.secure_infer_set_layer_sm_limit(sms)
+        try:
+            for keystream in (None, ks.data_ptr()):
+                dest = torch.full((n + 4, count), 0x5A, dtype=torch.uint8, device="cuda")
+                assert reload(nl, drecs, stride, count, tk, dest, order, keystream) == [0 if i == 5 else 1 for i in range(n)]
+                got = dest.cpu()
+                good = [i for i in range(n) if i != 5]
+                assert torch.equal(got[[order[i] for i in good]], plain[good]), (sms, keystream)
+                assert not got[order[5]].any()
+        finally:
+            assert lib.secure_infer_set_layer_sm_limit(prev) == sms
