@@ -274,9 +274,9 @@ int secure_infer_writeback_records(const void* const* srcs, void* const* host_ds
  * otherwise queue for the same SMs.  A caller that alternates consecutive
  * layers between k streams sets it to about SMs / k so those launches run
  * side by side: measured on a B200 with two streams and half the SMs each,
- * 45.5 us per Llama-3-8B layer (8 KV heads, 6144 tokens) against 51.8 on one
- * stream with all SMs, and 9.6 against 15.4 us at one KV head.  Set it between
- * calls; a launch reads it once.  Returns the previous limit. */
+ * 46.3 us per Llama-3-8B layer (8 KV heads, 6144 tokens) against 51.8 on one
+ * stream with all SMs, and 10.9 against 15.4 us at one KV head.  Set it
+ * between calls; a launch reads it once.  Returns the previous limit. */
 uint32_t secure_infer_set_layer_sm_limit(uint32_t sms);
 
 /* ------------------------------------------------------ kernel profile */
