@@ -716,7 +716,8 @@ def run_gpu(args, cfg):
 
     # Consecutive layers alternate between two streams: the layers are
     # independent (own records, destinations, status and launch slot, no
-    # keystream buffer), and with each launch limited to half the SMs
+    # keystream buffer), so one layer's launch ramp and tail overlap the other
+    # stream's kernel, and with each launch limited to half the SMs
     # (with_sm_share) the two streams' kernels run side by side.  The timed
     # events stay on `stream`, which forks to and joins the second stream
     # every step.
@@ -787,11 +788,16 @@ def run_gpu(args, cfg):
         assert int(status.min().item()) == 1
         return ms / args.steps, launches, clk
 
+    # Two-stream paths with every launch on all SMs, and with each launch
+    # limited to half of them (the better of the two depends on the layer).
     paths = {"prefetched_keystream": device_step,
-             "prefetched_keystream_two_streams": with_sm_share(lib, torch, local, device_step_two_streams, 2)}
+             "prefetched_keystream_two_streams": device_step_two_streams,
+             "prefetched_keystream_two_streams_half_sms": with_sm_share(lib, torch, local, device_step_two_streams, 2)}
     if all(b == 0 for b in bits):
         paths["inline_keystream"] = device_step_inline
-        paths["inline_keystream_two_streams"] = with_sm_share(lib, torch, local, device_step_inline_two_streams, 2)
+        paths["inline_keystream_two_streams"] = device_step_inline_two_streams
+        paths["inline_keystream_two_streams_half_sms"] = with_sm_share(lib, torch, local,
+                                                                       device_step_inline_two_streams, 2)
     timings = {name: timed_steps(fn) for name, fn in paths.items()}
     best = min(timings, key=lambda name: timings[name][0])
     ms_per_step, launches, clocks = timings[best]
@@ -1123,7 +1129,8 @@ def run_gpu_writeback(args, cfg):
         barrier()
         return max_over_ranks(start.elapsed_time(end), dist) / args.steps, launches, clk
 
-    paths = {"one_stream": device_step, "two_streams": with_sm_share(lib, torch, local, device_step_two_streams, 2)}
+    paths = {"one_stream": device_step, "two_streams": device_step_two_streams,
+             "two_streams_half_sms": with_sm_share(lib, torch, local, device_step_two_streams, 2)}
     timings = {name: timed_steps(fn) for name, fn in paths.items()}
     best = min(timings, key=lambda name: timings[name][0])
     ms_per_step, launches, clocks = timings[best]
