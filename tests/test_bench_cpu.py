@@ -1,4 +1,4 @@
-"""bench.py's TP partition (the path's multi-GPU sharding):
+"""bench.py's TP partition (the multi-GPU sharding of the reload path):
 every rank owns heads / TP KV heads of every layer, TP from --tp, the
 config's own TP or the number of GPUs, and the scaling kind follows from it.
 Pure host logic, no GPU."""
